@@ -1,0 +1,241 @@
+// C ABI entry points: handle lifetime, workspace sizing and the per-step
+// launch sequence (embedding -> L x [LN, uvqk GEMM + KV append, paged
+// attention, gate, output GEMM + residual] -> heads -> legal projection).
+// Mirrors HSTUChessModel.forward_decode_grouped / forward
+// (src/imba_chess/model/hstu_model.py:337-374, :651-752).
+#include <cmath>
+#include <cstring>
+#include <new>
+
+#include "gemm_tc.cuh"
+#include "kernels.cuh"
+
+namespace imba {
+
+namespace {
+
+constexpr size_t kAlign = 256;
+inline size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+inline size_t dtype_bytes(int dtype) { return dtype == IMBA_DTYPE_BF16 ? 2 : 4; }
+
+size_t workspace_layout(const imba_model* m, int32_t rows, void* base, Workspace* ws) {
+  const imba_model_desc& d = m->d;
+  const size_t R = (size_t)(rows > 0 ? rows : 0);
+  const size_t eb = dtype_bytes(d.dtype);
+  const size_t hdv = (size_t)d.num_heads * d.linear_dim, hdq = (size_t)d.num_heads * d.attention_dim;
+  size_t off = 0;
+  char* b = static_cast<char*>(base);
+  auto take = [&](size_t bytes) -> void* {
+    void* p = b ? b + off : nullptr;
+    off += align_up(bytes);
+    return p;
+  };
+  Workspace w{};
+  w.x = static_cast<float*>(take(R * d.model_dim * 4));
+  w.xn = take(R * d.model_dim * eb);
+  w.u = static_cast<float*>(take(R * hdv * 4));
+  w.q = take(R * hdq * eb);
+  w.attn = static_cast<float*>(take(R * hdv * 4));
+  w.gated = take(R * hdv * eb);
+  w.xf32 = static_cast<float*>(take(R * d.model_dim * 4));
+  w.xf = take(R * d.model_dim * eb);
+  w.xf_lo = take(R * d.model_dim * eb);
+  w.hval = static_cast<float*>(take(R * (d.model_dim / 2 + 1) * 4));
+  w.logits = static_cast<float*>(take(R * d.vocab * 4));
+  w.bytes = off;
+  if (ws) *ws = w;
+  return off;
+}
+
+imba_status_t validate_desc(const imba_model_desc* d) {
+  if (!d) return IMBA_ERR_ARG;
+  if (d->model_dim <= 0 || d->model_dim > 1024 || d->model_dim % 2) return IMBA_ERR_UNSUPPORTED;
+  if (d->num_layers <= 0 || d->num_layers > IMBA_MAX_LAYERS) return IMBA_ERR_UNSUPPORTED;
+  if (d->num_heads <= 0 || d->attention_dim <= 0 || d->attention_dim > 64 || d->linear_dim <= 0 ||
+      d->linear_dim > 64)
+    return IMBA_ERR_UNSUPPORTED;
+  if ((int64_t)d->num_heads * d->linear_dim > 1024) return IMBA_ERR_UNSUPPORTED;
+  if (d->vocab <= 0 || d->max_pos <= 0 || d->halfmove_vocab <= 0 || d->fullmove_vocab <= 0) return IMBA_ERR_ARG;
+  if (d->dtype != IMBA_DTYPE_F32 && d->dtype != IMBA_DTYPE_BF16) return IMBA_ERR_ARG;
+  const void* req[] = {d->piece_square, d->board_params, d->board_out_w, d->board_out_b, d->emb_seq,
+                       d->emb_turn,     d->emb_castle,   d->emb_ep,      d->emb_halfmove, d->emb_fullmove,
+                       d->emb_prev_move, d->emb_pos,     d->final_norm_w, d->final_norm_b, d->policy_w,
+                       d->policy_w32};
+  for (const void* p : req)
+    if (!p) return IMBA_ERR_ARG;
+  for (int l = 0; l < d->num_layers; ++l)
+    if (!d->uvqk_w[l] || !d->o_w[l] || !d->o_b[l] || !d->ps_w[l]) return IMBA_ERR_ARG;
+  if (d->has_value_head && (!d->value0_w || !d->value0_b || !d->value2_w || !d->value2_b)) return IMBA_ERR_ARG;
+  if (d->dtype == IMBA_DTYPE_BF16 && !d->policy_w_lo) return IMBA_ERR_ARG;
+  return IMBA_OK;
+}
+
+imba_status_t validate_step(const imba_model* m, const imba_step_desc* st, const imba_pool_desc* pool) {
+  if (!st || !pool) return IMBA_ERR_ARG;
+  if (st->num_rows < 0 || st->num_groups < 0 || st->num_chunks < 0 || st->num_legal < 0 || st->num_extra < 0 ||
+      st->num_group_pages < 0)
+    return IMBA_ERR_ARG;
+  if (st->num_rows == 0) return IMBA_OK;
+  if (!pool->base || pool->num_pages <= 0) return IMBA_ERR_ARG;
+  if (pool->num_pages > (int64_t)INT32_MAX / IMBA_PAGE_TOKENS) return IMBA_ERR_RANGE;
+  const void* req[] = {st->piece_ids, st->side_ids, st->positions, st->row_vis, st->row_extra_off,
+                       st->row_dst_slot, st->row_perm};
+  for (const void* p : req)
+    if (!p) return IMBA_ERR_ARG;
+  if (st->num_chunks > 0 && (!st->chunk_group || !st->chunk_row_off || !st->chunk_nrows || !st->group_page_off))
+    return IMBA_ERR_ARG;
+  if (st->num_group_pages > 0 && !st->group_pages) return IMBA_ERR_ARG;
+  if (st->num_extra > 0 && (!st->extra_slot || !st->extra_pos)) return IMBA_ERR_ARG;
+  if (st->legal_off && st->num_legal > 0 && !st->legal_ids) return IMBA_ERR_ARG;
+  if ((st->legal_logits || st->legal_logprob) && !st->legal_off) return IMBA_ERR_ARG;
+  (void)m;
+  return IMBA_OK;
+}
+
+template <typename T>
+imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba_pool_desc& pool, Workspace& w,
+                       cudaStream_t s) {
+  const imba_model_desc& md = m->d;
+  const int R = st.num_rows, d = md.model_dim, H = md.num_heads;
+  const int hdv = H * md.linear_dim;
+  const PoolGeom g = m->geom(pool.num_pages);
+  T* poolp = static_cast<T*>(pool.base);
+  cudaError_t e;
+#define IMBA_CK(...)               \
+  do {                             \
+    e = (__VA_ARGS__);             \
+    if (e != cudaSuccess) return IMBA_ERR_CUDA; \
+  } while (0)
+
+  IMBA_CK(launch_embed(md, st, w.x, s));
+  for (int l = 0; l < md.num_layers; ++l) {
+    IMBA_CK(launch_ln_rows<T>(w.x, R, d, 1e-6f, static_cast<T*>(w.xn), s));
+    EpiUVQK<T> epi{w.u, static_cast<T*>(w.q), poolp, st.row_dst_slot, g, l, st.status};
+    if (!gemm_tc_launch_uvqk(m, l, R, static_cast<const T*>(w.xn), epi, s, &e)) {
+      IMBA_CK(launch_gemm_simt<T, T, EpiUVQK<T>>(static_cast<const T*>(w.xn), d,
+                                                static_cast<const T*>(md.uvqk_w[l]), d, R, m->uvqk_n, d, epi, s));
+    } else if (e != cudaSuccess) {
+      return IMBA_ERR_CUDA;
+    }
+    AttnArgs aa{w.q, pool.base, g, l, md.ps_w[l], md.max_pos, 1.0f / sqrtf((float)md.attention_dim), st, w.attn};
+    IMBA_CK(launch_attn_simt<T>(aa, s));
+    IMBA_CK(launch_gate<T>(w.attn, w.u, R, hdv, static_cast<T*>(w.gated), s));
+    EpiResidual er{w.x, md.o_b[l], d};
+    if (!gemm_tc_launch_out(m, l, R, static_cast<const T*>(w.gated), er, s, &e)) {
+      IMBA_CK(launch_gemm_simt<T, T, EpiResidual>(static_cast<const T*>(w.gated), hdv,
+                                                  static_cast<const T*>(md.o_w[l]), hdv, R, d, hdv, er, s));
+    } else if (e != cudaSuccess) {
+      return IMBA_ERR_CUDA;
+    }
+  }
+  const bool bf = md.dtype == IMBA_DTYPE_BF16;
+  IMBA_CK(launch_final_ln<T>(w.x, R, d, md.final_norm_w, md.final_norm_b, w.xf32, bf ? static_cast<T*>(w.xf) : nullptr,
+                             bf ? static_cast<T*>(w.xf_lo) : nullptr, s));
+  if (st.hidden) IMBA_CK(cudaMemcpyAsync(st.hidden, w.x, (size_t)R * d * 4, cudaMemcpyDeviceToDevice, s));
+  float* logits = st.logits ? st.logits : w.logits;
+  const bool need_logits = st.logits || st.legal_off;
+  if (need_logits) {
+    if (!gemm_tc_launch_policy(m, R, static_cast<const T*>(w.xf), static_cast<const T*>(w.xf_lo), logits, s, &e)) {
+      IMBA_CK(launch_gemm_simt<float, float, EpiStore>(w.xf32, d, md.policy_w32, d, R, md.vocab, d,
+                                                       EpiStore{logits, md.vocab}, s));
+    } else if (e != cudaSuccess) {
+      return IMBA_ERR_CUDA;
+    }
+  }
+  if (md.has_value_head) {
+    const int hd = d / 2;
+    EpiBiasSilu eb{w.hval, md.value0_b, hd};
+    const T* xin = bf ? static_cast<const T*>(w.xf) : reinterpret_cast<const T*>(w.xf32);
+    IMBA_CK(launch_gemm_simt<T, T, EpiBiasSilu>(xin, d, static_cast<const T*>(md.value0_w), d, R, hd, d, eb, s));
+  }
+  IMBA_CK(launch_value_legal(md, st, w.hval, logits, s));
+#undef IMBA_CK
+  return IMBA_OK;
+}
+
+}  // namespace
+
+Workspace carve_workspace(const imba_model* m, int32_t rows, void* base) {
+  Workspace w;
+  workspace_layout(m, rows, base, &w);
+  return w;
+}
+
+}  // namespace imba
+
+extern "C" {
+
+int32_t imba_version(void) { return 1; }
+int32_t imba_device_arch(void) { return 1000; }
+
+imba_status_t imba_model_create(const imba_model_desc* desc, imba_model** out) {
+  if (!out) return IMBA_ERR_ARG;
+  *out = nullptr;
+  const imba_status_t v = imba::validate_desc(desc);
+  if (v != IMBA_OK) return v;
+  imba_model* m = new (std::nothrow) imba_model();
+  if (!m) return IMBA_ERR_OOM;
+  m->d = *desc;
+  m->uvqk_n = 2 * desc->num_heads * (desc->linear_dim + desc->attention_dim);
+  const imba_status_t t = imba::gemm_tc_prepare(m);
+  if (t != IMBA_OK) {
+    delete m;
+    return t;
+  }
+  *out = m;
+  return IMBA_OK;
+}
+
+void imba_model_destroy(imba_model* model) { delete model; }
+
+size_t imba_step_workspace_bytes(const imba_model* model, int32_t max_rows) {
+  if (!model || max_rows < 0) return 0;
+  return imba::workspace_layout(model, max_rows, nullptr, nullptr);
+}
+
+imba_status_t imba_step(const imba_model* model, const imba_step_desc* step, const imba_pool_desc* pool,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (!model) return IMBA_ERR_ARG;
+  const imba_status_t v = imba::validate_step(model, step, pool);
+  if (v != IMBA_OK) return v;
+  if (step->num_rows == 0) return IMBA_OK;
+  const size_t need = imba::workspace_layout(model, step->num_rows, nullptr, nullptr);
+  if (!workspace || workspace_bytes < need) return IMBA_ERR_OOM;
+  imba::Workspace w = imba::carve_workspace(model, step->num_rows, workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (model->d.dtype == IMBA_DTYPE_BF16) return imba::run_step<imba::bf16>(model, *step, *pool, w, s);
+  return imba::run_step<float>(model, *step, *pool, w, s);
+}
+
+static imba_status_t kv_copy(const imba_model* model, const imba_pool_desc* pool, int32_t layer, int32_t n,
+                             const int32_t* slots, void* dk, void* dv, int to_pool, int32_t* status, void* stream) {
+  if (!model || !pool || !pool->base || pool->num_pages <= 0) return IMBA_ERR_ARG;
+  if (layer < 0 || layer >= model->d.num_layers || n < 0) return IMBA_ERR_RANGE;
+  if (n == 0) return IMBA_OK;
+  if (!slots || !dk || !dv) return IMBA_ERR_ARG;
+  const imba::PoolGeom g = model->geom(pool->num_pages);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (model->d.dtype == IMBA_DTYPE_BF16)
+    e = imba::launch_kv_copy<imba::bf16>(g, static_cast<imba::bf16*>(pool->base), layer, n, slots,
+                                         static_cast<imba::bf16*>(dk), static_cast<imba::bf16*>(dv), to_pool, status, s);
+  else
+    e = imba::launch_kv_copy<float>(g, static_cast<float*>(pool->base), layer, n, slots, static_cast<float*>(dk),
+                                    static_cast<float*>(dv), to_pool, status, s);
+  return e == cudaSuccess ? IMBA_OK : IMBA_ERR_CUDA;
+}
+
+imba_status_t imba_kv_scatter(const imba_model* model, const imba_pool_desc* pool, int32_t layer, int32_t n,
+                              const int32_t* slots, const void* dense_k, const void* dense_v, int32_t* status,
+                              void* stream) {
+  return kv_copy(model, pool, layer, n, slots, const_cast<void*>(dense_k), const_cast<void*>(dense_v), 1, status,
+                 stream);
+}
+
+imba_status_t imba_kv_gather(const imba_model* model, const imba_pool_desc* pool, int32_t layer, int32_t n,
+                             const int32_t* slots, void* dense_k, void* dense_v, int32_t* status, void* stream) {
+  return kv_copy(model, pool, layer, n, slots, dense_k, dense_v, 0, status, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,108 @@
+// Shared device helpers and the internal model / workspace structures of the
+// imba_b200 library.  Device code only uses the fp32 and bf16 storage types;
+// every reduction and every softmax is carried out in fp32 (fp64 for the
+// legal-move log-softmax, which the reference computes in float64).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "imba_b200.h"
+
+namespace imba {
+
+using bf16 = __nv_bfloat16;
+
+__device__ __forceinline__ float to_f(float x) { return x; }
+__device__ __forceinline__ float to_f(bf16 x) { return __bfloat162float(x); }
+
+template <typename T>
+__device__ __forceinline__ T from_f(float x);
+template <>
+__device__ __forceinline__ float from_f<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ bf16 from_f<bf16>(float x) { return __float2bfloat16_rn(x); }
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// First error wins; later errors never overwrite it.
+__device__ __forceinline__ void report(int32_t* status, int32_t code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+// Geometry of the paged KV pool for one model.
+struct PoolGeom {
+  int64_t page_stride;   // elements per page (all layers)
+  int64_t layer_stride;  // elements per layer within a page
+  int64_t v_offset;      // offset of the V block within a layer block
+  int64_t num_slots;     // num_pages * IMBA_PAGE_TOKENS
+  int H, dqk, dv;
+
+  // Element offset of token slot `slot`, layer `l`, head `h`, K block.
+  __host__ __device__ __forceinline__ int64_t k_off(int64_t slot, int l, int h) const {
+    return (slot / IMBA_PAGE_TOKENS) * page_stride + (int64_t)l * layer_stride +
+           ((int64_t)h * IMBA_PAGE_TOKENS + (slot % IMBA_PAGE_TOKENS)) * dqk;
+  }
+  __host__ __device__ __forceinline__ int64_t v_off(int64_t slot, int l, int h) const {
+    return (slot / IMBA_PAGE_TOKENS) * page_stride + (int64_t)l * layer_stride + v_offset +
+           ((int64_t)h * IMBA_PAGE_TOKENS + (slot % IMBA_PAGE_TOKENS)) * dv;
+  }
+};
+
+}  // namespace imba
+
+// The opaque handle behind imba_model*.
+struct imba_model {
+  imba_model_desc d;
+  int uvqk_n;  // 2 H (d_v + d_qk)
+  imba::PoolGeom geom(int64_t num_pages) const {
+    imba::PoolGeom g;
+    g.H = d.num_heads;
+    g.dqk = d.attention_dim;
+    g.dv = d.linear_dim;
+    g.v_offset = (int64_t)d.num_heads * IMBA_PAGE_TOKENS * d.attention_dim;
+    g.layer_stride = (int64_t)d.num_heads * IMBA_PAGE_TOKENS * (d.attention_dim + d.linear_dim);
+    g.page_stride = g.layer_stride * d.num_layers;
+    g.num_slots = num_pages * IMBA_PAGE_TOKENS;
+    return g;
+  }
+};
+
+namespace imba {
+
+// Scratch buffers carved out of the caller's workspace for one step.
+struct Workspace {
+  float* x;        // [R, d]      residual stream
+  void* xn;        // [R, d]      LN(x), model dtype
+  float* u;        // [R, H dv]   gate (post-SiLU u)
+  void* q;         // [R, H dqk]  queries, model dtype
+  float* attn;     // [R, H dv]   attention output
+  void* gated;     // [R, H dv]   LN(attn) * u, model dtype
+  float* xf32;     // [R, d]      final LN output, fp32
+  void* xf;        // [R, d]      final LN output, model dtype (hi part in bf16)
+  void* xf_lo;     // [R, d]      bf16 only: fp32 - hi residual
+  float* hval;     // [R, d/2]    value-head hidden
+  float* logits;   // [R, vocab]  used when the caller passes no logits buffer
+  size_t bytes;
+};
+
+Workspace carve_workspace(const imba_model* m, int32_t rows, void* base);
+
+}  // namespace imba

@@ -1,0 +1,39 @@
+// Launch functions of the step kernels (one translation unit each).
+#pragma once
+
+#include "epilogues.cuh"
+
+namespace imba {
+
+struct AttnArgs {
+  const void* q;        // [R, H dqk] model dtype
+  const void* pool;     // paged KV pool, model dtype
+  PoolGeom g;
+  int layer;
+  const float* ps_w;    // [H, 2 max_pos - 1]
+  int max_pos;
+  float scale;          // 1 / sqrt(d_qk)
+  imba_step_desc st;
+  float* out;           // [R, H dv]
+};
+
+cudaError_t launch_embed(const imba_model_desc& md, const imba_step_desc& st, float* x, cudaStream_t s);
+template <typename T>
+cudaError_t launch_ln_rows(const float* x, int rows, int n, float eps, T* out, cudaStream_t s);
+template <typename T>
+cudaError_t launch_gate(const float* attn, const float* u, int rows, int n, T* out, cudaStream_t s);
+template <typename T>
+cudaError_t launch_final_ln(const float* x, int rows, int n, const float* w, const float* b, float* out32, T* outT,
+                            T* outLo, cudaStream_t s);
+cudaError_t launch_value_legal(const imba_model_desc& md, const imba_step_desc& st, const float* hval,
+                               const float* logits, cudaStream_t s);
+template <typename T>
+cudaError_t launch_kv_copy(const PoolGeom& g, T* pool, int layer, int n, const int32_t* slots, T* dk, T* dv,
+                           int to_pool, int32_t* status, cudaStream_t s);
+template <typename TA, typename TW, class Epi>
+cudaError_t launch_gemm_simt(const TA* A, int lda, const TW* W, int ldw, int M, int N, int K, Epi epi,
+                             cudaStream_t s);
+template <typename T>
+cudaError_t launch_attn_simt(const AttnArgs& a, cudaStream_t s);
+
+}  // namespace imba

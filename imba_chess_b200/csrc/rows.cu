@@ -1,0 +1,268 @@
+// Row-wise kernels of the decode step (one warp per row, fp32 math):
+//  - input LayerNorm of an STU layer (no affine, eps 1e-6), cast to the GEMM
+//    operand dtype                       (src/imba_chess/model/hstu_attention.py:51-52, :309)
+//  - attention-output LayerNorm (no affine, eps 1e-6) gated by u
+//                                        (hstu_attention.py:54-57, :415-421)
+//  - final LayerNorm (affine, eps 1e-5)  (src/imba_chess/model/hstu_model.py:245, :745)
+//  - value head output layer, p(win) - p(loss), legal-id gather and the
+//    legal-move log-softmax             (hstu_model.py:252-260;
+//    src/imba_chess/eval/actor_server.py:168-203; actor_worker.py:267-291)
+//  - dense <-> paged KV copies for one layer.
+#include "common.cuh"
+
+namespace imba {
+namespace {
+
+constexpr int kMaxPerLane = 32;  // supports row widths up to 1024
+
+template <typename TOut>
+__global__ void ln_rows_kernel(const float* __restrict__ x, int rows, int n, float eps, TOut* __restrict__ out) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const float* xr = x + (size_t)warp * n;
+  float v[kMaxPerLane];
+  float s = 0.f;
+  const int per = (n + 31) / 32;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    const int c = lane + 32 * i;
+    v[i] = (i < per && c < n) ? xr[c] : 0.f;
+    s += v[i];
+  }
+  const float mu = warp_sum(s) / n;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    const int c = lane + 32 * i;
+    if (i < per && c < n) q += (v[i] - mu) * (v[i] - mu);
+  }
+  const float rs = 1.0f / sqrtf(warp_sum(q) / n + eps);
+  TOut* o = out + (size_t)warp * n;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    const int c = lane + 32 * i;
+    if (i < per && c < n) o[c] = from_f<TOut>((v[i] - mu) * rs);
+  }
+}
+
+template <typename TOut>
+__global__ void gate_kernel(const float* __restrict__ attn, const float* __restrict__ u, int rows, int n,
+                            TOut* __restrict__ out) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const float* ar = attn + (size_t)warp * n;
+  const float* ur = u + (size_t)warp * n;
+  float v[kMaxPerLane];
+  float s = 0.f;
+  const int per = (n + 31) / 32;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    const int c = lane + 32 * i;
+    v[i] = (i < per && c < n) ? ar[c] : 0.f;
+    s += v[i];
+  }
+  const float mu = warp_sum(s) / n;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    const int c = lane + 32 * i;
+    if (i < per && c < n) q += (v[i] - mu) * (v[i] - mu);
+  }
+  const float rs = 1.0f / sqrtf(warp_sum(q) / n + 1e-6f);
+  TOut* o = out + (size_t)warp * n;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    const int c = lane + 32 * i;
+    if (i < per && c < n) o[c] = from_f<TOut>(ur[c] * ((v[i] - mu) * rs));
+  }
+}
+
+// Final affine LayerNorm.  Writes fp32 and the model-dtype copy; for bf16 it
+// also writes the bf16 residual lo = x - float(hi) used by the split-precision
+// policy GEMM.
+template <typename T>
+__global__ void final_ln_kernel(const float* __restrict__ x, int rows, int n, const float* __restrict__ w,
+                                const float* __restrict__ b, float* __restrict__ out32, T* __restrict__ outT,
+                                T* __restrict__ outLo) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const float* xr = x + (size_t)warp * n;
+  float v[kMaxPerLane];
+  float s = 0.f;
+  const int per = (n + 31) / 32;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    const int c = lane + 32 * i;
+    v[i] = (i < per && c < n) ? xr[c] : 0.f;
+    s += v[i];
+  }
+  const float mu = warp_sum(s) / n;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    const int c = lane + 32 * i;
+    if (i < per && c < n) q += (v[i] - mu) * (v[i] - mu);
+  }
+  const float rs = 1.0f / sqrtf(warp_sum(q) / n + 1e-5f);
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    const int c = lane + 32 * i;
+    if (i < per && c < n) {
+      const float y = (v[i] - mu) * rs * w[c] + b[c];
+      const size_t o = (size_t)warp * n + c;
+      out32[o] = y;
+      if (outT) {
+        const T hi = from_f<T>(y);
+        outT[o] = hi;
+        if (outLo) outLo[o] = from_f<T>(y - to_f(hi));
+      }
+    }
+  }
+}
+
+// Value output layer + v + legal projection, one warp per row.
+__global__ void value_legal_kernel(imba_model_desc md, imba_step_desc st, const float* __restrict__ hval,
+                                   const float* __restrict__ logits) {
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (r >= st.num_rows) return;
+  if (md.has_value_head) {
+    const int hd = md.model_dim / 2;
+    const float* hr = hval + (size_t)r * hd;
+    float z[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      float a = 0.f;
+      for (int c = lane; c < hd; c += 32) a = fmaf(hr[c], md.value2_w[(size_t)j * hd + c], a);
+      z[j] = warp_sum(a) + md.value2_b[j];
+    }
+    if (lane == 0) {
+      if (st.value_logits) {
+        st.value_logits[(size_t)r * 3 + 0] = z[0];
+        st.value_logits[(size_t)r * 3 + 1] = z[1];
+        st.value_logits[(size_t)r * 3 + 2] = z[2];
+      }
+      if (st.value_stm) {
+        const float m = fmaxf(z[0], fmaxf(z[1], z[2]));
+        const float e0 = expf(z[0] - m), e1 = expf(z[1] - m), e2 = expf(z[2] - m);
+        const float sum = e0 + e1 + e2;
+        st.value_stm[r] = e2 / sum - e0 / sum;
+      }
+    }
+  } else if (lane == 0) {
+    // No value head: the reference serves a zero placeholder (uniform softmax, v = 0).
+    if (st.value_logits) {
+      st.value_logits[(size_t)r * 3 + 0] = 0.f;
+      st.value_logits[(size_t)r * 3 + 1] = 0.f;
+      st.value_logits[(size_t)r * 3 + 2] = 0.f;
+    }
+    if (st.value_stm) st.value_stm[r] = 0.f;
+  }
+  if (!st.legal_off) return;
+  const int a = st.legal_off[r], b = st.legal_off[r + 1];
+  if (a < 0 || b < a || b > st.num_legal) {
+    if (lane == 0) report(st.status, IMBA_ERR_RANGE);
+    return;
+  }
+  const float* lr = logits + (size_t)r * md.vocab;
+  float mx = -INFINITY;
+  for (int i = a + lane; i < b; i += 32) {
+    int id = st.legal_ids[i];
+    if (id < 0 || id >= md.vocab) {
+      report(st.status, IMBA_ERR_RANGE);
+      id = 0;
+    }
+    const float v = lr[id];
+    if (st.legal_logits) st.legal_logits[i] = v;
+    mx = fmaxf(mx, v);
+  }
+  mx = warp_max(mx);
+  if (!st.legal_logprob || b == a) return;
+  double se = 0.0;
+  for (int i = a + lane; i < b; i += 32) {
+    int id = st.legal_ids[i];
+    id = (id < 0 || id >= md.vocab) ? 0 : id;
+    se += exp((double)lr[id] - (double)mx);
+  }
+  const double lse = log(warp_sum_d(se));
+  for (int i = a + lane; i < b; i += 32) {
+    int id = st.legal_ids[i];
+    id = (id < 0 || id >= md.vocab) ? 0 : id;
+    st.legal_logprob[i] = (float)(((double)lr[id] - (double)mx) - lse);
+  }
+}
+
+template <typename T>
+__global__ void kv_copy_kernel(PoolGeom g, T* pool, int layer, int n, const int32_t* __restrict__ slots,
+                               T* dk, T* dv, int to_pool, int32_t* status) {
+  const int r = blockIdx.x;
+  if (r >= n) return;
+  const int64_t slot = slots[r];
+  if (slot < 0 || slot >= g.num_slots) {
+    if (threadIdx.x == 0) report(status, IMBA_ERR_RANGE);
+    return;
+  }
+  const int nk = g.H * g.dqk, nv = g.H * g.dv;
+  for (int i = threadIdx.x; i < nk + nv; i += blockDim.x) {
+    if (i < nk) {
+      const int h = i / g.dqk, e = i % g.dqk;
+      T* p = pool + g.k_off(slot, layer, h) + e;
+      T* q = dk + (size_t)r * nk + i;
+      if (to_pool) *p = *q; else *q = *p;
+    } else {
+      const int j = i - nk, h = j / g.dv, e = j % g.dv;
+      T* p = pool + g.v_off(slot, layer, h) + e;
+      T* q = dv + (size_t)r * nv + j;
+      if (to_pool) *p = *q; else *q = *p;
+    }
+  }
+}
+
+inline int warp_blocks(int rows) { return (rows + 7) / 8; }  // 8 warps per 256-thread block
+
+}  // namespace
+
+template <typename T>
+cudaError_t launch_ln_rows(const float* x, int rows, int n, float eps, T* out, cudaStream_t s) {
+  ln_rows_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(x, rows, n, eps, out);
+  return cudaGetLastError();
+}
+template cudaError_t launch_ln_rows<float>(const float*, int, int, float, float*, cudaStream_t);
+template cudaError_t launch_ln_rows<bf16>(const float*, int, int, float, bf16*, cudaStream_t);
+
+template <typename T>
+cudaError_t launch_gate(const float* attn, const float* u, int rows, int n, T* out, cudaStream_t s) {
+  gate_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(attn, u, rows, n, out);
+  return cudaGetLastError();
+}
+template cudaError_t launch_gate<float>(const float*, const float*, int, int, float*, cudaStream_t);
+template cudaError_t launch_gate<bf16>(const float*, const float*, int, int, bf16*, cudaStream_t);
+
+template <typename T>
+cudaError_t launch_final_ln(const float* x, int rows, int n, const float* w, const float* b, float* out32, T* outT,
+                            T* outLo, cudaStream_t s) {
+  final_ln_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(x, rows, n, w, b, out32, outT, outLo);
+  return cudaGetLastError();
+}
+template cudaError_t launch_final_ln<float>(const float*, int, int, const float*, const float*, float*, float*,
+                                            float*, cudaStream_t);
+template cudaError_t launch_final_ln<bf16>(const float*, int, int, const float*, const float*, float*, bf16*, bf16*,
+                                           cudaStream_t);
+
+cudaError_t launch_value_legal(const imba_model_desc& md, const imba_step_desc& st, const float* hval,
+                               const float* logits, cudaStream_t s) {
+  value_legal_kernel<<<warp_blocks(st.num_rows), 256, 0, s>>>(md, st, hval, logits);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_kv_copy(const PoolGeom& g, T* pool, int layer, int n, const int32_t* slots, T* dk, T* dv,
+                           int to_pool, int32_t* status, cudaStream_t s) {
+  kv_copy_kernel<T><<<n, 128, 0, s>>>(g, pool, layer, n, slots, dk, dv, to_pool, status);
+  return cudaGetLastError();
+}
+template cudaError_t launch_kv_copy<float>(const PoolGeom&, float*, int, int, const int32_t*, float*, float*, int,
+                                           int32_t*, cudaStream_t);
+template cudaError_t launch_kv_copy<bf16>(const PoolGeom&, bf16*, int, int, const int32_t*, bf16*, bf16*, int,
+                                          int32_t*, cudaStream_t);
+
+}  // namespace imba

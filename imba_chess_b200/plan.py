@@ -1,0 +1,193 @@
+"""Host-side planning of one jagged step (integer bookkeeping only).
+
+A ``StepPlan`` holds every integer input of ``imba_step`` as numpy arrays.
+``pack()`` lays them out in ONE int32 buffer so a step costs a single
+host-to-device copy; ``DeviceStep`` points a ``StepDesc`` into the device
+copy.  All arrays are built with vectorised numpy: no per-row Python loops.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import _native
+from .synth import TOKEN_FIELDS
+
+CHUNK = _native.CHUNK_ROWS
+
+# Order of the int32 sections in the packed buffer.
+_SECTIONS = (
+    "side_ids",
+    "positions",
+    "row_vis",
+    "row_extra_off",
+    "extra_slot",
+    "extra_pos",
+    "row_dst_slot",
+    "group_page_off",
+    "group_pages",
+    "chunk_group",
+    "chunk_row_off",
+    "chunk_nrows",
+    "row_perm",
+    "legal_off",
+    "legal_ids",
+)
+
+
+def side_ids_from_tokens(tok: dict) -> np.ndarray:
+    """[R, 7] int32: seq, turn, castle, ep, halfmove, fullmove, prev_move."""
+    cols = [np.asarray(tok[k], dtype=np.int64).reshape(-1) for k in TOKEN_FIELDS[1:]]
+    return np.stack(cols, axis=1).clip(-(2**31), 2**31 - 1).astype(np.int32)
+
+
+def piece_ids_from_tokens(tok: dict) -> np.ndarray:
+    p = np.asarray(tok["piece_ids"], dtype=np.int64).reshape(-1, 64)
+    if p.size and (p.min() < 0 or p.max() > 12):
+        raise ValueError("piece_ids values must be in [0, 12]")
+    return p.astype(np.uint8)
+
+
+def build_chunks(row_group: np.ndarray, num_groups: int):
+    """Rows ordered by group (stable), split into chunks of <= 64 rows.  A
+    group with more than 64 rows is split into equal-size chunks."""
+    row_group = np.asarray(row_group, dtype=np.int64)
+    order = np.argsort(row_group, kind="stable").astype(np.int32)
+    counts = np.bincount(row_group, minlength=num_groups).astype(np.int64)
+    starts = np.concatenate([[0], np.cumsum(counts)[:-1]]).astype(np.int64)
+    nch = (counts + CHUNK - 1) // CHUNK
+    chunk_group = np.repeat(np.arange(num_groups, dtype=np.int64), nch)
+    first = np.repeat(np.cumsum(nch) - nch, nch)
+    cidx = np.arange(int(nch.sum()), dtype=np.int64) - first
+    # balanced split: chunk i of a group with n rows and k chunks covers
+    # [i*n//k, (i+1)*n//k)
+    n_g = counts[chunk_group]
+    k_g = nch[chunk_group]
+    lo = cidx * n_g // k_g
+    hi = (cidx + 1) * n_g // k_g
+    chunk_row_off = starts[chunk_group] + lo
+    chunk_nrows = hi - lo
+    return (
+        order,
+        chunk_group.astype(np.int32),
+        chunk_row_off.astype(np.int32),
+        chunk_nrows.astype(np.int32),
+    )
+
+
+@dataclass
+class StepPlan:
+    piece_ids: np.ndarray          # uint8 [R, 64]
+    side_ids: np.ndarray           # int32 [R, 7]
+    positions: np.ndarray          # int32 [R]
+    row_group: np.ndarray          # int32 [R]
+    row_vis: np.ndarray            # int32 [R]
+    row_extra_off: np.ndarray      # int32 [R + 1]
+    extra_slot: np.ndarray         # int32 [E]
+    extra_pos: np.ndarray          # int32 [E]
+    row_dst_slot: np.ndarray       # int32 [R]
+    group_page_off: np.ndarray     # int32 [G + 1]
+    group_pages: np.ndarray        # int32 [NP]
+    legal_off: np.ndarray | None = None  # int32 [R + 1]
+    legal_ids: np.ndarray | None = None  # int32 [NL]
+    chunks: tuple = field(default=None, repr=False)
+
+    @property
+    def num_rows(self) -> int:
+        return int(self.positions.shape[0])
+
+    @property
+    def num_groups(self) -> int:
+        return int(self.group_page_off.shape[0]) - 1
+
+    def finalize(self) -> "StepPlan":
+        if self.chunks is None:
+            self.chunks = build_chunks(self.row_group, self.num_groups)
+        return self
+
+    def arrays(self) -> dict[str, np.ndarray]:
+        self.finalize()
+        row_perm, cg, co, cn = self.chunks
+        R = self.num_rows
+        out = {
+            "side_ids": self.side_ids.reshape(-1),
+            "positions": self.positions,
+            "row_vis": self.row_vis,
+            "row_extra_off": self.row_extra_off,
+            "extra_slot": self.extra_slot,
+            "extra_pos": self.extra_pos,
+            "row_dst_slot": self.row_dst_slot,
+            "group_page_off": self.group_page_off,
+            "group_pages": self.group_pages,
+            "chunk_group": cg,
+            "chunk_row_off": co,
+            "chunk_nrows": cn,
+            "row_perm": row_perm,
+            "legal_off": self.legal_off if self.legal_off is not None else np.zeros(R + 1, np.int32),
+            "legal_ids": self.legal_ids if self.legal_ids is not None else np.zeros(0, np.int32),
+        }
+        return {k: np.ascontiguousarray(v, dtype=np.int32).reshape(-1) for k, v in out.items()}
+
+    def pack(self) -> tuple[np.ndarray, dict[str, tuple[int, int]]]:
+        """One int32 buffer: piece bytes (padded to 16 B), then each section
+        padded to a multiple of 4 elements.  Returns (buffer, {name: (offset
+        in int32 elements, length)})."""
+        arrs = self.arrays()
+        R = self.num_rows
+        piece_words = -(-(R * 64) // 16) * 4
+        layout: dict[str, tuple[int, int]] = {"piece_ids": (0, R * 64)}
+        off = piece_words
+        for name in _SECTIONS:
+            n = int(arrs[name].shape[0])
+            layout[name] = (off, n)
+            off += -(-max(n, 1) // 4) * 4
+        buf = np.zeros(off, dtype=np.int32)
+        buf.view(np.uint8)[: R * 64] = self.piece_ids.reshape(-1)
+        for name in _SECTIONS:
+            o, n = layout[name]
+            buf[o : o + n] = arrs[name]
+        return buf, layout
+
+    def counts(self) -> dict[str, int]:
+        self.finalize()
+        return {
+            "num_rows": self.num_rows,
+            "num_groups": self.num_groups,
+            "num_chunks": int(self.chunks[1].shape[0]),
+            "num_legal": 0 if self.legal_ids is None else int(self.legal_ids.shape[0]),
+            "num_extra": int(self.extra_slot.shape[0]),
+            "num_group_pages": int(self.group_pages.shape[0]),
+        }
+
+
+class DeviceStep:
+    """A packed plan resident on the device, with a ``StepDesc`` pointing
+    into it.  Output pointers are filled by the caller."""
+
+    def __init__(self, plan: StepPlan, device: torch.device, *, pinned: bool = False,
+                 stream: torch.cuda.Stream | None = None) -> None:
+        buf, layout = plan.pack()
+        host = torch.from_numpy(buf)
+        if pinned:
+            host = host.pin_memory()
+        self.host = host
+        self.buf = torch.empty_like(host, device=device)
+        self.buf.copy_(host, non_blocking=pinned)
+        self.layout = layout
+        self.has_legal = plan.legal_off is not None
+        self.desc = _native.StepDesc()
+        for k, v in plan.counts().items():
+            setattr(self.desc, k, v)
+        base = self.buf.data_ptr()
+        for name, (off, _n) in layout.items():
+            setattr(self.desc, name, base + 4 * off)
+        if not self.has_legal:
+            self.desc.legal_off = None
+            self.desc.legal_ids = None
+
+    @property
+    def h2d_bytes(self) -> int:
+        return int(self.buf.numel() * 4)

@@ -1,0 +1,433 @@
+"""``ActorInferenceServer`` on the B200 library: the reference server's
+``service()`` contract (src/imba_chess/eval/actor_server.py:408-925) with
+every prefix and every search node's KV resident in one paged device pool.
+
+What changes relative to the reference, and what does not:
+
+* Root requests (full and incremental) of one ``service()`` call run as ONE
+  jagged prefill step per form: every game's tokens are appended in place to
+  that game's pool sequence (no ``torch.cat`` of the whole prefix per token,
+  actor_server.py:749-781).
+* A wave of decode requests is ONE grouped step: each request's rows form a
+  group over its turn's root prefix (read in place, never padded and
+  stacked, merged_executors.py:187-196); each row's suffix is its parent
+  chain read straight from the turn's arena pages, plus itself.
+* Logical bookkeeping is the reference's: per-turn arena rows are minted
+  consecutively in wave order (``_KVArena.append``), ``node_chains[child] =
+  chain(parent) + [own_row]``, positions are ``prefix_len + depth``, a turn's
+  prefix is a snapshot of its game's prefix at root time.
+* Error conventions are the reference's: ``TypeError`` for unsupported
+  request types, ``KeyError`` for an unknown turn/game/parent node,
+  ``RuntimeError`` for prefix desync or max-position overflow, ``ValueError``
+  for empty incremental requests or a model without a value head.
+"""
+
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+from typing import Any
+
+import numpy as np
+import torch
+
+from . import _native
+from .kvpool import PAGE, KVPool, KVSequence
+from .model import B200HSTUChessModel
+from .plan import DeviceStep, StepPlan
+from .protocol import RootEvalResponse, WaveResponse, is_root_request, is_wave_request
+from .synth import EVENT_TOKEN_ID, TOKEN_FIELDS
+
+_TOKEN_FIELDS = TOKEN_FIELDS
+
+
+@dataclass
+class _GameState:
+    """A worker's current game: its prefix sequence and length."""
+
+    seq: KVSequence
+    prefix_len: int
+
+
+@dataclass
+class _TurnState:
+    """One live (worker_id, turn_id): a snapshot (sequence, length) of the
+    game prefix at root time, the turn's node arena and node chains."""
+
+    seq: KVSequence
+    prefix_len: int
+    arena: KVSequence | None = None
+    node_chains: dict[int, list[int]] = field(default_factory=dict)
+
+    def release(self) -> None:
+        self.seq.release()
+        if self.arena is not None:
+            self.arena.release()
+            self.arena = None
+
+
+def _ids_csr(id_lists: list) -> tuple[np.ndarray, np.ndarray]:
+    lengths = np.fromiter((len(x) for x in id_lists), dtype=np.int64, count=len(id_lists))
+    off = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    flat = np.fromiter((v for ids in id_lists for v in ids), dtype=np.int64, count=int(off[-1]))
+    return off, flat.astype(np.int32)
+
+
+class ActorInferenceServer:
+    """Owns the model and every worker's KV state, keyed like the reference:
+    ``(worker_id, turn_id)`` for a turn's search tree, ``worker_id`` for the
+    worker's current game prefix."""
+
+    def __init__(self, *, model, device: torch.device | str, dtype: torch.dtype, require_value_head: bool = True,
+                 profile_sync: bool = False, kv_pool_pages: int | None = None,
+                 kv_pool_bytes: int | None = None) -> None:
+        device = torch.device(device)
+        if not isinstance(model, B200HSTUChessModel):
+            model_dtype = torch.float32 if dtype == torch.float32 else torch.bfloat16
+            model = B200HSTUChessModel.from_reference(model, dtype=model_dtype, device=device)
+        if require_value_head and getattr(model, "value_head", None) is None:
+            raise ValueError(
+                "ActorInferenceServer(require_value_head=True) requires a model with an enabled value head: "
+                "every response row carries value_stm. Pass require_value_head=False to serve a "
+                "value-head-less model (value_stm is then a 0.0 placeholder)."
+            )
+        self._model = model
+        self._device = model.device
+        self._dtype = dtype
+        self.profile_sync = bool(profile_sync)
+        self.stats: dict[str, float] = {
+            "root_build_s": 0.0, "root_gpu_s": 0.0, "root_post_s": 0.0,
+            "wave_build_s": 0.0, "wave_gpu_s": 0.0, "wave_post_s": 0.0,
+            "root_calls": 0, "root_reqs": 0,
+            "wave_calls": 0, "wave_reqs": 0, "wave_rows": 0,
+            "incremental_root_gpu_s": 0.0,
+            "incremental_root_calls": 0, "incremental_root_reqs": 0,
+            "incremental_root_tokens": 0,
+        }
+        if kv_pool_pages is None:
+            page_bytes = self._page_bytes()
+            budget = kv_pool_bytes
+            if budget is None:
+                free, _total = torch.cuda.mem_get_info(self._device)
+                budget = min(int(free * 0.25), 8 << 30)
+            kv_pool_pages = max(64, budget // page_bytes)
+        self.pool: KVPool = model.new_pool(int(kv_pool_pages))
+        self._turns: dict[tuple[int, int], _TurnState] = {}
+        self._games: dict[int, _GameState] = {}
+        self._status = torch.zeros(1, dtype=torch.int32, device=self._device)
+
+    def _page_bytes(self) -> int:
+        d = self._model.dims
+        esize = 2 if self._model.dtype == torch.bfloat16 else 4
+        return d.num_layers * d.num_heads * PAGE * (d.attention_dim + d.linear_dim) * esize
+
+    # ------------------------------------------------------------------
+    def register_root(self, worker_id: int, turn_id: int, batch_arrays: dict, legal_vocab_ids: list[int]):
+        from .protocol import RootEvalRequest
+
+        req = RootEvalRequest(worker_id=int(worker_id), turn_id=int(turn_id), batch_arrays=batch_arrays,
+                              legal_vocab_ids=list(legal_vocab_ids))
+        return self._service_roots([req])[0]
+
+    def service(self, requests: list) -> list:
+        """Responses in the order of ``requests`` (roots run before waves)."""
+        responses: list[Any] = [None] * len(requests)
+        root_pos = [i for i, r in enumerate(requests) if is_root_request(r)]
+        wave_pos = [i for i, r in enumerate(requests) if is_wave_request(r)]
+        if len(root_pos) + len(wave_pos) != len(requests):
+            bad = sorted({type(r).__name__ for r in requests if not (is_root_request(r) or is_wave_request(r))})
+            raise TypeError(f"ActorInferenceServer.service() got unsupported request type(s): {bad}")
+        if root_pos:
+            for i, resp in zip(root_pos, self._service_roots([requests[i] for i in root_pos])):
+                responses[i] = resp
+        if wave_pos:
+            for i, resp in zip(wave_pos, self._service_waves([requests[i] for i in wave_pos])):
+                responses[i] = resp
+        return responses
+
+    def release_turn(self, worker_id: int, turn_id: int) -> None:
+        ts = self._turns.pop((int(worker_id), int(turn_id)), None)
+        if ts is not None:
+            ts.release()
+
+    def release_game(self, worker_id: int) -> None:
+        gs = self._games.pop(int(worker_id), None)
+        if gs is not None:
+            gs.seq.release()
+
+    def _sync_if_profiling(self) -> None:
+        if self.profile_sync:
+            torch.cuda.synchronize(self._device)
+
+    # ------------------------------------------------------------------
+    def _set_turn(self, key: tuple[int, int], game: _GameState) -> None:
+        old = self._turns.pop(key, None)
+        if old is not None:
+            old.release()
+        self._turns[key] = _TurnState(seq=game.seq.retain(), prefix_len=game.prefix_len)
+
+    def _run_rows(self, plan: StepPlan, n_legal_rows: int):
+        """Run one step and bring back (value_stm [R], legal_logits flat)."""
+        R = plan.num_rows
+        dstep = DeviceStep(plan, self._device, pinned=True)
+        nl = 0 if plan.legal_ids is None else int(plan.legal_ids.shape[0])
+        out = torch.empty(R + nl + 1, dtype=torch.float32, device=self._device)
+        self._status.zero_()
+        self._model.run(dstep, self.pool, value_stm=out[:R], legal_logits=out[R : R + nl],
+                        status=self._status)
+        out[R + nl :].copy_(self._status.view(torch.float32))
+        host = torch.empty(R + nl + 1, dtype=torch.float32, pin_memory=True)
+        host.copy_(out, non_blocking=True)
+        torch.cuda.current_stream(self._device).synchronize()
+        status = int(host[R + nl :].view(torch.int32).item())
+        if status != _native.IMBA_OK:
+            raise _native.ImbaError(status, "device-side check")
+        arr = host.numpy()
+        return arr[:R].copy(), arr[R : R + nl].copy(), dstep
+
+    def _service_roots(self, requests: list) -> list:
+        if not requests:
+            return []
+        full = [i for i, r in enumerate(requests) if r.batch_arrays is not None]
+        inc = [i for i, r in enumerate(requests) if r.incremental_tokens is not None]
+        responses: list[Any] = [None] * len(requests)
+        if full:
+            for i, resp in zip(full, self._service_full_roots([requests[i] for i in full])):
+                responses[i] = resp
+        if inc:
+            for i, resp in zip(inc, self._service_incremental_roots([requests[i] for i in inc])):
+                responses[i] = resp
+        return responses
+
+    def _root_step(self, seqs: list[KVSequence], starts: list[int], tokens: list[dict], legal: list[list[int]]):
+        """One step appending ``tokens[g]`` to ``seqs[g]`` after ``starts[g]``
+        existing tokens (causal within the new tokens).  Legal ids and value
+        are produced for each group's last token."""
+        counts = np.asarray([len(t["piece_ids"]) for t in tokens], dtype=np.int64)
+        G = len(seqs)
+        row_group = np.repeat(np.arange(G), counts)
+        local = np.arange(int(counts.sum())) - np.repeat(np.cumsum(counts) - counts, counts)
+        base = np.asarray(starts, dtype=np.int64)[row_group]
+        positions = base + local
+        dst = np.concatenate([s.reserve(int(n)) for s, n in zip(seqs, counts)]) if G else np.zeros(0, np.int64)
+        pages = [s.page_array() for s in seqs]
+        gpo = np.concatenate([[0], np.cumsum([len(p) for p in pages])]).astype(np.int32)
+        piece = np.concatenate([np.asarray(t["piece_ids"], dtype=np.int64).reshape(-1, 64) for t in tokens])
+        if piece.size and (piece.min() < 0 or piece.max() > 12):
+            raise ValueError("piece_ids values must be in [0, 12]")
+        side = np.stack([np.concatenate([np.asarray(t[k], dtype=np.int64).reshape(-1) for t in tokens])
+                         for k in _TOKEN_FIELDS[1:]], axis=1)
+        R = int(counts.sum())
+        last = np.cumsum(counts) - 1
+        per_row = [[] for _ in range(R)]
+        for g, ids in enumerate(legal):
+            per_row[last[g]] = list(ids)
+        loff, lids = _ids_csr(per_row)
+        plan = StepPlan(
+            piece_ids=piece.astype(np.uint8),
+            side_ids=side.clip(-(2**31), 2**31 - 1).astype(np.int32),
+            positions=positions.astype(np.int32),
+            row_group=row_group.astype(np.int32),
+            row_vis=(positions + 1).astype(np.int32),
+            row_extra_off=np.zeros(R + 1, np.int32),
+            extra_slot=np.zeros(0, np.int32),
+            extra_pos=np.zeros(0, np.int32),
+            row_dst_slot=dst.astype(np.int32),
+            group_page_off=gpo,
+            group_pages=np.concatenate(pages).astype(np.int32) if pages else np.zeros(0, np.int32),
+            legal_off=loff,
+            legal_ids=lids,
+        )
+        value_stm, legal_flat, _ = self._run_rows(plan, G)
+        outs = []
+        for g in range(G):
+            a, b = int(loff[last[g]]), int(loff[last[g] + 1])
+            outs.append((float(value_stm[last[g]]), legal_flat[a:b].tolist()))
+        return outs
+
+    def _service_full_roots(self, requests: list) -> list:
+        t0 = time.perf_counter()
+        seqs, tokens, legal = [], [], []
+        for r in requests:
+            ba = r.batch_arrays
+            offs = list(ba["seq_offsets"])
+            if len(offs) != 2:
+                raise ValueError("a full RootEvalRequest must carry exactly one game (seq_offsets [0, T])")
+            T = int(ba["total_tokens"])
+            if T < 1:
+                raise ValueError("a full RootEvalRequest must carry at least one token")
+            tokens.append({k: ba[k] for k in _TOKEN_FIELDS})
+            seqs.append(KVSequence(self.pool))
+            legal.append(list(r.legal_vocab_ids))
+        self._sync_if_profiling()
+        t1 = time.perf_counter()
+        try:
+            outs = self._root_step(seqs, [0] * len(seqs), tokens, legal)
+        except BaseException:
+            for s in seqs:
+                s.release()
+            raise
+        t2 = time.perf_counter()
+        self.stats["root_build_s"] += t1 - t0
+        self.stats["root_gpu_s"] += t2 - t1
+        self.stats["root_calls"] += 1
+        self.stats["root_reqs"] += len(requests)
+        responses = []
+        for r, seq, (v, ll) in zip(requests, seqs, outs):
+            w = int(r.worker_id)
+            old = self._games.pop(w, None)
+            if old is not None:
+                old.seq.release()
+            game = _GameState(seq=seq, prefix_len=seq.length)
+            self._games[w] = game
+            self._set_turn((w, int(r.turn_id)), game)
+            responses.append(RootEvalResponse(turn_id=r.turn_id, value_stm=v, legal_logits=ll))
+        self.stats["root_post_s"] += time.perf_counter() - t2
+        return responses
+
+    def _service_incremental_roots(self, requests: list) -> list:
+        max_pos = int(self._model.position_embedding.max_seq_len)
+        seen = set()
+        for r in requests:
+            w = int(r.worker_id)
+            game = self._games.get(w)
+            if game is None:
+                raise KeyError(
+                    f"RootEvalRequest(incremental) for worker={w} has no persisted game prefix -- "
+                    "missing/out-of-order full RootEvalRequest, or release_game() already freed it."
+                )
+            if w in seen:
+                raise RuntimeError(f"worker={w}: two incremental root extensions in one service() call")
+            seen.add(w)
+            if int(r.prefix_len_before) != game.prefix_len:
+                raise RuntimeError(
+                    f"worker={w}: incremental RootEvalRequest expected prefix_len_before={r.prefix_len_before}, "
+                    f"server has {game.prefix_len} -- worker/server prefix desync."
+                )
+            n_new = len(r.incremental_tokens["piece_ids"])
+            if n_new < 1:
+                raise ValueError(f"worker={w}: incremental RootEvalRequest carries zero new tokens.")
+            if game.prefix_len + n_new > max_pos:
+                raise RuntimeError(
+                    f"worker={w}: incremental root extension would grow the persisted prefix to "
+                    f"{game.prefix_len + n_new} tokens, past this model's max_position_embeddings={max_pos}."
+                )
+        t0 = time.perf_counter()
+        games = [self._games[int(r.worker_id)] for r in requests]
+        starts = [g.prefix_len for g in games]
+        outs = self._root_step([g.seq for g in games], starts,
+                               [{k: r.incremental_tokens[k] for k in _TOKEN_FIELDS} for r in requests],
+                               [list(r.legal_vocab_ids) for r in requests])
+        self._sync_if_profiling()
+        self.stats["incremental_root_gpu_s"] += time.perf_counter() - t0
+        self.stats["incremental_root_calls"] += len(requests)
+        self.stats["incremental_root_reqs"] += len(requests)
+        responses = []
+        for r, game, (v, ll) in zip(requests, games, outs):
+            n_new = len(r.incremental_tokens["piece_ids"])
+            self.stats["incremental_root_tokens"] += n_new
+            game.prefix_len += n_new
+            self._set_turn((int(r.worker_id), int(r.turn_id)), game)
+            responses.append(RootEvalResponse(turn_id=r.turn_id, value_stm=v, legal_logits=ll))
+        return responses
+
+    # ------------------------------------------------------------------
+    def _service_waves(self, requests: list) -> list:
+        if not requests:
+            return []
+        t0 = time.perf_counter()
+        turns: list[_TurnState] = []
+        chains_per_req: list[list[list[int]]] = []
+        for req in requests:
+            key = (int(req.worker_id), int(req.turn_id))
+            turn = self._turns.get(key)
+            if turn is None:
+                raise KeyError(
+                    f"WaveRequest for worker={req.worker_id} turn={req.turn_id} has no registered root eval -- "
+                    "missing/out-of-order RootEvalRequest, or release_turn() already freed this turn."
+                )
+            chains = [turn.node_chains[row.parent_id] if row.parent_id is not None else [] for row in req.rows]
+            turns.append(turn)
+            chains_per_req.append(chains)
+        # Tokens (one per row), in request order.
+        rows = [row for req in requests for row in req.rows]
+        R = len(rows)
+        piece = np.asarray([row.board_state["piece_ids"] for row in rows], dtype=np.int64).reshape(R, 64)
+        if piece.size and (piece.min() < 0 or piece.max() > 12):
+            raise ValueError("piece_ids values must be in [0, 12]")
+        side = np.empty((R, 7), dtype=np.int64)
+        side[:, 0] = EVENT_TOKEN_ID
+        for j, k in enumerate(("turn_id", "castle_id", "ep_file_id", "halfmove_bucket_id", "fullmove_bucket_id")):
+            side[:, 1 + j] = [int(row.board_state[k]) for row in rows]
+        side[:, 6] = [int(row.prev_move_vocab_id) for row in rows]
+        # Arena rows (logical ids exactly as _KVArena.append mints them) and slots.
+        counts = [len(req.rows) for req in requests]
+        own_rows: list[list[int]] = []
+        dst_parts, extra_slot_parts, extra_pos_parts, extra_len, positions = [], [], [], [], []
+        group_pages, gpo = [], [0]
+        for g, (req, turn, chains) in enumerate(zip(requests, turns, chains_per_req)):
+            n = counts[g]
+            if turn.arena is None:
+                turn.arena = KVSequence(self.pool)
+            start = turn.arena.length
+            dst = turn.arena.reserve(n)
+            own = list(range(start, start + n))
+            own_rows.append(own)
+            dst_parts.append(dst)
+            P = turn.prefix_len
+            depths = np.fromiter((len(c) for c in chains), dtype=np.int64, count=n)
+            positions.append(P + depths)
+            flat_chain = np.fromiter((x for c in chains for x in c), dtype=np.int64, count=int(depths.sum()))
+            chain_slots = turn.arena.slots_of(flat_chain) if flat_chain.size else np.zeros(0, np.int64)
+            chain_pos = P + (np.arange(flat_chain.size) - np.repeat(np.cumsum(depths) - depths, depths))
+            # per row: chain slots then own slot
+            ins = np.cumsum(depths)  # insertion points for own slots
+            es = np.insert(chain_slots, ins, dst)
+            ep = np.insert(chain_pos, ins, P + depths)
+            extra_slot_parts.append(es)
+            extra_pos_parts.append(ep)
+            extra_len.append(depths + 1)
+            pg = turn.seq.page_array(P)
+            group_pages.append(pg)
+            gpo.append(gpo[-1] + len(pg))
+        pos = np.concatenate(positions)
+        elen = np.concatenate(extra_len)
+        loff, lids = _ids_csr([row.legal_vocab_ids for row in rows])
+        plan = StepPlan(
+            piece_ids=piece.astype(np.uint8),
+            side_ids=side.clip(-(2**31), 2**31 - 1).astype(np.int32),
+            positions=pos.astype(np.int32),
+            row_group=np.repeat(np.arange(len(requests)), counts).astype(np.int32),
+            row_vis=np.repeat([t.prefix_len for t in turns], counts).astype(np.int32),
+            row_extra_off=np.concatenate([[0], np.cumsum(elen)]).astype(np.int32),
+            extra_slot=np.concatenate(extra_slot_parts).astype(np.int32),
+            extra_pos=np.concatenate(extra_pos_parts).astype(np.int32),
+            row_dst_slot=np.concatenate(dst_parts).astype(np.int32),
+            group_page_off=np.asarray(gpo, dtype=np.int32),
+            group_pages=np.concatenate(group_pages).astype(np.int32),
+            legal_off=loff,
+            legal_ids=lids,
+        )
+        self._sync_if_profiling()
+        t1 = time.perf_counter()
+        value_stm, legal_flat, _ = self._run_rows(plan, R)
+        t2 = time.perf_counter()
+        self.stats["wave_build_s"] += t1 - t0
+        self.stats["wave_gpu_s"] += t2 - t1
+        self.stats["wave_calls"] += 1
+        self.stats["wave_reqs"] += len(requests)
+        self.stats["wave_rows"] += R
+        responses = []
+        r0 = 0
+        for req, turn, chains, own in zip(requests, turns, chains_per_req, own_rows):
+            for row, chain, own_row in zip(req.rows, chains, own):
+                turn.node_chains[row.node_id] = chain + [own_row]
+            out_rows = []
+            for i in range(len(req.rows)):
+                a, b = int(loff[r0 + i]), int(loff[r0 + i + 1])
+                out_rows.append((float(value_stm[r0 + i]), legal_flat[a:b].tolist()))
+            r0 += len(req.rows)
+            responses.append(WaveResponse(rows=out_rows))
+        self._sync_if_profiling()
+        self.stats["wave_post_s"] += time.perf_counter() - t2
+        return responses
