@@ -42,11 +42,14 @@ BOARD_PARAM_FLOATS = 2 * BOARD_BLOCK_FLOATS + 128
 
 EXPORTED_SYMBOLS = (
     "imba_version",
+    "imba_abi_size",
     "imba_device_arch",
     "imba_model_create",
     "imba_model_destroy",
     "imba_step_workspace_bytes",
     "imba_step",
+    "imba_profile_event_count",
+    "imba_step_profiled",
     "imba_kv_scatter",
     "imba_kv_gather",
 )
@@ -162,6 +165,15 @@ def load() -> ctypes.CDLL:
             )
         lib = ctypes.CDLL(LIB_PATH)
         lib.imba_version.restype = _I32
+        lib.imba_abi_size.argtypes = [_I32]
+        lib.imba_abi_size.restype = _I32
+        want = (ctypes.sizeof(ModelDesc), ctypes.sizeof(StepDesc), ctypes.sizeof(PoolDesc))
+        got = tuple(int(lib.imba_abi_size(i)) for i in range(3))
+        if got != want:
+            raise NativeLibraryError(
+                f"{LIB_PATH} was built against a different include/imba_b200.h (struct sizes {got}, "
+                f"binding expects {want}): rebuild with `python -m imba_chess_b200.build`"
+            )
         lib.imba_device_arch.restype = _I32
         lib.imba_model_create.argtypes = [ctypes.POINTER(ModelDesc), ctypes.POINTER(_P)]
         lib.imba_model_create.restype = _I32
@@ -171,6 +183,11 @@ def load() -> ctypes.CDLL:
         lib.imba_step_workspace_bytes.restype = ctypes.c_size_t
         lib.imba_step.argtypes = [_P, ctypes.POINTER(StepDesc), ctypes.POINTER(PoolDesc), _P, ctypes.c_size_t, _P]
         lib.imba_step.restype = _I32
+        lib.imba_profile_event_count.argtypes = [_P]
+        lib.imba_profile_event_count.restype = _I32
+        lib.imba_step_profiled.argtypes = [_P, ctypes.POINTER(StepDesc), ctypes.POINTER(PoolDesc), _P,
+                                           ctypes.c_size_t, _P, ctypes.POINTER(_P), _I32]
+        lib.imba_step_profiled.restype = _I32
         for name in ("imba_kv_scatter", "imba_kv_gather"):
             fn = getattr(lib, name)
             fn.argtypes = [_P, ctypes.POINTER(PoolDesc), _I32, _I32, _P, _P, _P, _P, _P]

@@ -93,9 +93,21 @@ imba_status_t validate_step(const imba_model* m, const imba_step_desc* st, const
   return IMBA_OK;
 }
 
+// Records phase-boundary events when profiling; a no-op otherwise.
+struct PhaseMarks {
+  void* const* ev = nullptr;
+  int n = 0;
+  int next = 0;
+  cudaError_t mark(cudaStream_t s) {
+    if (!ev) return cudaSuccess;
+    if (next >= n) return cudaErrorInvalidValue;
+    return cudaEventRecord(static_cast<cudaEvent_t>(ev[next++]), s);
+  }
+};
+
 template <typename T>
 imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba_pool_desc& pool, Workspace& w,
-                       cudaStream_t s) {
+                       cudaStream_t s, PhaseMarks& pm) {
   const imba_model_desc& md = m->d;
   const int R = st.num_rows, d = md.model_dim, H = md.num_heads;
   const int hdv = H * md.linear_dim;
@@ -108,9 +120,12 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
     if (e != cudaSuccess) return IMBA_ERR_CUDA; \
   } while (0)
 
+  IMBA_CK(pm.mark(s));
   IMBA_CK(launch_embed(md, st, w.x, s));
+  IMBA_CK(pm.mark(s));
   for (int l = 0; l < md.num_layers; ++l) {
     IMBA_CK(launch_ln_rows<T>(w.x, R, d, 1e-6f, static_cast<T*>(w.xn), s));
+    IMBA_CK(pm.mark(s));
     EpiUVQK<T> epi{w.u, static_cast<T*>(w.q), poolp, st.row_dst_slot, g, l, st.status};
     if (!gemm_tc_launch_uvqk(m, l, R, static_cast<const T*>(w.xn), epi, s, &e)) {
       IMBA_CK(launch_gemm_simt<T, T, EpiUVQK<T>>(static_cast<const T*>(w.xn), d,
@@ -118,9 +133,12 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
     } else if (e != cudaSuccess) {
       return IMBA_ERR_CUDA;
     }
+    IMBA_CK(pm.mark(s));
     AttnArgs aa{w.q, pool.base, g, l, md.ps_w[l], md.max_pos, 1.0f / sqrtf((float)md.attention_dim), st, w.attn};
     IMBA_CK(launch_attn_simt<T>(aa, s));
+    IMBA_CK(pm.mark(s));
     IMBA_CK(launch_gate<T>(w.attn, w.u, R, hdv, static_cast<T*>(w.gated), s));
+    IMBA_CK(pm.mark(s));
     EpiResidual er{w.x, md.o_b[l], d};
     if (!gemm_tc_launch_out(m, l, R, static_cast<const T*>(w.gated), er, s, &e)) {
       IMBA_CK(launch_gemm_simt<T, T, EpiResidual>(static_cast<const T*>(w.gated), hdv,
@@ -128,10 +146,12 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
     } else if (e != cudaSuccess) {
       return IMBA_ERR_CUDA;
     }
+    IMBA_CK(pm.mark(s));
   }
   const bool bf = md.dtype == IMBA_DTYPE_BF16;
   IMBA_CK(launch_final_ln<T>(w.x, R, d, md.final_norm_w, md.final_norm_b, w.xf32, bf ? static_cast<T*>(w.xf) : nullptr,
                              bf ? static_cast<T*>(w.xf_lo) : nullptr, s));
+  IMBA_CK(pm.mark(s));
   if (st.hidden) IMBA_CK(cudaMemcpyAsync(st.hidden, w.x, (size_t)R * d * 4, cudaMemcpyDeviceToDevice, s));
   float* logits = st.logits ? st.logits : w.logits;
   const bool need_logits = st.logits || st.legal_off;
@@ -143,13 +163,16 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
       return IMBA_ERR_CUDA;
     }
   }
+  IMBA_CK(pm.mark(s));
   if (md.has_value_head) {
     const int hd = d / 2;
     EpiBiasSilu eb{w.hval, md.value0_b, hd};
     const T* xin = bf ? static_cast<const T*>(w.xf) : reinterpret_cast<const T*>(w.xf32);
     IMBA_CK(launch_gemm_simt<T, T, EpiBiasSilu>(xin, d, static_cast<const T*>(md.value0_w), d, R, hd, d, eb, s));
   }
+  IMBA_CK(pm.mark(s));
   IMBA_CK(launch_value_legal(md, st, w.hval, logits, s));
+  IMBA_CK(pm.mark(s));
 #undef IMBA_CK
   return IMBA_OK;
 }
@@ -167,6 +190,14 @@ Workspace carve_workspace(const imba_model* m, int32_t rows, void* base) {
 extern "C" {
 
 int32_t imba_version(void) { return 1; }
+int32_t imba_abi_size(int32_t which) {
+  switch (which) {
+    case 0: return (int32_t)sizeof(imba_model_desc);
+    case 1: return (int32_t)sizeof(imba_step_desc);
+    case 2: return (int32_t)sizeof(imba_pool_desc);
+    default: return -1;
+  }
+}
 int32_t imba_device_arch(void) { return 1000; }
 
 imba_status_t imba_model_create(const imba_model_desc* desc, imba_model** out) {
@@ -194,8 +225,12 @@ size_t imba_step_workspace_bytes(const imba_model* model, int32_t max_rows) {
   return imba::workspace_layout(model, max_rows, nullptr, nullptr);
 }
 
-imba_status_t imba_step(const imba_model* model, const imba_step_desc* step, const imba_pool_desc* pool,
-                        void* workspace, size_t workspace_bytes, void* stream) {
+int32_t imba_profile_event_count(const imba_model* model) {
+  return model ? 2 + 5 * model->d.num_layers + 4 : 0;
+}
+
+static imba_status_t step_impl(const imba_model* model, const imba_step_desc* step, const imba_pool_desc* pool,
+                               void* workspace, size_t workspace_bytes, void* stream, imba::PhaseMarks pm) {
   if (!model) return IMBA_ERR_ARG;
   const imba_status_t v = imba::validate_step(model, step, pool);
   if (v != IMBA_OK) return v;
@@ -204,8 +239,25 @@ imba_status_t imba_step(const imba_model* model, const imba_step_desc* step, con
   if (!workspace || workspace_bytes < need) return IMBA_ERR_OOM;
   imba::Workspace w = imba::carve_workspace(model, step->num_rows, workspace);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (model->d.dtype == IMBA_DTYPE_BF16) return imba::run_step<imba::bf16>(model, *step, *pool, w, s);
-  return imba::run_step<float>(model, *step, *pool, w, s);
+  if (model->d.dtype == IMBA_DTYPE_BF16) return imba::run_step<imba::bf16>(model, *step, *pool, w, s, pm);
+  return imba::run_step<float>(model, *step, *pool, w, s, pm);
+}
+
+imba_status_t imba_step(const imba_model* model, const imba_step_desc* step, const imba_pool_desc* pool,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  return step_impl(model, step, pool, workspace, workspace_bytes, stream, imba::PhaseMarks{});
+}
+
+imba_status_t imba_step_profiled(const imba_model* model, const imba_step_desc* step, const imba_pool_desc* pool,
+                                 void* workspace, size_t workspace_bytes, void* stream, void* const* events,
+                                 int32_t num_events) {
+  if (!model || !events || num_events != imba_profile_event_count(model)) return IMBA_ERR_ARG;
+  for (int i = 0; i < num_events; ++i)
+    if (!events[i]) return IMBA_ERR_ARG;
+  imba::PhaseMarks pm;
+  pm.ev = events;
+  pm.n = num_events;
+  return step_impl(model, step, pool, workspace, workspace_bytes, stream, pm);
 }
 
 static imba_status_t kv_copy(const imba_model* model, const imba_pool_desc* pool, int32_t layer, int32_t n,

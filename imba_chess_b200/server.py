@@ -35,6 +35,7 @@ from . import _native
 from .kvpool import PAGE, KVPool, KVSequence
 from .model import B200HSTUChessModel
 from .plan import DeviceStep, StepPlan
+from .steps import WaveGroup, ids_csr, root_plan, wave_plan
 from .protocol import RootEvalResponse, WaveResponse, is_root_request, is_wave_request
 from .synth import EVENT_TOKEN_ID, TOKEN_FIELDS
 
@@ -64,13 +65,6 @@ class _TurnState:
         if self.arena is not None:
             self.arena.release()
             self.arena = None
-
-
-def _ids_csr(id_lists: list) -> tuple[np.ndarray, np.ndarray]:
-    lengths = np.fromiter((len(x) for x in id_lists), dtype=np.int64, count=len(id_lists))
-    off = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
-    flat = np.fromiter((v for ids in id_lists for v in ids), dtype=np.int64, count=int(off[-1]))
-    return off, flat.astype(np.int32)
 
 
 class ActorInferenceServer:
@@ -199,51 +193,15 @@ class ActorInferenceServer:
                 responses[i] = resp
         return responses
 
-    def _root_step(self, seqs: list[KVSequence], starts: list[int], tokens: list[dict], legal: list[list[int]]):
-        """One step appending ``tokens[g]`` to ``seqs[g]`` after ``starts[g]``
-        existing tokens (causal within the new tokens).  Legal ids and value
-        are produced for each group's last token."""
-        counts = np.asarray([len(t["piece_ids"]) for t in tokens], dtype=np.int64)
-        G = len(seqs)
-        row_group = np.repeat(np.arange(G), counts)
-        local = np.arange(int(counts.sum())) - np.repeat(np.cumsum(counts) - counts, counts)
-        base = np.asarray(starts, dtype=np.int64)[row_group]
-        positions = base + local
-        dst = np.concatenate([s.reserve(int(n)) for s, n in zip(seqs, counts)]) if G else np.zeros(0, np.int64)
-        pages = [s.page_array() for s in seqs]
-        gpo = np.concatenate([[0], np.cumsum([len(p) for p in pages])]).astype(np.int32)
-        piece = np.concatenate([np.asarray(t["piece_ids"], dtype=np.int64).reshape(-1, 64) for t in tokens])
-        if piece.size and (piece.min() < 0 or piece.max() > 12):
-            raise ValueError("piece_ids values must be in [0, 12]")
-        side = np.stack([np.concatenate([np.asarray(t[k], dtype=np.int64).reshape(-1) for t in tokens])
-                         for k in _TOKEN_FIELDS[1:]], axis=1)
-        R = int(counts.sum())
-        last = np.cumsum(counts) - 1
-        per_row = [[] for _ in range(R)]
-        for g, ids in enumerate(legal):
-            per_row[last[g]] = list(ids)
-        loff, lids = _ids_csr(per_row)
-        plan = StepPlan(
-            piece_ids=piece.astype(np.uint8),
-            side_ids=side.clip(-(2**31), 2**31 - 1).astype(np.int32),
-            positions=positions.astype(np.int32),
-            row_group=row_group.astype(np.int32),
-            row_vis=(positions + 1).astype(np.int32),
-            row_extra_off=np.zeros(R + 1, np.int32),
-            extra_slot=np.zeros(0, np.int32),
-            extra_pos=np.zeros(0, np.int32),
-            row_dst_slot=dst.astype(np.int32),
-            group_page_off=gpo,
-            group_pages=np.concatenate(pages).astype(np.int32) if pages else np.zeros(0, np.int32),
-            legal_off=loff,
-            legal_ids=lids,
-        )
-        value_stm, legal_flat, _ = self._run_rows(plan, G)
-        outs = []
-        for g in range(G):
-            a, b = int(loff[last[g]]), int(loff[last[g] + 1])
-            outs.append((float(value_stm[last[g]]), legal_flat[a:b].tolist()))
-        return outs
+    def _root_step(self, seqs: list[KVSequence], tokens: list[dict], legal: list[list[int]]):
+        """One step appending ``tokens[g]`` to ``seqs[g]`` (causal within the
+        new tokens).  Value and legal logits come from each group's last token."""
+        plan, last = root_plan(seqs, tokens, legal)
+        value_stm, legal_flat, _ = self._run_rows(plan, len(seqs))
+        loff = plan.legal_off
+        return [
+            (float(value_stm[i]), legal_flat[int(loff[i]) : int(loff[i + 1])].tolist()) for i in last
+        ]
 
     def _service_full_roots(self, requests: list) -> list:
         t0 = time.perf_counter()
@@ -262,7 +220,7 @@ class ActorInferenceServer:
         self._sync_if_profiling()
         t1 = time.perf_counter()
         try:
-            outs = self._root_step(seqs, [0] * len(seqs), tokens, legal)
+            outs = self._root_step(seqs, tokens, legal)
         except BaseException:
             for s in seqs:
                 s.release()
@@ -314,8 +272,10 @@ class ActorInferenceServer:
                 )
         t0 = time.perf_counter()
         games = [self._games[int(r.worker_id)] for r in requests]
-        starts = [g.prefix_len for g in games]
-        outs = self._root_step([g.seq for g in games], starts,
+        for g in games:
+            if g.seq.length != g.prefix_len:
+                raise RuntimeError("game prefix sequence and recorded prefix length disagree")
+        outs = self._root_step([g.seq for g in games],
                                [{k: r.incremental_tokens[k] for k in _TOKEN_FIELDS} for r in requests],
                                [list(r.legal_vocab_ids) for r in requests])
         self._sync_if_profiling()
@@ -361,53 +321,14 @@ class ActorInferenceServer:
             side[:, 1 + j] = [int(row.board_state[k]) for row in rows]
         side[:, 6] = [int(row.prev_move_vocab_id) for row in rows]
         # Arena rows (logical ids exactly as _KVArena.append mints them) and slots.
-        counts = [len(req.rows) for req in requests]
-        own_rows: list[list[int]] = []
-        dst_parts, extra_slot_parts, extra_pos_parts, extra_len, positions = [], [], [], [], []
-        group_pages, gpo = [], [0]
-        for g, (req, turn, chains) in enumerate(zip(requests, turns, chains_per_req)):
-            n = counts[g]
+        groups = []
+        for turn, chains in zip(turns, chains_per_req):
             if turn.arena is None:
                 turn.arena = KVSequence(self.pool)
-            start = turn.arena.length
-            dst = turn.arena.reserve(n)
-            own = list(range(start, start + n))
-            own_rows.append(own)
-            dst_parts.append(dst)
-            P = turn.prefix_len
-            depths = np.fromiter((len(c) for c in chains), dtype=np.int64, count=n)
-            positions.append(P + depths)
-            flat_chain = np.fromiter((x for c in chains for x in c), dtype=np.int64, count=int(depths.sum()))
-            chain_slots = turn.arena.slots_of(flat_chain) if flat_chain.size else np.zeros(0, np.int64)
-            chain_pos = P + (np.arange(flat_chain.size) - np.repeat(np.cumsum(depths) - depths, depths))
-            # per row: chain slots then own slot
-            ins = np.cumsum(depths)  # insertion points for own slots
-            es = np.insert(chain_slots, ins, dst)
-            ep = np.insert(chain_pos, ins, P + depths)
-            extra_slot_parts.append(es)
-            extra_pos_parts.append(ep)
-            extra_len.append(depths + 1)
-            pg = turn.seq.page_array(P)
-            group_pages.append(pg)
-            gpo.append(gpo[-1] + len(pg))
-        pos = np.concatenate(positions)
-        elen = np.concatenate(extra_len)
-        loff, lids = _ids_csr([row.legal_vocab_ids for row in rows])
-        plan = StepPlan(
-            piece_ids=piece.astype(np.uint8),
-            side_ids=side.clip(-(2**31), 2**31 - 1).astype(np.int32),
-            positions=pos.astype(np.int32),
-            row_group=np.repeat(np.arange(len(requests)), counts).astype(np.int32),
-            row_vis=np.repeat([t.prefix_len for t in turns], counts).astype(np.int32),
-            row_extra_off=np.concatenate([[0], np.cumsum(elen)]).astype(np.int32),
-            extra_slot=np.concatenate(extra_slot_parts).astype(np.int32),
-            extra_pos=np.concatenate(extra_pos_parts).astype(np.int32),
-            row_dst_slot=np.concatenate(dst_parts).astype(np.int32),
-            group_page_off=np.asarray(gpo, dtype=np.int32),
-            group_pages=np.concatenate(group_pages).astype(np.int32),
-            legal_off=loff,
-            legal_ids=lids,
-        )
+            groups.append(WaveGroup(prefix=turn.seq, prefix_len=turn.prefix_len, arena=turn.arena, chains=chains))
+        plan, own_rows = wave_plan(groups, piece.astype(np.uint8), side.clip(-(2**31), 2**31 - 1).astype(np.int32),
+                                   [row.legal_vocab_ids for row in rows])
+        loff = plan.legal_off
         self._sync_if_profiling()
         t1 = time.perf_counter()
         value_stm, legal_flat, _ = self._run_rows(plan, R)

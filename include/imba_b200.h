@@ -179,6 +179,10 @@ typedef struct imba_step_desc {
 
 /* Library version and the compiled device architecture (e.g. 1000 for sm_100a). */
 IMBA_API int32_t imba_version(void);
+/* sizeof() of the descriptor structs as compiled into the library
+ * (0: imba_model_desc, 1: imba_step_desc, 2: imba_pool_desc), so a binding
+ * can refuse a library built against a different header. */
+IMBA_API int32_t imba_abi_size(int32_t which);
 IMBA_API int32_t imba_device_arch(void);
 
 /* Validate a model description and build a handle.  No device memory is
@@ -194,6 +198,20 @@ IMBA_API size_t imba_step_workspace_bytes(const imba_model* model, int32_t max_r
 IMBA_API imba_status_t imba_step(const imba_model* model, const imba_step_desc* step,
                         const imba_pool_desc* pool, void* workspace,
                         size_t workspace_bytes, void* stream);
+
+/* Per-phase timing.  imba_step_profiled is imba_step that additionally
+ * records caller-created CUDA events (cudaEvent_t handles) on `stream` at
+ * every phase boundary, in this order:
+ *   [0] start, [1] after the content embedding,
+ *   per layer l: [2+5l] input LN, [3+5l] uvqk GEMM + KV append,
+ *                [4+5l] attention, [5+5l] gate, [6+5l] output GEMM,
+ *   then final LN, policy GEMM, value GEMM, value/legal kernel.
+ * num_events must equal imba_profile_event_count(model). */
+IMBA_API int32_t imba_profile_event_count(const imba_model* model);
+IMBA_API imba_status_t imba_step_profiled(const imba_model* model, const imba_step_desc* step,
+                                          const imba_pool_desc* pool, void* workspace,
+                                          size_t workspace_bytes, void* stream,
+                                          void* const* events, int32_t num_events);
 
 /* KV page kernels for dense <-> paged conversion (the reference's dense
  * prefix/suffix tensors, hstu_model.py:651-752).  `dense_k` is [n, H, d_qk]
