@@ -1,0 +1,613 @@
+#!/usr/bin/env python
+"""Benchmark: positions evaluated per second on the grouped-decode wave.
+
+Workload (one step = one wave): a bf16 HSTU chess model, d_model 512, 8
+layers, 8 heads (head dims 64/64), random-initialised with the reference's
+initialisers; 256 parent positions with game prefixes of U[20, 200] plies
+(n plies = n + 2 tokens), each expanding U[20, 40] sibling candidate moves
+(depth-0 children sharing the parent prefix in the paged KV pool, 16-token
+pages); every sibling carries U[20, 40] legal move ids.  A step computes
+every sibling's policy logits at its legal ids, their log-softmax, the WDL
+value and v = p(win) - p(loss), and appends the sibling's KV to its turn
+arena.  Inputs are seeded synthetic token streams with the reference's
+encoded value ranges (no dataset or checkpoint is available).
+
+Reported:
+  value  - positions/s with the wave's inputs resident in HBM (device time,
+           CUDA events on the launching stream, max over ranks).
+  e2e    - positions/s through the C-ABI step with host buffers: pinned
+           host->device copy of the packed wave, the step, device->host copy
+           of value / legal logits / log-priors, synchronised every step; its
+           p50 per-wave latency.
+  service_api - the reference-compatible ActorInferenceServer.service() on
+           the same wave (Python wire objects in and out), p50 latency.
+  roofline - the dominant kernel's algorithmic work per launch over its
+           average launch duration (CUDA events around each phase inside the
+           timed region), against the measured peaks.
+  cpu_baseline - the CPU oracle (numpy restatement of the reference decode
+           path) on a bounded sample of the same workload on the host cores.
+
+Multi-GPU (torchrun): each rank runs the same-size workload on its own
+parents (weak scaling, no collective on the data path).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "positions evaluated/sec (grouped decode)"
+UNIT = "positions/s"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--parents", type=int, default=256)
+    ap.add_argument("--plies", type=int, nargs=2, default=(20, 200))
+    ap.add_argument("--siblings", type=int, nargs=2, default=(20, 40))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-service", action="store_true")
+    ap.add_argument("--cpu-sample-parents", type=int, default=4)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {k: float(p[k]) for k in PEAKS_FALLBACK}, "measured"
+    except Exception:
+        return dict(PEAKS_FALLBACK), "fallback"
+
+
+# ----------------------------------------------------------------------
+# Workload
+# ----------------------------------------------------------------------
+def workload(args, rank):
+    from imba_chess_b200 import synth
+
+    dims = synth.D512
+    wave = synth.grouped_wave(dims, n_parents=args.parents, plies=tuple(args.plies), siblings=tuple(args.siblings),
+                              seed=1234 + rank * args.parents)
+    return dims, wave
+
+
+# ----------------------------------------------------------------------
+# Clock sampling during the timed region
+# ----------------------------------------------------------------------
+REASON_FIELDS = (
+    ("hw_slowdown", "clocks_event_reasons.hw_slowdown"),
+    ("hw_thermal_slowdown", "clocks_event_reasons.hw_thermal_slowdown"),
+    ("sw_thermal_slowdown", "clocks_event_reasons.sw_thermal_slowdown"),
+    ("sw_power_cap", "clocks_event_reasons.sw_power_cap"),
+)
+
+
+class ClockSampler:
+    def __init__(self, device_index: int) -> None:
+        self.samples: list[tuple[float, float, list[str]]] = []
+        self._proc = None
+        self._thread = None
+        q = ",".join(["clocks.sm", "clocks.max.sm"] + [f for _, f in REASON_FIELDS])
+        ident = str(device_index)
+        try:
+            import torch
+
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            pass
+        self._cmd = ["nvidia-smi", "-i", ident, f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "200"]
+
+    def start(self):
+        try:
+            self._proc = subprocess.Popen(self._cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self._proc = None
+            return
+        self._thread = threading.Thread(target=self._read, daemon=True)
+        self._thread.start()
+
+    def _read(self):
+        for line in self._proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 2 + len(REASON_FIELDS):
+                continue
+            try:
+                sm, mx = float(parts[0]), float(parts[1])
+            except ValueError:
+                continue
+            active = [name for (name, _), v in zip(REASON_FIELDS, parts[2:]) if v.lower() == "active"]
+            self.samples.append((sm, mx, active))
+
+    def stop(self):
+        if self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except Exception:
+                self._proc.kill()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        loaded = [s for s in self.samples if s[0] > 0.5 * s[1]] or self.samples
+        reasons = sorted({r for s in loaded for r in s[2]})
+        return {
+            "sm_mhz": statistics.median(s[0] for s in loaded),
+            "sm_max_mhz": max(s[1] for s in self.samples),
+            "reasons": reasons,
+            "samples": len(self.samples),
+        }
+
+
+# ----------------------------------------------------------------------
+# CPU oracle baseline
+# ----------------------------------------------------------------------
+def cpu_oracle_rate(dims, wave, n_sample_parents, seconds, steps=None):
+    """Rows/s of the CPU oracle's grouped decode (legal log-priors and v
+    included) on the first ``n_sample_parents`` parents of the wave."""
+    from imba_chess_b200 import synth
+    from oracle.hstu_np import OracleModel, gather_legal, log_softmax_f32, value_stm
+
+    sd = synth.make_state_dict(dims, 2, profile="reference")
+    orc = OracleModel(sd, dims)
+    gsel = list(range(min(n_sample_parents, len(wave.prefix_tokens))))
+    lens = [wave.prefix_lens[g] for g in gsel]
+    pref = [orc.forward(wave.prefix_tokens[g], [0, lens[i]])["kv_caches"] for i, g in enumerate(gsel)]
+    max_p = max(lens)
+    grouped = []
+    for l in range(dims.num_layers):
+        ks = np.stack([np.pad(p[l][0], ((0, 0), (0, max_p - p[l][0].shape[1]), (0, 0))) for p in pref])
+        vs = np.stack([np.pad(p[l][1], ((0, 0), (0, max_p - p[l][1].shape[1]), (0, 0))) for p in pref])
+        grouped.append((ks, vs))
+    rows = np.nonzero(np.isin(wave.group_index, gsel))[0]
+    tok = synth.slice_tokens(wave.row_tokens, rows)
+    gi = wave.group_index[rows]
+    legal = [wave.legal_ids[i] for i in rows]
+
+    def one():
+        out = orc.forward_decode_grouped(new_token_batch=tok, positions=np.asarray(lens)[gi], group_index=gi,
+                                         prefix_kv_grouped=grouped, prefix_lens_list=lens)
+        for x in gather_legal(out["logits"], legal):
+            log_softmax_f32(x)
+        value_stm(out["value_logits"])
+
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+        if steps is not None:
+            if len(times) >= steps:
+                break
+        elif time.perf_counter() - t_start >= seconds:
+            break
+    return len(rows), times
+
+
+def run_reference(args):
+    """Reference arm: the CPU oracle port of the reference decode path, all
+    host threads, each step one bounded sample (4 parents) of the wave."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    dims, wave = workload(args, 0)
+    n_rows, _ = cpu_oracle_rate(dims, wave, args.cpu_sample_parents, 0.0, steps=1)  # warm (imports, caches)
+    for _ in range(max(args.warmup - 1, 0)):
+        cpu_oracle_rate(dims, wave, args.cpu_sample_parents, 0.0, steps=1)
+    n_rows, times = cpu_oracle_rate(dims, wave, args.cpu_sample_parents, 0.0, steps=args.steps)
+    total = float(sum(times))
+    value = n_rows * len(times) / total
+    cores = os.cpu_count() or 1
+    sample = f"{args.cpu_sample_parents} parents ({n_rows} sibling rows) of the {args.parents}-parent wave per step"
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1000.0 * total / len(times),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": workload_config(args),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args):
+    return {
+        "workload": "grouped-decode wave: bf16 HSTU d512/8L/8H (head dims 64/64, max_pos 513), "
+                    f"{args.parents} parents, prefixes U[{args.plies[0]},{args.plies[1]}] plies, "
+                    f"U[{args.siblings[0]},{args.siblings[1]}] depth-0 siblings each, 16-token KV pages",
+        "parents_per_gpu": args.parents,
+        "page_tokens": 16,
+        "l2": "inputs larger than L2 (prefix KV read per step > 126 MB at full size)",
+    }
+
+
+# ----------------------------------------------------------------------
+# B200 arm
+# ----------------------------------------------------------------------
+PHASES = ("embed", "ln", "uvqk_gemm", "attention", "gate", "out_gemm", "final_ln", "policy_gemm", "value_gemm",
+          "value_legal")
+
+
+def phase_times(events, L):
+    """Per-phase durations (ms) of one profiled step from its events."""
+    t = {p: 0.0 for p in PHASES}
+    e = events
+    t["embed"] += e[0].elapsed_time(e[1])
+    for l in range(L):
+        b = 1 + 5 * l
+        t["ln"] += e[b].elapsed_time(e[b + 1])
+        t["uvqk_gemm"] += e[b + 1].elapsed_time(e[b + 2])
+        t["attention"] += e[b + 2].elapsed_time(e[b + 3])
+        t["gate"] += e[b + 3].elapsed_time(e[b + 4])
+        t["out_gemm"] += e[b + 4].elapsed_time(e[b + 5])
+    b = 1 + 5 * L
+    t["final_ln"] += e[b].elapsed_time(e[b + 1])
+    t["policy_gemm"] += e[b + 1].elapsed_time(e[b + 2])
+    t["value_gemm"] += e[b + 2].elapsed_time(e[b + 3])
+    t["value_legal"] += e[b + 3].elapsed_time(e[b + 4])
+    return t
+
+
+def algorithmic_work(dims, plan, eb=2):
+    """Per-launch algorithmic FLOPs (tensor-bound phases) or bytes (HBM-bound
+    phases) of one wave step, and launches per step."""
+    R = plan.num_rows
+    d, L, H, dqk, dv, V = dims.model_dim, dims.num_layers, dims.num_heads, dims.attention_dim, dims.linear_dim, dims.vocab
+    uvqk_n = 2 * H * (dqk + dv)
+    board_mac = 2 * (64 * 64 * 192 + 2 * 4 * 64 * 64 * 16 + 64 * 64 * 64 + 2 * 64 * 64 * 128) + 64 * d
+    prefix_tokens = int(plan.row_vis[np.unique(plan.row_group, return_index=True)[1]].sum()) if R else 0
+    kv_tok = H * (dqk + dv) * eb
+    extras = int(plan.extra_slot.shape[0])
+    attn_bytes = prefix_tokens * kv_tok + extras * kv_tok + R * H * dqk * eb + R * H * dv * 4
+    nl = 0 if plan.legal_ids is None else int(plan.legal_ids.shape[0])
+    return {
+        "embed": ("tensor", 2.0 * board_mac * R, 1),
+        "ln": ("hbm", R * d * (4 + eb), L),
+        "uvqk_gemm": ("tensor", 2.0 * R * d * uvqk_n, L),
+        "attention": ("hbm", attn_bytes, L),
+        "gate": ("hbm", R * H * dv * (4 + 4 + eb), L),
+        "out_gemm": ("tensor", 2.0 * R * H * dv * d, L),
+        "final_ln": ("hbm", R * d * (4 + 4 + 2 * eb), 1),
+        "policy_gemm": ("tensor", 2.0 * R * d * V, 1),
+        "value_gemm": ("tensor", 2.0 * R * d * (d // 2), 1),
+        "value_legal": ("hbm", R * (d // 2) * 4 + nl * 12 + R * 16, 1),
+    }
+
+
+def read_traffic():
+    """Per-row DRAM traffic of each phase's kernel from the committed ncu
+    summary (profiles/ncu_traffic_per_row.txt: '<phase> <bytes per row>')."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic_per_row.txt")
+    out = {}
+    if os.path.exists(path):
+        for line in open(path):
+            parts = line.split()
+            if len(parts) == 2 and not line.startswith("#"):
+                try:
+                    out[parts[0]] = float(parts[1])
+                except ValueError:
+                    pass
+    return out
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device, timeout=__import__("datetime").timedelta(seconds=300))
+
+    from imba_chess_b200 import _native, synth
+    from imba_chess_b200.kvpool import KVSequence
+    from imba_chess_b200.model import B200HSTUChessModel
+    from imba_chess_b200.plan import DeviceStep
+    from imba_chess_b200.steps import WaveGroup, root_plan, wave_plan
+
+    dims, wave = workload(args, rank)
+    sd = synth.make_state_dict(dims, 2, profile="reference")
+    model = B200HSTUChessModel(sd, dtype=torch.bfloat16, device=device)
+    lens = wave.prefix_lens
+    B = wave.num_rows
+    pages_needed = sum(-(-n // 16) for n in lens) + 4 * (-(-B // 16)) + 64
+    pool = model.new_pool(pages_needed)
+    # Prefill every parent prefix (setup, untimed).
+    seqs = [KVSequence(pool) for _ in lens]
+    pplan, _ = root_plan(seqs, wave.prefix_tokens)
+    model.run(DeviceStep(pplan, device), pool)
+    torch.cuda.synchronize()
+    model.check_status()
+    # The wave: every parent's siblings at depth 0 in a fresh turn arena.
+    order = np.argsort(wave.group_index, kind="stable")
+    arenas = [KVSequence(pool) for _ in lens]
+    counts = np.bincount(wave.group_index, minlength=len(lens))
+    groups = [WaveGroup(prefix=seqs[g], prefix_len=lens[g], arena=arenas[g], chains=[[]] * int(counts[g]))
+              for g in range(len(lens))]
+    tok = synth.slice_tokens(wave.row_tokens, order)
+    from imba_chess_b200.plan import piece_ids_from_tokens, side_ids_from_tokens
+
+    plan, _ = wave_plan(groups, piece_ids_from_tokens(tok), side_ids_from_tokens(tok),
+                        [wave.legal_ids[i] for i in order])
+    R = plan.num_rows
+    NL = int(plan.legal_ids.shape[0])
+    dstep = DeviceStep(plan, device, pinned=True)
+    out = torch.empty(R + 2 * NL, dtype=torch.float32, device=device)
+    v_out, ll_out, lp_out = out[:R], out[R : R + NL], out[R + NL :]
+    stream = torch.cuda.current_stream(device)
+    L = dims.num_layers
+    n_ev = int(model._lib.imba_profile_event_count(model._handle))
+
+    import ctypes
+
+    def make_events():
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+        for e in evs:
+            e.record(stream)  # creates the handle
+        arr = (ctypes.c_void_p * n_ev)(*[e.cuda_event for e in evs])
+        return evs, arr
+
+    def step_profiled(arr):
+        desc = dstep.desc
+        desc.value_stm = v_out.data_ptr()
+        desc.legal_logits = ll_out.data_ptr()
+        desc.legal_logprob = lp_out.data_ptr()
+        desc.logits = None
+        desc.value_logits = None
+        desc.hidden = None
+        desc.status = model._status.data_ptr()
+        ws = model.workspace(R)
+        code = model._lib.imba_step_profiled(model._handle, ctypes.byref(desc), ctypes.byref(pool.desc),
+                                             ws.data_ptr(), ws.numel(), stream.cuda_stream, arr, n_ev)
+        _native.check(code, "imba_step_profiled")
+
+    def step_plain():
+        model.run(dstep, pool, value_stm=v_out, legal_logits=ll_out, legal_logprob=lp_out)
+
+    for _ in range(args.warmup):
+        step_plain()
+    torch.cuda.synchronize()
+    model.check_status()
+    ev_sets = [make_events() for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        step_profiled(ev_sets[i][1])
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler.stop()
+    model.check_status()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    if world > 1:
+        tmax = torch.tensor([elapsed_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(tmax.item())
+    ms_per_step = elapsed_ms / args.steps
+    value = R * args.steps * world / (elapsed_ms / 1000.0)
+
+    # Per-phase device times (averaged over the timed steps).
+    acc = {p: 0.0 for p in PHASES}
+    for evs, _ in ev_sets:
+        for k, v in phase_times(evs, L).items():
+            acc[k] += v
+    per_step = {k: v / args.steps for k, v in acc.items()}
+    work = algorithmic_work(dims, plan)
+    peaks, peak_src = load_peaks()
+    traffic = read_traffic()
+    kernels = {}
+    t_roof_ms = 0.0
+    for k, (bound, amount, launches) in work.items():
+        ms_launch = per_step[k] / launches
+        if bound == "tensor":
+            ach = amount / (ms_launch / 1000.0) / 1e12
+            peak = peaks["bf16_tflops_sustained"]
+            unit = "TFLOP/s"
+            t_roof_ms += launches * amount / (peak * 1e12) * 1000.0
+        else:
+            ach = amount / (ms_launch / 1000.0) / 1e9
+            peak = peaks["hbm_gbs"]
+            unit = "GB/s"
+            t_roof_ms += launches * amount / (peak * 1e9) * 1000.0
+        kernels[k] = {"bound": bound, "ms_per_step": round(per_step[k], 4), "launches_per_step": launches,
+                      "achieved": round(ach, 2), "unit": unit, "frac": round(ach / peak, 4)}
+    dom = max(per_step, key=per_step.get)
+    dk = kernels[dom]
+    bound, amount, launches = work[dom]
+    roofline = {
+        "kernel": dom,
+        "bound": "tensor" if bound == "tensor" else "hbm",
+        "achieved": dk["achieved"],
+        "peak": peaks["bf16_tflops_sustained"] if bound == "tensor" else peaks["hbm_gbs"],
+        "unit": dk["unit"],
+        "frac": dk["frac"],
+        "traffic": (traffic[dom] * R) if dom in traffic else None,
+        "peak_source": f"{peak_src} (MEASURED_PEAKS.json: bf16 sustained / HBM copy)",
+        "per_launch_work": amount,
+        "step_roof_ms": round(t_roof_ms, 4),
+        "step_frac": round(t_roof_ms / ms_per_step, 4),
+    }
+
+    # End-to-end through the C ABI with host buffers, synchronised per wave.
+    host_out = torch.empty(R + 2 * NL, dtype=torch.float32, pin_memory=True)
+    lat = []
+    e2e_start = torch.cuda.Event(enable_timing=True)
+    e2e_end = torch.cuda.Event(enable_timing=True)
+    for i in range(args.warmup + args.steps):
+        if i == args.warmup:
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            e2e_start.record(stream)
+        t0 = time.perf_counter()
+        dstep.buf.copy_(dstep.host, non_blocking=True)
+        step_plain()
+        host_out.copy_(out, non_blocking=True)
+        stream.synchronize()
+        if i >= args.warmup:
+            lat.append(time.perf_counter() - t0)
+    e2e_end.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e2e_start.elapsed_time(e2e_end)
+    if world > 1:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {
+        "value": R * args.steps * world / (e2e_ms / 1000.0),
+        "unit": UNIT,
+        "h2d_bytes_per_step": int(dstep.h2d_bytes),
+        "d2h_bytes_per_step": int(host_out.numel() * 4),
+        "p50_wave_latency_ms": round(1000.0 * statistics.median(lat), 3),
+    }
+
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": workload_config(args) | {"rows_per_step": R, "parallelism": f"dp{world} (independent games)"},
+        "e2e": e2e,
+        "roofline": roofline,
+        "kernels": kernels,
+        "clocks": sampler.summary(),
+        "gpu_launches": int(args.steps * count_launches(dims, plan)),
+    }
+
+    if rank == 0 and world == 1 and not args.no_service:
+        line["service_api"] = service_api(args, dims, wave, sd, device)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        n_rows, times = cpu_oracle_rate(dims, wave, args.cpu_sample_parents, args.cpu_seconds)
+        line["cpu_baseline"] = {
+            "value": n_rows * len(times) / sum(times),
+            "unit": UNIT,
+            "cores": os.cpu_count() or 1,
+            "kind": "port",
+            "sample": f"{args.cpu_sample_parents} parents ({n_rows} sibling rows) x {len(times)} repetitions, "
+                      "numpy oracle fp32",
+        }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def count_launches(dims, plan):
+    """Kernel launches of one step: embed, L x (LN, uvqk, attention, gate,
+    out), final LN, policy, value GEMM, value/legal."""
+    return 1 + 5 * dims.num_layers + 4
+
+
+def service_api(args, dims, wave, sd, device):
+    """Reference-compatible ActorInferenceServer.service() on the same wave:
+    one WaveRequest per parent, Python wire objects in and out."""
+    import torch
+
+    from imba_chess_b200.model import B200HSTUChessModel
+    from imba_chess_b200.protocol import RootEvalRequest, WaveRequest, WaveRow
+    from imba_chess_b200.server import ActorInferenceServer
+
+    model = B200HSTUChessModel(sd, dtype=torch.bfloat16, device=device)
+    B = wave.num_rows
+    reps = 5
+    pages = sum(-(-n // 16) for n in wave.prefix_lens) + (reps + 2) * (-(-B // 16)) + 2 * len(wave.prefix_lens) + 64
+    server = ActorInferenceServer(model=model, device=device, dtype=torch.bfloat16, kv_pool_pages=pages)
+    roots = []
+    for g, pt in enumerate(wave.prefix_tokens):
+        T = int(pt["piece_ids"].shape[0])
+        ba = {k: v.tolist() for k, v in pt.items()}
+        ba.update(total_tokens=T, seq_offsets=[0, T])
+        roots.append(RootEvalRequest(worker_id=g, turn_id=0, legal_vocab_ids=[2], batch_arrays=ba))
+    server.service(roots)
+    keys = ("turn_id", "castle_id", "ep_file_id", "halfmove_bucket_id", "fullmove_bucket_id")
+    reqs = []
+    rt = wave.row_tokens
+    for g in range(len(wave.prefix_tokens)):
+        rows = []
+        for i in np.nonzero(wave.group_index == g)[0]:
+            bs = {"piece_ids": rt["piece_ids"][i].tolist(), **{k: int(rt[k][i]) for k in keys}}
+            rows.append(WaveRow(node_id=int(i), parent_id=None, prev_move_vocab_id=int(rt["prev_move_id"][i]),
+                                board_state=bs, legal_vocab_ids=wave.legal_ids[i].tolist()))
+        reqs.append(WaveRequest(worker_id=g, turn_id=0, rows=rows))
+    server.service(reqs)  # warm-up
+    lat = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        server.service(reqs)
+        lat.append(time.perf_counter() - t0)
+    p50 = statistics.median(lat)
+    return {"value": B / p50, "unit": UNIT, "p50_wave_latency_ms": round(1000 * p50, 3), "calls": reps,
+            "stats_wave_build_s": round(server.stats["wave_build_s"], 4),
+            "stats_wave_gpu_s": round(server.stats["wave_gpu_s"], 4),
+            "stats_wave_post_s": round(server.stats["wave_post_s"], 4)}
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()
