@@ -36,6 +36,7 @@ DTYPE_F32 = 0
 DTYPE_BF16 = 1
 MAX_LAYERS = 32
 PAGE_TOKENS = 16
+NOALLOC_SCRATCH_BYTES = 8 << 20
 CHUNK_ROWS = 64
 BOARD_BLOCK_FLOATS = 64 + 64 + 192 * 64 + 64 * 64 + 64 + 64 + 128 * 64 + 128 + 64 * 128 + 64
 BOARD_PARAM_FLOATS = 2 * BOARD_BLOCK_FLOATS + 128
@@ -48,6 +49,7 @@ EXPORTED_SYMBOLS = (
     "imba_model_destroy",
     "imba_step_workspace_bytes",
     "imba_step",
+    "imba_step_noalloc",
     "imba_profile_event_count",
     "imba_step_profiled",
     "imba_kv_scatter",
@@ -183,6 +185,8 @@ def load() -> ctypes.CDLL:
         lib.imba_step_workspace_bytes.restype = ctypes.c_size_t
         lib.imba_step.argtypes = [_P, ctypes.POINTER(StepDesc), ctypes.POINTER(PoolDesc), _P, ctypes.c_size_t, _P]
         lib.imba_step.restype = _I32
+        lib.imba_step_noalloc.argtypes = [_P, ctypes.POINTER(StepDesc), ctypes.POINTER(PoolDesc), _P]
+        lib.imba_step_noalloc.restype = _I32
         lib.imba_profile_event_count.argtypes = [_P]
         lib.imba_profile_event_count.restype = _I32
         lib.imba_step_profiled.argtypes = [_P, ctypes.POINTER(StepDesc), ctypes.POINTER(PoolDesc), _P,

@@ -199,6 +199,21 @@ IMBA_API imba_status_t imba_step(const imba_model* model, const imba_step_desc* 
                         const imba_pool_desc* pool, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/* Allocation-free step.  No counterpart in the reference: it exists for hosts
+ * that may not allocate GPU memory at decode time (a runtime whose allocator
+ * owns all device memory, or an engine driver with a fixed footprint) and so
+ * cannot supply imba_step's workspace.  It runs imba_step on a scratch array
+ * of IMBA_NOALLOC_SCRATCH_BYTES compiled into the library (held on every GPU
+ * that loads the library until exit) and calls no allocator.  Returns
+ * IMBA_ERR_OOM, launching nothing, when imba_step_workspace_bytes(model,
+ * step->num_rows) exceeds that size.  The first call on a device looks up the
+ * array's device address and must come before any stream capture.  All calls
+ * share the array: calls that overlap on the GPU race and must be serialised
+ * by the caller. */
+#define IMBA_NOALLOC_SCRATCH_BYTES (8u << 20)
+IMBA_API imba_status_t imba_step_noalloc(const imba_model* model, const imba_step_desc* step,
+                                         const imba_pool_desc* pool, void* stream);
+
 /* Per-phase timing.  imba_step_profiled is imba_step that additionally
  * records caller-created CUDA events (cudaEvent_t handles) on `stream` at
  * every phase boundary, in this order:
