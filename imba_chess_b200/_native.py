@@ -103,7 +103,6 @@ class ModelDesc(ctypes.Structure):
         ("final_norm_w", _P),
         ("final_norm_b", _P),
         ("policy_w", _P),
-        ("policy_w_lo", _P),
         ("policy_w32", _P),
         ("value0_w", _P),
         ("value0_b", _P),

@@ -4,6 +4,7 @@
 // Mirrors HSTUChessModel.forward_decode_grouped / forward
 // (src/imba_chess/model/hstu_model.py:337-374, :651-752).
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 
@@ -39,10 +40,10 @@ size_t workspace_layout(const imba_model* m, int32_t rows, void* base, Workspace
   w.attn = static_cast<float*>(take(R * hdv * 4));
   w.gated = take(R * hdv * eb);
   w.xf32 = static_cast<float*>(take(R * d.model_dim * 4));
-  w.xf = take(R * d.model_dim * eb);
-  w.xf_lo = take(R * d.model_dim * eb);
+  w.xf3 = take(d.dtype == IMBA_DTYPE_BF16 ? R * 3 * d.model_dim * 2 : 0);
   w.hval = static_cast<float*>(take(R * (d.model_dim / 2 + 1) * 4));
   w.logits = static_cast<float*>(take(R * d.vocab * 4));
+  w.pooled = static_cast<float*>(take(d.dtype == IMBA_DTYPE_BF16 ? R * IMBA_BOARD_DIM * 4 : 0));
   w.bytes = off;
   if (ws) *ws = w;
   return off;
@@ -67,7 +68,6 @@ imba_status_t validate_desc(const imba_model_desc* d) {
   for (int l = 0; l < d->num_layers; ++l)
     if (!d->uvqk_w[l] || !d->o_w[l] || !d->o_b[l] || !d->ps_w[l]) return IMBA_ERR_ARG;
   if (d->has_value_head && (!d->value0_w || !d->value0_b || !d->value2_w || !d->value2_b)) return IMBA_ERR_ARG;
-  if (d->dtype == IMBA_DTYPE_BF16 && !d->policy_w_lo) return IMBA_ERR_ARG;
   return IMBA_OK;
 }
 
@@ -121,7 +121,17 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
   } while (0)
 
   IMBA_CK(pm.mark(s));
-  IMBA_CK(launch_embed(md, st, w.x, s));
+  if (md.dtype == IMBA_DTYPE_BF16 && !m->simt_board) {
+    // tensor-core board encoder -> pooled [R, 64]; projection + embeddings in the GEMM epilogue
+    IMBA_CK(launch_board_mma(md, st, w.pooled, s));
+    EpiContent ec{w.x, nullptr, md.board_out_b, md.emb_seq, md.emb_turn, md.emb_castle, md.emb_ep, md.emb_halfmove,
+                  md.emb_fullmove, md.emb_prev_move, md.emb_pos, st.side_ids, st.positions, d, md.halfmove_vocab,
+                  md.fullmove_vocab, md.vocab, md.max_pos, sqrtf((float)d), st.status};
+    IMBA_CK(launch_gemm_simt<float, float, EpiContent>(w.pooled, IMBA_BOARD_DIM, md.board_out_w, IMBA_BOARD_DIM, R, d,
+                                                       IMBA_BOARD_DIM, ec, s));
+  } else {
+    IMBA_CK(launch_embed(md, st, w.x, s));
+  }
   IMBA_CK(pm.mark(s));
   for (int l = 0; l < md.num_layers; ++l) {
     IMBA_CK(launch_ln_rows<T>(w.x, R, d, 1e-6f, static_cast<T*>(w.xn), s));
@@ -135,12 +145,16 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
     }
     IMBA_CK(pm.mark(s));
     AttnArgs aa{w.q, pool.base, g, l, md.ps_w[l], md.max_pos, 1.0f / sqrtf((float)md.attention_dim), st, w.attn};
-    IMBA_CK(launch_attn_simt<T>(aa, s));
+    if (m->simt_attn || !launch_attn_mma(aa, md.num_layers, md, pool.num_pages, s, &e)) {
+      IMBA_CK(launch_attn_simt<T>(aa, s));
+    } else if (e != cudaSuccess) {
+      return IMBA_ERR_CUDA;
+    }
     IMBA_CK(pm.mark(s));
     IMBA_CK(launch_gate<T>(w.attn, w.u, R, hdv, static_cast<T*>(w.gated), s));
     IMBA_CK(pm.mark(s));
     EpiResidual er{w.x, md.o_b[l], d};
-    if (!gemm_tc_launch_out(m, l, R, static_cast<const T*>(w.gated), er, s, &e)) {
+    if (!gemm_tc_launch_out(m, l, R, static_cast<const T*>(w.gated), er, st.status, s, &e)) {
       IMBA_CK(launch_gemm_simt<T, T, EpiResidual>(static_cast<const T*>(w.gated), hdv,
                                                   static_cast<const T*>(md.o_w[l]), hdv, R, d, hdv, er, s));
     } else if (e != cudaSuccess) {
@@ -149,14 +163,14 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
     IMBA_CK(pm.mark(s));
   }
   const bool bf = md.dtype == IMBA_DTYPE_BF16;
-  IMBA_CK(launch_final_ln<T>(w.x, R, d, md.final_norm_w, md.final_norm_b, w.xf32, bf ? static_cast<T*>(w.xf) : nullptr,
-                             bf ? static_cast<T*>(w.xf_lo) : nullptr, s));
+  IMBA_CK(launch_final_ln<T>(w.x, R, d, md.final_norm_w, md.final_norm_b, w.xf32,
+                             bf ? static_cast<T*>(w.xf3) : nullptr, s));
   IMBA_CK(pm.mark(s));
   if (st.hidden) IMBA_CK(cudaMemcpyAsync(st.hidden, w.x, (size_t)R * d * 4, cudaMemcpyDeviceToDevice, s));
   float* logits = st.logits ? st.logits : w.logits;
   const bool need_logits = st.logits || st.legal_off;
   if (need_logits) {
-    if (!gemm_tc_launch_policy(m, R, static_cast<const T*>(w.xf), static_cast<const T*>(w.xf_lo), logits, s, &e)) {
+    if (!gemm_tc_launch_policy(m, R, static_cast<const T*>(w.xf3), EpiStore{logits, md.vocab}, st.status, s, &e)) {
       IMBA_CK(launch_gemm_simt<float, float, EpiStore>(w.xf32, d, md.policy_w32, d, R, md.vocab, d,
                                                        EpiStore{logits, md.vocab}, s));
     } else if (e != cudaSuccess) {
@@ -167,8 +181,14 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
   if (md.has_value_head) {
     const int hd = d / 2;
     EpiBiasSilu eb{w.hval, md.value0_b, hd};
-    const T* xin = bf ? static_cast<const T*>(w.xf) : reinterpret_cast<const T*>(w.xf32);
-    IMBA_CK(launch_gemm_simt<T, T, EpiBiasSilu>(xin, d, static_cast<const T*>(md.value0_w), d, R, hd, d, eb, s));
+    // bf16: the first d columns of [x_hi | x_lo | x_hi]; fp32: the fp32 final-LN output.
+    const T* xin = bf ? static_cast<const T*>(w.xf3) : reinterpret_cast<const T*>(w.xf32);
+    const int lda = bf ? 3 * d : d;
+    if (!gemm_tc_launch_value(m, R, xin, lda, eb, st.status, s, &e)) {
+      IMBA_CK(launch_gemm_simt<T, T, EpiBiasSilu>(xin, lda, static_cast<const T*>(md.value0_w), d, R, hd, d, eb, s));
+    } else if (e != cudaSuccess) {
+      return IMBA_ERR_CUDA;
+    }
   }
   IMBA_CK(pm.mark(s));
   IMBA_CK(launch_value_legal(md, st, w.hval, logits, s));
@@ -209,6 +229,10 @@ imba_status_t imba_model_create(const imba_model_desc* desc, imba_model** out) {
   if (!m) return IMBA_ERR_OOM;
   m->d = *desc;
   m->uvqk_n = 2 * desc->num_heads * (desc->linear_dim + desc->attention_dim);
+  if (const char* sel = getenv("IMBA_SIMT")) {
+    m->simt_attn = strstr(sel, "attn") != nullptr;
+    m->simt_board = strstr(sel, "board") != nullptr;
+  }
   const imba_status_t t = imba::gemm_tc_prepare(m);
   if (t != IMBA_OK) {
     delete m;
@@ -218,7 +242,11 @@ imba_status_t imba_model_create(const imba_model_desc* desc, imba_model** out) {
   return IMBA_OK;
 }
 
-void imba_model_destroy(imba_model* model) { delete model; }
+void imba_model_destroy(imba_model* model) {
+  if (!model) return;
+  imba::gemm_tc_release(model);
+  delete model;
+}
 
 size_t imba_step_workspace_bytes(const imba_model* model, int32_t max_rows) {
   if (!model || max_rows < 0) return 0;

@@ -71,7 +71,12 @@ struct PoolGeom {
 // The opaque handle behind imba_model*.
 struct imba_model {
   imba_model_desc d;
-  int uvqk_n;  // 2 H (d_v + d_qk)
+  int uvqk_n;         // 2 H (d_v + d_qk)
+  void* tc = nullptr;  // tensor-core GEMM state (TMA descriptors of the weights), or null
+  // Kernel selection for bf16 models (IMBA_SIMT=gemm,attn,board at handle
+  // creation selects the SIMT kernel of a component, for cross-checking).
+  bool simt_attn = false;
+  bool simt_board = false;
   imba::PoolGeom geom(int64_t num_pages) const {
     imba::PoolGeom g;
     g.H = d.num_heads;
@@ -96,10 +101,10 @@ struct Workspace {
   float* attn;     // [R, H dv]   attention output
   void* gated;     // [R, H dv]   LN(attn) * u, model dtype
   float* xf32;     // [R, d]      final LN output, fp32
-  void* xf;        // [R, d]      final LN output, model dtype (hi part in bf16)
-  void* xf_lo;     // [R, d]      bf16 only: fp32 - hi residual
+  void* xf3;       // [R, 3d]     bf16 only: final LN output as [hi | lo | hi]
   float* hval;     // [R, d/2]    value-head hidden
   float* logits;   // [R, vocab]  used when the caller passes no logits buffer
+  float* pooled;   // [R, 64]     bf16 models: mean-pooled board-encoder output
   size_t bytes;
 };
 

@@ -72,7 +72,8 @@ struct EpiUVQK {
 
   // 32 consecutive columns starting at c0 (a multiple of 32; d_qk and d_v
   // are multiples of 32, so a chunk never straddles a head or a region).
-  __device__ __forceinline__ void chunk32(int r, int c0, int /*N*/, const float (&a)[32]) const {
+  __device__ __forceinline__ void chunk32(int r, int c0, int N, const float (&a)[32]) const {
+    if (c0 >= N) return;
     float y[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) y[i] = silu_f(a[i]);
@@ -109,20 +110,28 @@ struct EpiResidual {
     float* p = x + (size_t)r * ld + c;
     *p = (acc + bias[c]) + *p;
   }
+  // All loads are issued before any store: interleaving each load after the
+  // previous store of the same row serialises them (the compiler cannot prove
+  // x and bias do not alias) and was measured ~30x slower.
   __device__ __forceinline__ void chunk32(int r, int c0, int N, const float (&a)[32]) const {
     if (c0 >= N) return;
     float4* p = reinterpret_cast<float4*>(x + (size_t)r * ld + c0);
     const float4* b = reinterpret_cast<const float4*>(bias + c0);
+    float4 xv[8], bv[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      float4 xv = p[i];
-      const float4 bv = b[i];
-      xv.x = (a[4 * i] + bv.x) + xv.x;
-      xv.y = (a[4 * i + 1] + bv.y) + xv.y;
-      xv.z = (a[4 * i + 2] + bv.z) + xv.z;
-      xv.w = (a[4 * i + 3] + bv.w) + xv.w;
-      p[i] = xv;
+      xv[i] = p[i];
+      bv[i] = __ldg(b + i);
     }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      xv[i].x = (a[4 * i] + bv[i].x) + xv[i].x;
+      xv[i].y = (a[4 * i + 1] + bv[i].y) + xv[i].y;
+      xv[i].z = (a[4 * i + 2] + bv[i].z) + xv[i].z;
+      xv[i].w = (a[4 * i + 3] + bv[i].w) + xv[i].w;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) p[i] = xv[i];
   }
 };
 
@@ -130,12 +139,19 @@ struct EpiStore {
   float* out;
   int ld;
   __device__ __forceinline__ void operator()(int r, int c, float acc) const { out[(size_t)r * ld + c] = acc; }
-  // Scalar stores: the policy row stride (vocab floats) is not 16-byte aligned.
+  // The policy row stride (vocab floats) is even but not a multiple of 4:
+  // full chunks use 8-byte stores, the ragged last chunk scalar stores.
   __device__ __forceinline__ void chunk32(int r, int c0, int N, const float (&a)[32]) const {
-    float* o = out + (size_t)r * ld;
+    float* o = out + (size_t)r * ld + c0;
+    if (c0 + 32 <= N && ((reinterpret_cast<uintptr_t>(o) & 7) == 0)) {
+      float2* o2 = reinterpret_cast<float2*>(o);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) o2[i] = make_float2(a[2 * i], a[2 * i + 1]);
+      return;
+    }
 #pragma unroll
     for (int i = 0; i < 32; ++i)
-      if (c0 + i < N) o[c0 + i] = a[i];
+      if (c0 + i < N) o[i] = a[i];
   }
 };
 
@@ -157,9 +173,53 @@ struct EpiBiasSilu {
   __device__ __forceinline__ void chunk32(int r, int c0, int N, const float (&a)[32]) const {
     if (c0 >= N) return;
     float y[32];
+    const float4* b = reinterpret_cast<const float4*>(bias + c0);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) y[i] = silu_f(a[i] + bias[c0 + i]);
+    for (int i = 0; i < 8; ++i) {
+      const float4 bv = __ldg(b + i);
+      y[4 * i] = silu_f(a[4 * i] + bv.x);
+      y[4 * i + 1] = silu_f(a[4 * i + 1] + bv.y);
+      y[4 * i + 2] = silu_f(a[4 * i + 2] + bv.z);
+      y[4 * i + 3] = silu_f(a[4 * i + 3] + bv.w);
+    }
     store32(out + (size_t)r * ld + c0, y);
+  }
+};
+
+// Content embedding epilogue (bf16 models): acc = pooled . board_out^T, then
+// x = (acc + b_out + seq + turn + castle + ep + halfmove + fullmove + prev_move)
+//     * sqrt(d) + pos_emb[min(pos, max_pos - 1)]
+// with side ids clamped to their tables (hstu_model.py:275-335;
+// position_embedding.py:52-62).
+struct EpiContent {
+  float* x;
+  const imba_model_desc* md;  // device copy not needed: pointers and sizes only
+  const float* bias;
+  const float *seq, *turn, *castle, *ep, *half, *full, *prev, *pos_emb;
+  const int32_t* side_ids;
+  const int32_t* positions;
+  int d, halfmove_vocab, fullmove_vocab, vocab, max_pos;
+  float scale;
+  int32_t* status;
+
+  __device__ __forceinline__ static int clampi(int v, int n) { return v < 0 ? 0 : (v >= n ? n - 1 : v); }
+  __device__ __forceinline__ void operator()(int r, int c, float acc) const {
+    const int32_t* ids = side_ids + (size_t)r * IMBA_NUM_SIDE_IDS;
+    float v = acc + bias[c];
+    v += seq[(size_t)clampi(ids[0], 2) * d + c];
+    v += turn[(size_t)clampi(ids[1], 2) * d + c];
+    v += castle[(size_t)clampi(ids[2], 16) * d + c];
+    v += ep[(size_t)clampi(ids[3], 9) * d + c];
+    v += half[(size_t)clampi(ids[4], halfmove_vocab) * d + c];
+    v += full[(size_t)clampi(ids[5], fullmove_vocab) * d + c];
+    v += prev[(size_t)clampi(ids[6], vocab) * d + c];
+    int p = positions[r];
+    if (p < 0) {
+      report(status, IMBA_ERR_RANGE);
+      p = 0;
+    }
+    if (p > max_pos - 1) p = max_pos - 1;
+    x[(size_t)r * d + c] = v * scale + pos_emb[(size_t)p * d + c];
   }
 };
 

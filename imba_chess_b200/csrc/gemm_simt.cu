@@ -80,6 +80,7 @@ IMBA_INST(bf16, bf16, EpiResidual)
 IMBA_INST(float, float, EpiStore)
 IMBA_INST(float, float, EpiBiasSilu)
 IMBA_INST(bf16, bf16, EpiBiasSilu)
+IMBA_INST(float, float, EpiContent)
 #undef IMBA_INST
 
 }  // namespace imba

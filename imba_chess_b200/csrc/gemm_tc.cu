@@ -1,28 +1,288 @@
-// Placeholder until the tcgen05 kernel lands: no shape is handled here, so
-// every GEMM takes the SIMT path.
+// bf16 tensor-core GEMM for sm_100a: acc[M, N] = A[M, K] . W[N, K]^T with a
+// fused epilogue, on the 5th-generation tensor cores.
+//
+// One CTA computes a 128 x BN output tile.  Both operands are K-major; TMA
+// copies 128 x 64 (A) and BN x 64 (W) bf16 tiles into shared memory with the
+// 128-byte swizzle, a STAGES-deep ring guarded by full / empty mbarriers.
+// Warp 0 (one thread) issues the TMA copies, warp 1 (one thread) issues
+// tcgen05.mma (M = 128, N = BN, K = 16 per instruction) into a TMEM
+// accumulator and releases each stage with tcgen05.commit; then all four
+// warps read the accumulator back (warp w owns TMEM lanes 32w..32w+31 = tile
+// rows) and hand 32-column chunks to the epilogue functor.  Out-of-range rows
+// and columns of A / W are zero-filled by TMA and skipped by the epilogue.
+//
+// Used for the STU projections (uvqk with SiLU + KV append; output projection
+// with bias + residual), the split-precision policy GEMM and the value-head
+// hidden layer (hstu_attention.py:307-325, :415-424; hstu_model.py:745-751).
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <new>
+
 #include "gemm_tc.cuh"
+#include "tc_ptx.cuh"
 
 namespace imba {
+namespace {
 
-imba_status_t gemm_tc_prepare(imba_model*) { return IMBA_OK; }
+constexpr int kBM = 128;
+constexpr int kBK = 64;
 
-template <typename T>
-bool gemm_tc_launch_uvqk(const imba_model*, int, int, const T*, const EpiUVQK<T>&, cudaStream_t, cudaError_t*) {
+template <int BN, int STAGES>
+struct TileShape {
+  static constexpr uint32_t kABytes = kBM * kBK * 2;
+  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr size_t kSmem = 1024 + STAGES * (kABytes + kBBytes) + (2 * STAGES + 1) * 8 + 16;
+};
+
+template <int BN, int STAGES, class Epi>
+__global__ void __launch_bounds__(128, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                   int K, Epi epi, int32_t* status) {
+  using S = TileShape<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * S::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * S::kBBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accum = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
+  const int KB = K / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    tc::mbar_init(accum, 1);
+    tc::fence_mbar_init();
+    tc::prefetch_tmap(&tmA);
+    tc::prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, BN);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // TMA producer.
+    for (int kb = 0; kb < KB; ++kb) {
+      const int s = kb % STAGES;
+      if (kb >= STAGES && !tc::mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1, status)) break;
+      tc::mbar_arrive_expect_tx(&full[s], S::kABytes + S::kBBytes);
+      tc::tma_load_2d(sA + s * S::kABytes, &tmA, &full[s], kb * kBK, m0);
+      tc::tma_load_2d(sB + s * S::kBBytes, &tmB, &full[s], kb * kBK, n0);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer.
+    constexpr uint32_t idesc = tc::idesc_bf16_f32(kBM, BN);
+    for (int kb = 0; kb < KB; ++kb) {
+      const int s = kb % STAGES;
+      if (!tc::mbar_wait(&full[s], (kb / STAGES) & 1, status)) break;
+      tc::fence_after_sync();
+      const uint64_t ad = tc::smem_desc_k128(sA + s * S::kABytes);
+      const uint64_t bd = tc::smem_desc_k128(sB + s * S::kBBytes);
+#pragma unroll
+      for (int k = 0; k < kBK / 16; ++k) tc::umma_f16(tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+      tc::umma_commit(&empty[s]);
+    }
+    // Signals once every MMA issued above has completed (also after an early exit).
+    tc::umma_commit(accum);
+  }
+  __syncwarp();
+
+  // Epilogue: TMEM -> registers -> functor.
+  bool ok = tc::mbar_wait(accum, 0, status);
+  ok = __all_sync(0xffffffffu, ok);
+  tc::fence_after_sync();
+  if (ok) {
+    const int row = m0 + warp * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      float v[32];
+      tc::tmem_ld32(tmem + lane_base + c, v);
+      if (row < M && n0 + c < N) epi.chunk32(row, n0 + c, N, v);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) tc::tmem_dealloc(tmem, BN);
+}
+
+// ---------------------------------------------------------------------------
+// Host side: TMA descriptors.
+// ---------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// K-major bf16 operand [rows, cols] with the given row stride; 64 x box_rows
+// boxes, 128-byte swizzle, zero fill out of range.
+bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_stride_bytes,
+              uint32_t box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc || !base || rows == 0 || cols == 0) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_stride_bytes & 15)) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {row_stride_bytes};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+constexpr int kBNWide = 256;
+constexpr int kBNNarrow = 128;
+constexpr int kStages = 4;
+
+struct TCState {
+  CUtensorMap uvqk[IMBA_MAX_LAYERS];
+  CUtensorMap o[IMBA_MAX_LAYERS];
+  CUtensorMap policy;
+  CUtensorMap value;
+  bool has_value = false;
+};
+
+template <int BN, class Epi>
+cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const Epi& epi, int32_t* status,
+                   cudaStream_t s) {
+  using S = TileShape<BN, kStages>;
+  auto kern = gemm_tc_kernel<BN, kStages, Epi>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::kSmem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((M + kBM - 1) / kBM, (N + BN - 1) / BN);
+  kern<<<grid, 128, S::kSmem, s>>>(ta, tb, M, N, K, epi, status);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+imba_status_t gemm_tc_prepare(imba_model* m) {
+  const imba_model_desc& d = m->d;
+  m->tc = nullptr;
+  if (d.dtype != IMBA_DTYPE_BF16) return IMBA_OK;
+  // IMBA_SIMT containing "gemm" selects the SIMT GEMMs for this handle (cross-checking).
+  const char* sel = getenv("IMBA_SIMT");
+  if (sel && strstr(sel, "gemm")) return IMBA_OK;
+  const int hdv = d.num_heads * d.linear_dim;
+  const bool shapes_ok = d.model_dim % 64 == 0 && hdv % 64 == 0 && d.attention_dim % 32 == 0 &&
+                         d.linear_dim % 32 == 0 && m->uvqk_n % kBNWide == 0 && d.model_dim % kBNNarrow == 0 &&
+                         (d.model_dim / 2) % 32 == 0;
+  if (!shapes_ok || !encode_fn()) return IMBA_OK;  // SIMT GEMMs serve this model
+  TCState* t = new (std::nothrow) TCState();
+  if (!t) return IMBA_ERR_OOM;
+  bool ok = true;
+  for (int l = 0; l < d.num_layers && ok; ++l) {
+    ok = make_map(&t->uvqk[l], d.uvqk_w[l], m->uvqk_n, d.model_dim, (uint64_t)d.model_dim * 2, kBNWide) &&
+         make_map(&t->o[l], d.o_w[l], d.model_dim, hdv, (uint64_t)hdv * 2, kBNNarrow);
+  }
+  ok = ok && make_map(&t->policy, d.policy_w, d.vocab, 3 * d.model_dim, (uint64_t)3 * d.model_dim * 2, kBNWide);
+  if (ok && d.has_value_head) {
+    ok = make_map(&t->value, d.value0_w, d.model_dim / 2, d.model_dim, (uint64_t)d.model_dim * 2, kBNNarrow);
+    t->has_value = ok;
+  }
+  if (!ok) {
+    delete t;
+    return IMBA_OK;
+  }
+  m->tc = t;
+  return IMBA_OK;
+}
+
+void gemm_tc_release(imba_model* m) {
+  delete static_cast<TCState*>(m->tc);
+  m->tc = nullptr;
+}
+
+template <>
+bool gemm_tc_launch_uvqk<bf16>(const imba_model* m, int layer, int rows, const bf16* xn, const EpiUVQK<bf16>& epi,
+                               cudaStream_t s, cudaError_t* err) {
+  const TCState* t = static_cast<const TCState*>(m->tc);
+  if (!t || rows <= 0) return false;
+  CUtensorMap ta;
+  if (!make_map(&ta, xn, rows, m->d.model_dim, (uint64_t)m->d.model_dim * 2, kBM)) return false;
+  *err = launch<kBNWide>(ta, t->uvqk[layer], rows, m->uvqk_n, m->d.model_dim, epi, epi.status, s);
+  return true;
+}
+
+template <>
+bool gemm_tc_launch_out<bf16>(const imba_model* m, int layer, int rows, const bf16* gated, const EpiResidual& epi,
+                              int32_t* status, cudaStream_t s, cudaError_t* err) {
+  const TCState* t = static_cast<const TCState*>(m->tc);
+  if (!t || rows <= 0) return false;
+  const int hdv = m->d.num_heads * m->d.linear_dim;
+  CUtensorMap ta;
+  if (!make_map(&ta, gated, rows, hdv, (uint64_t)hdv * 2, kBM)) return false;
+  *err = launch<kBNNarrow>(ta, t->o[layer], rows, m->d.model_dim, hdv, epi, status, s);
+  return true;
+}
+
+template <>
+bool gemm_tc_launch_policy<bf16>(const imba_model* m, int rows, const bf16* xf3, const EpiStore& epi,
+                                 int32_t* status, cudaStream_t s, cudaError_t* err) {
+  const TCState* t = static_cast<const TCState*>(m->tc);
+  if (!t || rows <= 0) return false;
+  const int k3 = 3 * m->d.model_dim;
+  CUtensorMap ta;
+  if (!make_map(&ta, xf3, rows, k3, (uint64_t)k3 * 2, kBM)) return false;
+  *err = launch<kBNWide>(ta, t->policy, rows, m->d.vocab, k3, epi, status, s);
+  return true;
+}
+
+template <>
+bool gemm_tc_launch_value<bf16>(const imba_model* m, int rows, const bf16* xin, int lda, const EpiBiasSilu& epi,
+                                int32_t* status, cudaStream_t s, cudaError_t* err) {
+  const TCState* t = static_cast<const TCState*>(m->tc);
+  if (!t || !t->has_value || rows <= 0) return false;
+  CUtensorMap ta;
+  if (!make_map(&ta, xin, rows, m->d.model_dim, (uint64_t)lda * 2, kBM)) return false;
+  *err = launch<kBNNarrow>(ta, t->value, rows, m->d.model_dim / 2, m->d.model_dim, epi, status, s);
+  return true;
+}
+
+// fp32 models always take the SIMT path.
+template <>
+bool gemm_tc_launch_uvqk<float>(const imba_model*, int, int, const float*, const EpiUVQK<float>&, cudaStream_t,
+                                cudaError_t*) {
   return false;
 }
-template <typename T>
-bool gemm_tc_launch_out(const imba_model*, int, int, const T*, const EpiResidual&, cudaStream_t, cudaError_t*) {
+template <>
+bool gemm_tc_launch_out<float>(const imba_model*, int, int, const float*, const EpiResidual&, int32_t*, cudaStream_t,
+                               cudaError_t*) {
   return false;
 }
-template <typename T>
-bool gemm_tc_launch_policy(const imba_model*, int, const T*, const T*, float*, cudaStream_t, cudaError_t*) {
+template <>
+bool gemm_tc_launch_policy<float>(const imba_model*, int, const float*, const EpiStore&, int32_t*, cudaStream_t,
+                                  cudaError_t*) {
   return false;
 }
-template bool gemm_tc_launch_uvqk<float>(const imba_model*, int, int, const float*, const EpiUVQK<float>&, cudaStream_t, cudaError_t*);
-template bool gemm_tc_launch_uvqk<bf16>(const imba_model*, int, int, const bf16*, const EpiUVQK<bf16>&, cudaStream_t, cudaError_t*);
-template bool gemm_tc_launch_out<float>(const imba_model*, int, int, const float*, const EpiResidual&, cudaStream_t, cudaError_t*);
-template bool gemm_tc_launch_out<bf16>(const imba_model*, int, int, const bf16*, const EpiResidual&, cudaStream_t, cudaError_t*);
-template bool gemm_tc_launch_policy<float>(const imba_model*, int, const float*, const float*, float*, cudaStream_t, cudaError_t*);
-template bool gemm_tc_launch_policy<bf16>(const imba_model*, int, const bf16*, const bf16*, float*, cudaStream_t, cudaError_t*);
+template <>
+bool gemm_tc_launch_value<float>(const imba_model*, int, const float*, int, const EpiBiasSilu&, int32_t*,
+                                 cudaStream_t, cudaError_t*) {
+  return false;
+}
 
 }  // namespace imba

@@ -1,22 +1,29 @@
 // Tensor-core (tcgen05 + TMA) GEMMs of the bf16 step.  Each launcher returns
-// false when it does not handle the model / shape (fp32 models, head dims the
-// tile shapes do not cover); the caller then runs the SIMT GEMM.  When it
-// returns true, *err holds the launch status.
+// false when it does not handle the model / shape (fp32 models, dimensions the
+// tile shapes do not cover, a TMA descriptor that cannot be encoded); the
+// caller then runs the SIMT GEMM.  When it returns true, *err holds the launch
+// status.
 #pragma once
 
 #include "epilogues.cuh"
 
 namespace imba {
 
+// Encodes the weights' TMA descriptors once per model (bf16 models only).
 imba_status_t gemm_tc_prepare(imba_model* m);
+void gemm_tc_release(imba_model* m);
+
 template <typename T>
 bool gemm_tc_launch_uvqk(const imba_model* m, int layer, int rows, const T* xn, const EpiUVQK<T>& epi,
                          cudaStream_t s, cudaError_t* err);
 template <typename T>
 bool gemm_tc_launch_out(const imba_model* m, int layer, int rows, const T* gated, const EpiResidual& epi,
-                        cudaStream_t s, cudaError_t* err);
+                        int32_t* status, cudaStream_t s, cudaError_t* err);
 template <typename T>
-bool gemm_tc_launch_policy(const imba_model* m, int rows, const T* xf_hi, const T* xf_lo, float* logits,
+bool gemm_tc_launch_policy(const imba_model* m, int rows, const T* xf3, const EpiStore& epi, int32_t* status,
                            cudaStream_t s, cudaError_t* err);
+template <typename T>
+bool gemm_tc_launch_value(const imba_model* m, int rows, const T* xin, int lda, const EpiBiasSilu& epi,
+                          int32_t* status, cudaStream_t s, cudaError_t* err);
 
 }  // namespace imba

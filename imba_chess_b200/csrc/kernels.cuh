@@ -18,13 +18,14 @@ struct AttnArgs {
 };
 
 cudaError_t launch_embed(const imba_model_desc& md, const imba_step_desc& st, float* x, cudaStream_t s);
+cudaError_t launch_board_mma(const imba_model_desc& md, const imba_step_desc& st, float* pooled, cudaStream_t s);
 template <typename T>
 cudaError_t launch_ln_rows(const float* x, int rows, int n, float eps, T* out, cudaStream_t s);
 template <typename T>
 cudaError_t launch_gate(const float* attn, const float* u, int rows, int n, T* out, cudaStream_t s);
 template <typename T>
-cudaError_t launch_final_ln(const float* x, int rows, int n, const float* w, const float* b, float* out32, T* outT,
-                            T* outLo, cudaStream_t s);
+cudaError_t launch_final_ln(const float* x, int rows, int n, const float* w, const float* b, float* out32, T* out3,
+                            cudaStream_t s);
 cudaError_t launch_value_legal(const imba_model_desc& md, const imba_step_desc& st, const float* hval,
                                const float* logits, cudaStream_t s);
 template <typename T>
@@ -35,5 +36,8 @@ cudaError_t launch_gemm_simt(const TA* A, int lda, const TW* W, int ldw, int M, 
                              cudaStream_t s);
 template <typename T>
 cudaError_t launch_attn_simt(const AttnArgs& a, cudaStream_t s);
+// Tensor-core attention (bf16, head dims 64); false when it does not apply.
+bool launch_attn_mma(const AttnArgs& a, int num_layers, const imba_model_desc& md, int64_t num_pages,
+                     cudaStream_t s, cudaError_t* err);
 
 }  // namespace imba

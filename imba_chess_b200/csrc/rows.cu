@@ -77,13 +77,12 @@ __global__ void gate_kernel(const float* __restrict__ attn, const float* __restr
   }
 }
 
-// Final affine LayerNorm.  Writes fp32 and the model-dtype copy; for bf16 it
-// also writes the bf16 residual lo = x - float(hi) used by the split-precision
-// policy GEMM.
+// Final affine LayerNorm.  Writes fp32 and, for bf16 models, the split
+// operand [hi | lo | hi] (hi = bf16(y), lo = bf16(y - hi)) of the
+// split-precision policy GEMM; its first n columns are the value head's input.
 template <typename T>
 __global__ void final_ln_kernel(const float* __restrict__ x, int rows, int n, const float* __restrict__ w,
-                                const float* __restrict__ b, float* __restrict__ out32, T* __restrict__ outT,
-                                T* __restrict__ outLo) {
+                                const float* __restrict__ b, float* __restrict__ out32, T* __restrict__ out3) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= rows) return;
   const float* xr = x + (size_t)warp * n;
@@ -111,10 +110,12 @@ __global__ void final_ln_kernel(const float* __restrict__ x, int rows, int n, co
       const float y = (v[i] - mu) * rs * w[c] + b[c];
       const size_t o = (size_t)warp * n + c;
       out32[o] = y;
-      if (outT) {
+      if (out3) {
         const T hi = from_f<T>(y);
-        outT[o] = hi;
-        if (outLo) outLo[o] = from_f<T>(y - to_f(hi));
+        T* r3 = out3 + (size_t)warp * 3 * n;
+        r3[c] = hi;
+        r3[n + c] = from_f<T>(y - to_f(hi));
+        r3[2 * n + c] = hi;
       }
     }
   }
@@ -238,14 +239,14 @@ template cudaError_t launch_gate<float>(const float*, const float*, int, int, fl
 template cudaError_t launch_gate<bf16>(const float*, const float*, int, int, bf16*, cudaStream_t);
 
 template <typename T>
-cudaError_t launch_final_ln(const float* x, int rows, int n, const float* w, const float* b, float* out32, T* outT,
-                            T* outLo, cudaStream_t s) {
-  final_ln_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(x, rows, n, w, b, out32, outT, outLo);
+cudaError_t launch_final_ln(const float* x, int rows, int n, const float* w, const float* b, float* out32, T* out3,
+                            cudaStream_t s) {
+  final_ln_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(x, rows, n, w, b, out32, out3);
   return cudaGetLastError();
 }
 template cudaError_t launch_final_ln<float>(const float*, int, int, const float*, const float*, float*, float*,
-                                            float*, cudaStream_t);
-template cudaError_t launch_final_ln<bf16>(const float*, int, int, const float*, const float*, float*, bf16*, bf16*,
+                                            cudaStream_t);
+template cudaError_t launch_final_ln<bf16>(const float*, int, int, const float*, const float*, float*, bf16*,
                                            cudaStream_t);
 
 cudaError_t launch_value_legal(const imba_model_desc& md, const imba_step_desc& st, const float* hval,

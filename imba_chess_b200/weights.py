@@ -7,8 +7,8 @@ src/imba_chess/model/hstu_model.py:185-273) with the ``module.`` /
 (src/imba_chess/eval/position_evaluator.py:136-145).  Architecture sizes are
 read off the tensor shapes.  All tables stay fp32; the GEMM weights are
 stored in the model dtype, and for bf16 the tied policy matrix is split into
-a bf16 high part and a bf16 residual so the policy GEMM keeps ~16 mantissa
-bits.
+a bf16 high part and a bf16 residual, laid out [hi | hi | lo] along K, so the
+policy GEMM against [x_hi | x_lo | x_hi] keeps ~16 mantissa bits.
 """
 
 from __future__ import annotations
@@ -166,14 +166,13 @@ class PackedWeights:
         self._keep.append(policy)
         desc.policy_w32 = policy.data_ptr()
         if dtype == torch.bfloat16:
-            hi = policy.to(torch.bfloat16).contiguous()
-            lo = (policy - hi.float()).to(torch.bfloat16).contiguous()
-            self._keep += [hi, lo]
-            desc.policy_w = hi.data_ptr()
-            desc.policy_w_lo = lo.data_ptr()
+            hi = policy.to(torch.bfloat16)
+            lo = (policy - hi.float()).to(torch.bfloat16)
+            split = torch.cat([hi, hi, lo], dim=1).contiguous()  # [vocab, 3d]
+            self._keep.append(split)
+            desc.policy_w = split.data_ptr()
         else:
             desc.policy_w = policy.data_ptr()
-            desc.policy_w_lo = None
         if dims.value_head:
             desc.value0_w = wdt(sd["value_head.0.weight"]).data_ptr()
             desc.value0_b = f32("value_head.0.bias").data_ptr()

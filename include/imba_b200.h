@@ -102,8 +102,9 @@ typedef struct imba_model_desc {
   /* heads (hstu_model.py:245-260) */
   const float* final_norm_w;   /* [d] */
   const float* final_norm_b;   /* [d] */
-  const void* policy_w;        /* wdt [vocab, d]; bf16: high half of the split */
-  const void* policy_w_lo;     /* bf16 only: residual (w - hi) in bf16, else NULL */
+  const void* policy_w;        /* fp32: [vocab, d]; bf16: [vocab, 3d] = [hi | hi | lo] where
+                                  hi = bf16(w) and lo = bf16(w - hi), so that one K = 3d GEMM
+                                  against [x_hi | x_lo | x_hi] gives x.w to ~16 mantissa bits */
   const float* policy_w32;     /* [vocab, d] fp32 copy (the exact-precision path) */
   const void* value0_w;        /* wdt [d/2, d]   (NULL when no value head) */
   const float* value0_b;       /* [d/2]                                    */

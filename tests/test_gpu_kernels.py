@@ -1,0 +1,83 @@
+"""GPU: kernel-level cross-checks on identical inputs.
+
+Each tensor-core kernel of the bf16 model against the SIMT kernel of the same
+component (selected with IMBA_SIMT=<component> when the handle is created),
+on a full grouped-decode step: final hidden state, logits, value logits.
+
+* gemm  - tcgen05/TMA GEMMs vs SIMT GEMMs: the same bf16 operands, fp32
+          accumulation (the policy GEMM is exact fp32 in SIMT and split bf16 on
+          the tensor cores);
+* attn  - mma.sync attention with TMA-loaded KV tiles vs the SIMT attention
+          (the tensor-core kernel rounds softmax weights to bf16 for P.V);
+* board - mma.sync board encoder (bf16 operands) vs the fp32 SIMT encoder.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from imba_chess_b200 import synth
+from imba_chess_b200.kvpool import KVSequence
+from imba_chess_b200.model import B200HSTUChessModel
+from imba_chess_b200.plan import DeviceStep, piece_ids_from_tokens, side_ids_from_tokens
+from imba_chess_b200.steps import WaveGroup, root_plan, wave_plan
+
+pytestmark = pytest.mark.gpu
+
+# (hidden relative to its max magnitude, logits abs, value logits abs)
+TOL = {"gemm": (1e-4, 2e-3, 1e-3), "attn": (2e-3, 2e-2, 5e-3), "board": (2e-3, 3e-2, 1e-2)}
+
+
+def _run_wave(model, dims, wave, depth2=True):
+    pool = model.new_pool(4096)
+    seqs = [KVSequence(pool) for _ in wave.prefix_lens]
+    plan0, _ = root_plan(seqs, wave.prefix_tokens)
+    model.run(DeviceStep(plan0, model.device), pool)
+    order = np.argsort(wave.group_index, kind="stable")
+    counts = np.bincount(wave.group_index, minlength=len(seqs))
+    arenas = [KVSequence(pool) for _ in seqs]
+    tok = synth.slice_tokens(wave.row_tokens, order)
+    groups = [WaveGroup(seqs[g], wave.prefix_lens[g], arenas[g], [[]] * int(counts[g])) for g in range(len(seqs))]
+    plan, rows = wave_plan(groups, piece_ids_from_tokens(tok), side_ids_from_tokens(tok),
+                           [wave.legal_ids[i] for i in order])
+    model.run(DeviceStep(plan, model.device), pool)
+    if depth2:  # a second wave whose rows have one-token suffix chains
+        rng = np.random.default_rng(3)
+        tok2 = synth.random_tokens(rng, plan.num_rows, dims)
+        groups2 = [WaveGroup(seqs[g], wave.prefix_lens[g], arenas[g], [[r] for r in rows[g]])
+                   for g in range(len(seqs))]
+        plan, _ = wave_plan(groups2, piece_ids_from_tokens(tok2), side_ids_from_tokens(tok2),
+                            [wave.legal_ids[i] for i in order])
+    R = plan.num_rows
+    out = {
+        "logits": torch.empty((R, dims.vocab), device=model.device),
+        "value_logits": torch.empty((R, 3), device=model.device),
+        "hidden": torch.empty((R, dims.model_dim), device=model.device),
+    }
+    model.run(DeviceStep(plan, model.device), pool, **out)
+    torch.cuda.synchronize()
+    model.check_status()
+    return out
+
+
+@pytest.mark.parametrize("component", ["gemm", "attn", "board"])
+@pytest.mark.parametrize("dims,parents", [(synth.D512, 6), (synth.SMALL, 4), (synth.D256, 5)],
+                         ids=["d512", "d128", "d256"])
+def test_tensor_core_kernel_matches_simt(component, dims, parents, monkeypatch):
+    sd = synth.make_state_dict(dims, 9, profile="reference")
+    plies = (20, 140) if component == "attn" else (20, 45)
+    wave = synth.grouped_wave(dims, n_parents=parents, plies=plies, siblings=(20, 40), seed=99)
+    model_tc = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
+    monkeypatch.setenv("IMBA_SIMT", component)
+    model_simt = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
+    monkeypatch.delenv("IMBA_SIMT")
+    a = _run_wave(model_tc, dims, wave)
+    b = _run_wave(model_simt, dims, wave)
+    th, tl, tv = TOL[component]
+    scale = float(b["hidden"].abs().max())
+    assert torch.isfinite(a["logits"]).all()
+    assert float((a["hidden"] - b["hidden"]).abs().max()) <= th * scale
+    assert float((a["logits"] - b["logits"]).abs().max()) <= tl
+    assert float((a["value_logits"] - b["value_logits"]).abs().max()) <= tv
