@@ -268,10 +268,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         float l0 = 0.f, l1 = 0.f;
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
-          s[n][0] = expf(s[n][0] - m0);
-          s[n][1] = expf(s[n][1] - m0);
-          s[n][2] = expf(s[n][2] - m1);
-          s[n][3] = expf(s[n][3] - m1);
+          s[n][0] = __expf(s[n][0] - m0);
+          s[n][1] = __expf(s[n][1] - m0);
+          s[n][2] = __expf(s[n][2] - m1);
+          s[n][3] = __expf(s[n][3] - m1);
           l0 += s[n][0] + s[n][1];
           l1 += s[n][2] + s[n][3];
         }
@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma16816(oh[0], pa[kc], b[0], b[1]);
           mma16816(oh[1], pa[kc], b[2], b[3]);
         }
-        const float i0 = 1.0f / l0, i1 = 1.0f / l1;
+        const float i0 = __frcp_rn(l0), i1 = __frcp_rn(l1);
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           o[2 * h + j][0] = oh[j][0] * i0;
@@ -320,10 +320,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
           const int c = 64 * half + 8 * n + 2 * t;
-          acc[n][0] = silu_f(acc[n][0] + b1[c]);
-          acc[n][1] = silu_f(acc[n][1] + b1[c + 1]);
-          acc[n][2] = silu_f(acc[n][2] + b1[c]);
-          acc[n][3] = silu_f(acc[n][3] + b1[c + 1]);
+          acc[n][0] = silu_fast(acc[n][0] + b1[c]);
+          acc[n][1] = silu_fast(acc[n][1] + b1[c + 1]);
+          acc[n][2] = silu_fast(acc[n][2] + b1[c]);
+          acc[n][3] = silu_fast(acc[n][3] + b1[c + 1]);
         }
         uint32_t ma[4][4];
         to_afrag(acc, ma);

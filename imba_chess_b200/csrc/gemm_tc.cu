@@ -1,15 +1,17 @@
 // bf16 tensor-core GEMM for sm_100a: acc[M, N] = A[M, K] . W[N, K]^T with a
 // fused epilogue, on the 5th-generation tensor cores.
 //
-// One CTA computes a 128 x BN output tile.  Both operands are K-major; TMA
-// copies 128 x 64 (A) and BN x 64 (W) bf16 tiles into shared memory with the
-// 128-byte swizzle, a STAGES-deep ring guarded by full / empty mbarriers.
-// Warp 0 (one thread) issues the TMA copies, warp 1 (one thread) issues
-// tcgen05.mma (M = 128, N = BN, K = 16 per instruction) into a TMEM
-// accumulator and releases each stage with tcgen05.commit; then all four
-// warps read the accumulator back (warp w owns TMEM lanes 32w..32w+31 = tile
-// rows) and hand 32-column chunks to the epilogue functor.  Out-of-range rows
-// and columns of A / W are zero-filled by TMA and skipped by the epilogue.
+// Output tiles are 128 x BN; both operands are K-major.  A persistent grid (one
+// CTA per SM) walks the tiles; TMA copies 128 x 64 (A) and BN x 64 (W) bf16
+// tiles into shared memory with the 128-byte swizzle through a STAGES-deep
+// ring guarded by full / empty mbarriers.  Warp 0 (one thread) issues the TMA
+// copies, warp 1 (one thread) issues tcgen05.mma (M = 128, N = BN, K = 16 per
+// instruction) into one of two TMEM accumulators and releases each stage with
+// tcgen05.commit; four epilogue warps read the other accumulator back (TMEM
+// lane quadrant = warp % 4 = tile rows) and hand 32-column chunks to the
+// epilogue functor, so tile i's epilogue overlaps tile i + 1's main loop.
+// Out-of-range rows / columns of A / W are zero-filled by TMA and skipped by
+// the epilogue.
 //
 // Used for the STU projections (uvqk with SiLU + KV append; output projection
 // with bias + residual), the split-precision policy GEMM and the value-head
@@ -32,11 +34,19 @@ template <int BN, int STAGES>
 struct TileShape {
   static constexpr uint32_t kABytes = kBM * kBK * 2;
   static constexpr uint32_t kBBytes = BN * kBK * 2;
-  static constexpr size_t kSmem = 1024 + STAGES * (kABytes + kBBytes) + (2 * STAGES + 1) * 8 + 16;
+  static constexpr size_t kSmem = 1024 + STAGES * (kABytes + kBBytes) + (2 * STAGES + 4) * 8 + 16;
 };
 
+constexpr int kEpiWarps = 4;
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;  // producer warp, MMA warp, 4 epilogue warps
+
+// Persistent, warp-specialised: CTA b handles tiles b, b + gridDim.x, ...
+// (tile t -> m-tile t % mt, n-tile t / mt).  Warp 0 streams A / W tiles
+// through the smem ring; warp 1 issues the MMAs of tile i into TMEM buffer
+// i % 2 (2 x BN columns) and signals acc_full; warps 2..5 drain buffer i % 2
+// while tile i + 1 is being loaded and multiplied, then signal acc_empty.
 template <int BN, int STAGES, class Epi>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
                    int K, Epi epi, int32_t* status) {
   using S = TileShape<BN, STAGES>;
@@ -46,25 +56,33 @@ __global__ void __launch_bounds__(128, 1)
   uint8_t* sB = smem + STAGES * S::kABytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * S::kBBytes);
   uint64_t* empty = full + STAGES;
-  uint64_t* accum = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  __shared__ int abort_flag;
+  volatile int* abort = &abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
   const int KB = K / kBK;
+  const int mt = (M + kBM - 1) / kBM, ntl = (N + BN - 1) / BN;
+  const int tiles = mt * ntl;
 
   if (threadIdx.x == 0) {
+    abort_flag = 0;
     for (int s = 0; s < STAGES; ++s) {
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], 1);
     }
-    tc::mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&acc_full[b], 1);
+      tc::mbar_init(&acc_empty[b], kEpiWarps);
+    }
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmA);
     tc::prefetch_tmap(&tmB);
   }
   if (warp == 1) {
-    tc::tmem_alloc(tmem_slot, BN);
+    tc::tmem_alloc(tmem_slot, 2 * BN);
     tc::tmem_relinquish();
   }
   tc::fence_before_sync();
@@ -72,50 +90,73 @@ __global__ void __launch_bounds__(128, 1)
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // TMA producer.
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % STAGES;
-      if (kb >= STAGES && !tc::mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1, status)) break;
-      tc::mbar_arrive_expect_tx(&full[s], S::kABytes + S::kBBytes);
-      tc::tma_load_2d(sA + s * S::kABytes, &tmA, &full[s], kb * kBK, m0);
-      tc::tma_load_2d(sB + s * S::kBBytes, &tmB, &full[s], kb * kBK, n0);
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer
+      int it = 0;
+      for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x) {
+        const int m0 = (tile % mt) * kBM, n0 = (tile / mt) * BN;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (it >= STAGES && !tc::mbar_wait_or_abort(&empty[s], ((it / STAGES) - 1) & 1, status, abort)) break;
+          tc::mbar_arrive_expect_tx(&full[s], S::kABytes + S::kBBytes);
+          tc::tma_load_2d(sA + s * S::kABytes, &tmA, &full[s], kb * kBK, m0);
+          tc::tma_load_2d(sB + s * S::kBBytes, &tmB, &full[s], kb * kBK, n0);
+        }
+      }
     }
-  } else if (warp == 1 && lane == 0) {
-    // MMA issuer.
-    constexpr uint32_t idesc = tc::idesc_bf16_f32(kBM, BN);
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % STAGES;
-      if (!tc::mbar_wait(&full[s], (kb / STAGES) & 1, status)) break;
-      tc::fence_after_sync();
-      const uint64_t ad = tc::smem_desc_k128(sA + s * S::kABytes);
-      const uint64_t bd = tc::smem_desc_k128(sB + s * S::kBBytes);
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      constexpr uint32_t idesc = tc::idesc_bf16_f32(kBM, BN);
+      int it = 0, i = 0;
+      for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x, ++i) {
+        const int b = i & 1;
+        if (i >= 2 && !tc::mbar_wait_or_abort(&acc_empty[b], ((i >> 1) - 1) & 1, status, abort)) break;
+        tc::fence_after_sync();
+        const uint32_t d = tmem + b * BN;
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!tc::mbar_wait_or_abort(&full[s], (it / STAGES) & 1, status, abort)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint64_t ad = tc::smem_desc_k128(sA + s * S::kABytes);
+          const uint64_t bd = tc::smem_desc_k128(sB + s * S::kBBytes);
 #pragma unroll
-      for (int k = 0; k < kBK / 16; ++k) tc::umma_f16(tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
-      tc::umma_commit(&empty[s]);
+          for (int k = 0; k < kBK / 16; ++k) tc::umma_f16(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          tc::umma_commit(&empty[s]);
+        }
+        tc::umma_commit(&acc_full[b]);  // fires once the tile's MMAs (or those issued) complete
+        if (!ok) break;
+      }
     }
-    // Signals once every MMA issued above has completed (also after an early exit).
-    tc::umma_commit(accum);
-  }
-  __syncwarp();
-
-  // Epilogue: TMEM -> registers -> functor.
-  bool ok = tc::mbar_wait(accum, 0, status);
-  ok = __all_sync(0xffffffffu, ok);
-  tc::fence_after_sync();
-  if (ok) {
-    const int row = m0 + warp * 32 + lane;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+  } else {  // epilogue warps
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    int i = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++i) {
+      const int b = i & 1;
+      bool ok = tc::mbar_wait_or_abort(&acc_full[b], (i >> 1) & 1, status, abort);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc::fence_after_sync();
+      const int m0 = (tile % mt) * kBM, n0 = (tile / mt) * BN;
+      const int row = m0 + quad * 32 + lane;
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      float v[32];
-      tc::tmem_ld32(tmem + lane_base + c, v);
-      if (row < M && n0 + c < N) epi.chunk32(row, n0 + c, N, v);
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tc::tmem_ld32(tmem + b * BN + lane_base + c, v);
+        if (row < M && n0 + c < N) epi.chunk32(row, n0 + c, N, v);
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
     }
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 1) tc::tmem_dealloc(tmem, BN);
+  if (warp == 1) tc::tmem_dealloc(tmem, 2 * BN);
 }
 
 // ---------------------------------------------------------------------------
@@ -156,7 +197,6 @@ bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, 
 
 constexpr int kBNWide = 256;
 constexpr int kBNNarrow = 128;
-constexpr int kStages = 4;
 
 struct TCState {
   CUtensorMap uvqk[IMBA_MAX_LAYERS];
@@ -166,15 +206,25 @@ struct TCState {
   bool has_value = false;
 };
 
+int sm_count() {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
 template <int BN, class Epi>
 cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const Epi& epi, int32_t* status,
                    cudaStream_t s) {
-  using S = TileShape<BN, kStages>;
-  auto kern = gemm_tc_kernel<BN, kStages, Epi>;
+  constexpr int kSt = BN == 256 ? 4 : 6;
+  using S = TileShape<BN, kSt>;
+  auto kern = gemm_tc_kernel<BN, kSt, Epi>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::kSmem);
   if (e != cudaSuccess) return e;
-  dim3 grid((M + kBM - 1) / kBM, (N + BN - 1) / BN);
-  kern<<<grid, 128, S::kSmem, s>>>(ta, tb, M, N, K, epi, status);
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  const int sms = sm_count();
+  const int grid = tiles < sms ? tiles : sms;
+  kern<<<grid, kGemmThreads, S::kSmem, s>>>(ta, tb, M, N, K, epi, status);
   return cudaGetLastError();
 }
 

@@ -121,6 +121,116 @@ __global__ void final_ln_kernel(const float* __restrict__ x, int rows, int n, co
   }
 }
 
+// ---- 128-bit variants (row width a multiple of 128, at most 1024) --------
+// Lane l holds columns 128 i + 4 l .. +3 for i < n / 128.
+constexpr int kMaxVec = 8;
+
+__device__ __forceinline__ void store4(float* p, float a, float b, float c, float d) {
+  *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
+}
+__device__ __forceinline__ void store4(bf16* p, float a, float b, float c, float d) {
+  __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+  uint2 u;
+  u.x = *reinterpret_cast<uint32_t*>(&lo);
+  u.y = *reinterpret_cast<uint32_t*>(&hi);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+// mean and 1/sqrt(var + eps) of a row held as float4 chunks.
+__device__ __forceinline__ void row_stats4(const float4 (&v)[kMaxVec], int nv, int n, float eps, float& mu,
+                                           float& rs) {
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i)
+    if (i < nv) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  mu = warp_sum(s) / n;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i)
+    if (i < nv) {
+      const float a = v[i].x - mu, b = v[i].y - mu, c = v[i].z - mu, d = v[i].w - mu;
+      q += (a * a + b * b) + (c * c + d * d);
+    }
+  rs = 1.0f / sqrtf(warp_sum(q) / n + eps);
+}
+
+template <typename TOut>
+__global__ void ln_rows4_kernel(const float* __restrict__ x, int rows, int n, float eps, TOut* __restrict__ out) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const int nv = n >> 7;
+  const float* xr = x + (size_t)warp * n + 4 * lane;
+  float4 v[kMaxVec];
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i)
+    if (i < nv) v[i] = *reinterpret_cast<const float4*>(xr + 128 * i);
+  float mu, rs;
+  row_stats4(v, nv, n, eps, mu, rs);
+  TOut* o = out + (size_t)warp * n + 4 * lane;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i)
+    if (i < nv)
+      store4(o + 128 * i, (v[i].x - mu) * rs, (v[i].y - mu) * rs, (v[i].z - mu) * rs, (v[i].w - mu) * rs);
+}
+
+template <typename TOut>
+__global__ void gate4_kernel(const float* __restrict__ attn, const float* __restrict__ u, int rows, int n,
+                             TOut* __restrict__ out) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const int nv = n >> 7;
+  const float* ar = attn + (size_t)warp * n + 4 * lane;
+  const float* ur = u + (size_t)warp * n + 4 * lane;
+  float4 v[kMaxVec], w[kMaxVec];
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i)
+    if (i < nv) {
+      v[i] = *reinterpret_cast<const float4*>(ar + 128 * i);
+      w[i] = *reinterpret_cast<const float4*>(ur + 128 * i);
+    }
+  float mu, rs;
+  row_stats4(v, nv, n, 1e-6f, mu, rs);
+  TOut* o = out + (size_t)warp * n + 4 * lane;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i)
+    if (i < nv)
+      store4(o + 128 * i, w[i].x * ((v[i].x - mu) * rs), w[i].y * ((v[i].y - mu) * rs),
+             w[i].z * ((v[i].z - mu) * rs), w[i].w * ((v[i].w - mu) * rs));
+}
+
+template <typename T>
+__global__ void final_ln4_kernel(const float* __restrict__ x, int rows, int n, const float* __restrict__ w,
+                                 const float* __restrict__ b, float* __restrict__ out32, T* __restrict__ out3) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const int nv = n >> 7;
+  const float* xr = x + (size_t)warp * n + 4 * lane;
+  float4 v[kMaxVec];
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i)
+    if (i < nv) v[i] = *reinterpret_cast<const float4*>(xr + 128 * i);
+  float mu, rs;
+  row_stats4(v, nv, n, 1e-5f, mu, rs);
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i)
+    if (i < nv) {
+      const int c = 128 * i + 4 * lane;
+      const float4 wv = *reinterpret_cast<const float4*>(w + c);
+      const float4 bv = *reinterpret_cast<const float4*>(b + c);
+      const float y0 = (v[i].x - mu) * rs * wv.x + bv.x, y1 = (v[i].y - mu) * rs * wv.y + bv.y;
+      const float y2 = (v[i].z - mu) * rs * wv.z + bv.z, y3 = (v[i].w - mu) * rs * wv.w + bv.w;
+      store4(out32 + (size_t)warp * n + c, y0, y1, y2, y3);
+      if (out3) {
+        T* r3 = out3 + (size_t)warp * 3 * n + c;
+        const float h0 = to_f(from_f<T>(y0)), h1 = to_f(from_f<T>(y1)), h2 = to_f(from_f<T>(y2)),
+                    h3 = to_f(from_f<T>(y3));
+        store4(r3, h0, h1, h2, h3);
+        store4(r3 + n, y0 - h0, y1 - h1, y2 - h2, y3 - h3);
+        store4(r3 + 2 * n, h0, h1, h2, h3);
+      }
+    }
+}
+
 // Value output layer + v + legal projection, one warp per row.
 __global__ void value_legal_kernel(imba_model_desc md, imba_step_desc st, const float* __restrict__ hval,
                                    const float* __restrict__ logits) {
@@ -224,7 +334,10 @@ inline int warp_blocks(int rows) { return (rows + 7) / 8; }  // 8 warps per 256-
 
 template <typename T>
 cudaError_t launch_ln_rows(const float* x, int rows, int n, float eps, T* out, cudaStream_t s) {
-  ln_rows_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(x, rows, n, eps, out);
+  if (n % 128 == 0 && n <= 128 * kMaxVec)
+    ln_rows4_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(x, rows, n, eps, out);
+  else
+    ln_rows_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(x, rows, n, eps, out);
   return cudaGetLastError();
 }
 template cudaError_t launch_ln_rows<float>(const float*, int, int, float, float*, cudaStream_t);
@@ -232,7 +345,10 @@ template cudaError_t launch_ln_rows<bf16>(const float*, int, int, float, bf16*, 
 
 template <typename T>
 cudaError_t launch_gate(const float* attn, const float* u, int rows, int n, T* out, cudaStream_t s) {
-  gate_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(attn, u, rows, n, out);
+  if (n % 128 == 0 && n <= 128 * kMaxVec)
+    gate4_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(attn, u, rows, n, out);
+  else
+    gate_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(attn, u, rows, n, out);
   return cudaGetLastError();
 }
 template cudaError_t launch_gate<float>(const float*, const float*, int, int, float*, cudaStream_t);
@@ -241,7 +357,10 @@ template cudaError_t launch_gate<bf16>(const float*, const float*, int, int, bf1
 template <typename T>
 cudaError_t launch_final_ln(const float* x, int rows, int n, const float* w, const float* b, float* out32, T* out3,
                             cudaStream_t s) {
-  final_ln_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(x, rows, n, w, b, out32, out3);
+  if (n % 128 == 0 && n <= 128 * kMaxVec)
+    final_ln4_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(x, rows, n, w, b, out32, out3);
+  else
+    final_ln_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(x, rows, n, w, b, out32, out3);
   return cudaGetLastError();
 }
 template cudaError_t launch_final_ln<float>(const float*, int, int, const float*, const float*, float*, float*,

@@ -63,6 +63,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_
   }
 }
 
+// Bounded wait that also gives up as soon as another role has flagged an
+// abort (so one timed-out wait ends the whole CTA promptly).
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, int32_t* status,
+                                                   volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (global_ns() - t0 > kWaitNs) {
+      report(status, IMBA_ERR_TIMEOUT);
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
