@@ -70,9 +70,15 @@ struct EpiUVQK {
     pool[g.k_off(slot, layer, c / g.dqk) + (c % g.dqk)] = from_f<T>(y);
   }
 
+  // Per-row state of the tensor-core epilogue: the row's KV slot, loaded once per tile.
+  struct Ctx {
+    int64_t slot;
+  };
+  __device__ __forceinline__ Ctx begin(int r, int /*n0*/, int /*bn*/) const { return Ctx{(int64_t)dst_slot[r]}; }
+
   // 32 consecutive columns starting at c0 (a multiple of 32; d_qk and d_v
   // are multiples of 32, so a chunk never straddles a head or a region).
-  __device__ __forceinline__ void chunk32(int r, int c0, int N, const float (&a)[32]) const {
+  __device__ __forceinline__ void chunk32(const Ctx& cx, int r, int c0, int N, const float (&a)[32]) const {
     if (c0 >= N) return;
     float y[32];
 #pragma unroll
@@ -87,7 +93,7 @@ struct EpiUVQK {
       store32(q + (size_t)r * hdq + (c - hdv), y);
       return;
     }
-    const int64_t slot = dst_slot[r];
+    const int64_t slot = cx.slot;
     if (slot < 0 || slot >= g.num_slots) {
       report(status, IMBA_ERR_RANGE);
       return;
@@ -110,10 +116,18 @@ struct EpiResidual {
     float* p = x + (size_t)r * ld + c;
     *p = (acc + bias[c]) + *p;
   }
+  // The tile's residual lines are prefetched into L1 when the row starts.
+  struct Ctx {};
+  __device__ __forceinline__ Ctx begin(int r, int n0, int bn) const {
+    const float* p = x + (size_t)r * ld + n0;
+    for (int c = 0; c < bn && n0 + c < ld; c += 32)
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(p + c));
+    return Ctx{};
+  }
   // All loads are issued before any store: interleaving each load after the
   // previous store of the same row serialises them (the compiler cannot prove
   // x and bias do not alias) and was measured ~30x slower.
-  __device__ __forceinline__ void chunk32(int r, int c0, int N, const float (&a)[32]) const {
+  __device__ __forceinline__ void chunk32(const Ctx&, int r, int c0, int N, const float (&a)[32]) const {
     if (c0 >= N) return;
     float4* p = reinterpret_cast<float4*>(x + (size_t)r * ld + c0);
     const float4* b = reinterpret_cast<const float4*>(bias + c0);
@@ -139,9 +153,11 @@ struct EpiStore {
   float* out;
   int ld;
   __device__ __forceinline__ void operator()(int r, int c, float acc) const { out[(size_t)r * ld + c] = acc; }
+  struct Ctx {};
+  __device__ __forceinline__ Ctx begin(int, int, int) const { return Ctx{}; }
   // The policy row stride (vocab floats) is even but not a multiple of 4:
   // full chunks use 8-byte stores, the ragged last chunk scalar stores.
-  __device__ __forceinline__ void chunk32(int r, int c0, int N, const float (&a)[32]) const {
+  __device__ __forceinline__ void chunk32(const Ctx&, int r, int c0, int N, const float (&a)[32]) const {
     float* o = out + (size_t)r * ld + c0;
     if (c0 + 32 <= N && ((reinterpret_cast<uintptr_t>(o) & 7) == 0)) {
       float2* o2 = reinterpret_cast<float2*>(o);
@@ -170,7 +186,9 @@ struct EpiBiasSilu {
   __device__ __forceinline__ void operator()(int r, int c, float acc) const {
     out[(size_t)r * ld + c] = silu_f(acc + bias[c]);
   }
-  __device__ __forceinline__ void chunk32(int r, int c0, int N, const float (&a)[32]) const {
+  struct Ctx {};
+  __device__ __forceinline__ Ctx begin(int, int, int) const { return Ctx{}; }
+  __device__ __forceinline__ void chunk32(const Ctx&, int r, int c0, int N, const float (&a)[32]) const {
     if (c0 >= N) return;
     float y[32];
     const float4* b = reinterpret_cast<const float4*>(bias + c0);

@@ -143,11 +143,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc::fence_after_sync();
       const int m0 = (tile % mt) * kBM, n0 = (tile / mt) * BN;
       const int row = m0 + quad * 32 + lane;
+      typename Epi::Ctx cx{};
+      if (row < M) cx = epi.begin(row, n0, BN);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         float v[32];
         tc::tmem_ld32(tmem + b * BN + lane_base + c, v);
-        if (row < M && n0 + c < N) epi.chunk32(row, n0 + c, N, v);
+        if (row < M && n0 + c < N) epi.chunk32(cx, row, n0 + c, N, v);
       }
       tc::fence_before_sync();
       __syncwarp();

@@ -26,6 +26,8 @@ from __future__ import annotations
 
 import time
 from dataclasses import dataclass, field
+from itertools import chain
+from operator import itemgetter
 from typing import Any
 
 import numpy as np
@@ -40,6 +42,7 @@ from .protocol import RootEvalResponse, WaveResponse, is_root_request, is_wave_r
 from .synth import EVENT_TOKEN_ID, TOKEN_FIELDS
 
 _TOKEN_FIELDS = TOKEN_FIELDS
+_STATE_FIELDS = itemgetter("turn_id", "castle_id", "ep_file_id", "halfmove_bucket_id", "fullmove_bucket_id")
 
 
 @dataclass
@@ -309,24 +312,31 @@ class ActorInferenceServer:
             chains = [turn.node_chains[row.parent_id] if row.parent_id is not None else [] for row in req.rows]
             turns.append(turn)
             chains_per_req.append(chains)
-        # Tokens (one per row), in request order.
+        # Tokens (one per row), in request order, converted with C-level iterators.
         rows = [row for req in requests for row in req.rows]
         R = len(rows)
-        piece = np.asarray([row.board_state["piece_ids"] for row in rows], dtype=np.int64).reshape(R, 64)
-        if piece.size and (piece.min() < 0 or piece.max() > 12):
+        states = [row.board_state for row in rows]
+        try:  # bytes() converts each 64-int list in C and rejects values outside 0..255
+            piece = np.frombuffer(b"".join([bytes(bs["piece_ids"]) for bs in states]), dtype=np.uint8)
+        except (ValueError, TypeError) as exc:
+            raise ValueError("piece_ids values must be in [0, 12]") from exc
+        if piece.size != R * 64:
+            raise ValueError("every board_state must carry 64 piece_ids")
+        piece = piece.reshape(R, 64)
+        if piece.size and piece.max() > 12:
             raise ValueError("piece_ids values must be in [0, 12]")
         side = np.empty((R, 7), dtype=np.int64)
         side[:, 0] = EVENT_TOKEN_ID
-        for j, k in enumerate(("turn_id", "castle_id", "ep_file_id", "halfmove_bucket_id", "fullmove_bucket_id")):
-            side[:, 1 + j] = [int(row.board_state[k]) for row in rows]
-        side[:, 6] = [int(row.prev_move_vocab_id) for row in rows]
+        if R:
+            side[:, 1:6] = np.array(list(map(_STATE_FIELDS, states)), dtype=np.int64).reshape(R, 5)
+            side[:, 6] = np.fromiter((row.prev_move_vocab_id for row in rows), dtype=np.int64, count=R)
         # Arena rows (logical ids exactly as _KVArena.append mints them) and slots.
         groups = []
         for turn, chains in zip(turns, chains_per_req):
             if turn.arena is None:
                 turn.arena = KVSequence(self.pool)
             groups.append(WaveGroup(prefix=turn.seq, prefix_len=turn.prefix_len, arena=turn.arena, chains=chains))
-        plan, own_rows = wave_plan(groups, piece.astype(np.uint8), side.clip(-(2**31), 2**31 - 1).astype(np.int32),
+        plan, own_rows = wave_plan(groups, piece, side.clip(-(2**31), 2**31 - 1).astype(np.int32),
                                    [row.legal_vocab_ids for row in rows])
         loff = plan.legal_off
         self._sync_if_profiling()
@@ -339,16 +349,17 @@ class ActorInferenceServer:
         self.stats["wave_reqs"] += len(requests)
         self.stats["wave_rows"] += R
         responses = []
+        values = value_stm.tolist()
+        legal_all = legal_flat.tolist()
+        offs = loff.tolist()
         r0 = 0
         for req, turn, chains, own in zip(requests, turns, chains_per_req, own_rows):
-            for row, chain, own_row in zip(req.rows, chains, own):
-                turn.node_chains[row.node_id] = chain + [own_row]
-            out_rows = []
-            for i in range(len(req.rows)):
-                a, b = int(loff[r0 + i]), int(loff[r0 + i + 1])
-                out_rows.append((float(value_stm[r0 + i]), legal_flat[a:b].tolist()))
-            r0 += len(req.rows)
-            responses.append(WaveResponse(rows=out_rows))
+            nc = turn.node_chains
+            for row, ch, own_row in zip(req.rows, chains, own):
+                nc[row.node_id] = ch + [own_row]
+            n = len(req.rows)
+            responses.append(WaveResponse(rows=[(values[i], legal_all[offs[i] : offs[i + 1]]) for i in range(r0, r0 + n)]))
+            r0 += n
         self._sync_if_profiling()
         self.stats["wave_post_s"] += time.perf_counter() - t2
         return responses

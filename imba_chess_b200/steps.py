@@ -17,6 +17,7 @@ row per decode row, numbered consecutively like ``_KVArena.append``.
 from __future__ import annotations
 
 from dataclasses import dataclass
+from itertools import chain
 
 import numpy as np
 
@@ -26,11 +27,13 @@ from .synth import TOKEN_FIELDS
 
 
 def ids_csr(id_lists) -> tuple[np.ndarray, np.ndarray]:
-    """List of per-row id lists -> (int32 offsets [R+1], int32 flat ids)."""
-    lengths = np.fromiter((len(x) for x in id_lists), dtype=np.int64, count=len(id_lists))
-    off = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
-    flat = np.fromiter((int(v) for ids in id_lists for v in ids), dtype=np.int64, count=int(off[-1]))
-    return off, flat.astype(np.int32)
+    """List of per-row id lists -> (int32 offsets [R+1], int32 flat ids).
+    Iterates with C-level iterators (no per-element Python code)."""
+    lengths = np.fromiter(map(len, id_lists), dtype=np.int64, count=len(id_lists))
+    off = np.zeros(len(id_lists) + 1, dtype=np.int64)
+    np.cumsum(lengths, out=off[1:])
+    flat = np.fromiter(chain.from_iterable(id_lists), dtype=np.int64, count=int(off[-1]))
+    return off.astype(np.int32), flat.astype(np.int32)
 
 
 def _token_arrays(tokens: list[dict]) -> tuple[np.ndarray, np.ndarray]:
@@ -98,41 +101,57 @@ class WaveGroup:
 def wave_plan(groups: list[WaveGroup], piece: np.ndarray, side: np.ndarray, legal_ids: list) -> tuple[StepPlan, list[list[int]]]:
     """Grouped decode of every group's rows (rows ordered group by group).
     Returns the plan and, per group, the arena rows minted for its rows."""
-    counts = [len(g.chains) for g in groups]
+    G = len(groups)
+    counts = np.fromiter((len(g.chains) for g in groups), dtype=np.int64, count=G)
+    R = int(counts.sum())
     own_rows: list[list[int]] = []
-    dst_parts, es_parts, ep_parts, elen, positions, pages, gpo = [], [], [], [], [], [], [0]
+    dst_parts, pages = [], []
     for g in groups:
-        n = len(g.chains)
         start = g.arena.length
-        dst = g.arena.reserve(n)
-        own_rows.append(list(range(start, start + n)))
-        P = g.prefix_len
-        depths = np.fromiter((len(c) for c in g.chains), dtype=np.int64, count=n)
-        flat = np.fromiter((x for c in g.chains for x in c), dtype=np.int64, count=int(depths.sum()))
-        chain_slots = g.arena.slots_of(flat) if flat.size else np.zeros(0, np.int64)
-        chain_pos = P + (np.arange(flat.size) - np.repeat(np.cumsum(depths) - depths, depths))
-        ins = np.cumsum(depths)
-        es_parts.append(np.insert(chain_slots, ins, dst))
-        ep_parts.append(np.insert(chain_pos, ins, P + depths))
-        elen.append(depths + 1)
-        positions.append(P + depths)
-        dst_parts.append(dst)
-        pg = g.prefix.page_array(P)
-        pages.append(pg)
-        gpo.append(gpo[-1] + len(pg))
+        dst_parts.append(g.arena.reserve(len(g.chains)))
+        own_rows.append(list(range(start, start + len(g.chains))))
+        pages.append(g.prefix.page_array(g.prefix_len))
+    dst = np.concatenate(dst_parts) if dst_parts else np.zeros(0, np.int64)
+    row_group = np.repeat(np.arange(G), counts)
+    plen = np.fromiter((g.prefix_len for g in groups), dtype=np.int64, count=G)
+    all_chains = [c for g in groups for c in g.chains]
+    depths = np.fromiter(map(len, all_chains), dtype=np.int64, count=R)
+    prow = plen[row_group]
+    positions = prow + depths
+    # Extras of row r: its chain (positions P + j), then itself (position P + depth).
+    per_row = depths + 1
+    eoff = np.zeros(R + 1, dtype=np.int64)
+    np.cumsum(per_row, out=eoff[1:])
+    E = int(eoff[-1])
+    extra_slot = np.empty(E, dtype=np.int64)
+    extra_pos = np.empty(E, dtype=np.int64)
+    own_idx = eoff[1:] - 1
+    extra_slot[own_idx] = dst
+    extra_pos[own_idx] = positions
+    if int(depths.sum()):
+        is_chain = np.ones(E, dtype=bool)
+        is_chain[own_idx] = False
+        chain_slots = []
+        for g in groups:
+            flat = np.fromiter(chain.from_iterable(g.chains), dtype=np.int64)
+            chain_slots.append(g.arena.slots_of(flat) if flat.size else np.zeros(0, np.int64))
+        extra_slot[is_chain] = np.concatenate(chain_slots)
+        j = np.arange(E) - np.repeat(eoff[:-1], per_row)  # index within the row's extras
+        extra_pos[is_chain] = (np.repeat(prow, per_row) + j)[is_chain]
+    gpo = np.zeros(G + 1, dtype=np.int64)
+    np.cumsum([len(p) for p in pages], out=gpo[1:])
     loff, lids = ids_csr(legal_ids)
-    elen_a = np.concatenate(elen) if elen else np.zeros(0, np.int64)
     plan = StepPlan(
         piece_ids=piece,
         side_ids=side,
-        positions=np.concatenate(positions).astype(np.int32) if positions else np.zeros(0, np.int32),
-        row_group=np.repeat(np.arange(len(groups)), counts).astype(np.int32),
-        row_vis=np.repeat([g.prefix_len for g in groups], counts).astype(np.int32),
-        row_extra_off=np.concatenate([[0], np.cumsum(elen_a)]).astype(np.int32),
-        extra_slot=np.concatenate(es_parts).astype(np.int32) if es_parts else np.zeros(0, np.int32),
-        extra_pos=np.concatenate(ep_parts).astype(np.int32) if ep_parts else np.zeros(0, np.int32),
-        row_dst_slot=np.concatenate(dst_parts).astype(np.int32) if dst_parts else np.zeros(0, np.int32),
-        group_page_off=np.asarray(gpo, dtype=np.int32),
+        positions=positions.astype(np.int32),
+        row_group=row_group.astype(np.int32),
+        row_vis=prow.astype(np.int32),
+        row_extra_off=eoff.astype(np.int32),
+        extra_slot=extra_slot.astype(np.int32),
+        extra_pos=extra_pos.astype(np.int32),
+        row_dst_slot=dst.astype(np.int32),
+        group_page_off=gpo.astype(np.int32),
         group_pages=np.concatenate(pages).astype(np.int32) if pages else np.zeros(0, np.int32),
         legal_off=loff,
         legal_ids=lids,
