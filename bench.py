@@ -69,10 +69,9 @@ def parse_args():
 
 
 def dist_env():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return world, rank, local
+    from imba_chess_b200.shard import dist_env as env
+
+    return env()
 
 
 def load_peaks():
@@ -88,12 +87,23 @@ def load_peaks():
 # ----------------------------------------------------------------------
 # Workload
 # ----------------------------------------------------------------------
-def workload(args, rank):
+def workload(args, rank, world=1):
+    """This rank's parents: global parent i (seed 1234 + i) belongs to rank
+    i % world (imba_chess_b200.shard.shard_games); every rank gets
+    ``--parents`` of them (weak scaling)."""
     from imba_chess_b200 import synth
+    from imba_chess_b200.shard import shard_games
 
     dims = synth.D512
-    wave = synth.grouped_wave(dims, n_parents=args.parents, plies=tuple(args.plies), siblings=tuple(args.siblings),
-                              seed=1234 + rank * args.parents)
+    mine = shard_games(args.parents * world, rank, world)
+    parts = [synth.grouped_wave(dims, n_parents=1, plies=tuple(args.plies), siblings=tuple(args.siblings),
+                                seed=1234 + i) for i in mine]
+    wave = synth.GroupedWave(
+        prefix_tokens=[p.prefix_tokens[0] for p in parts],
+        row_tokens=synth.concat_tokens([p.row_tokens for p in parts]),
+        group_index=np.concatenate([np.full(p.num_rows, g, dtype=np.int64) for g, p in enumerate(parts)]),
+        legal_ids=[ids for p in parts for ids in p.legal_ids],
+    )
     return dims, wave
 
 
@@ -344,9 +354,10 @@ def run_b200(args):
     from imba_chess_b200.kvpool import KVSequence
     from imba_chess_b200.model import B200HSTUChessModel
     from imba_chess_b200.plan import DeviceStep
+    from imba_chess_b200.shard import reduce_max, reduce_sum
     from imba_chess_b200.steps import WaveGroup, root_plan, wave_plan
 
-    dims, wave = workload(args, rank)
+    dims, wave = workload(args, rank, world)
     sd = synth.make_state_dict(dims, 2, profile="reference")
     model = B200HSTUChessModel(sd, dtype=torch.bfloat16, device=device)
     lens = wave.prefix_lens
@@ -428,13 +439,10 @@ def run_b200(args):
         dist.barrier()
     sampler.stop()
     model.check_status()
-    elapsed_ms = t_start.elapsed_time(t_end)
-    if world > 1:
-        tmax = torch.tensor([elapsed_ms], dtype=torch.float64, device=device)
-        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(tmax.item())
+    elapsed_ms = reduce_max(t_start.elapsed_time(t_end), device)
+    rows_all = reduce_sum(R, device)  # positions per step over all ranks
     ms_per_step = elapsed_ms / args.steps
-    value = R * args.steps * world / (elapsed_ms / 1000.0)
+    value = rows_all * args.steps / (elapsed_ms / 1000.0)
 
     # Per-phase device times (averaged over the timed steps).
     acc = {p: 0.0 for p in PHASES}
@@ -498,13 +506,9 @@ def run_b200(args):
             lat.append(time.perf_counter() - t0)
     e2e_end.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e2e_start.elapsed_time(e2e_end)
-    if world > 1:
-        t = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = reduce_max(e2e_start.elapsed_time(e2e_end), device)
     e2e = {
-        "value": R * args.steps * world / (e2e_ms / 1000.0),
+        "value": rows_all * args.steps / (e2e_ms / 1000.0),
         "unit": UNIT,
         "h2d_bytes_per_step": int(dstep.h2d_bytes),
         "d2h_bytes_per_step": int(host_out.numel() * 4),
@@ -524,7 +528,7 @@ def run_b200(args):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": workload_config(args) | {"rows_per_step": R, "parallelism": f"dp{world} (independent games)"},
+        "config": workload_config(args) | {"rows_per_step": int(rows_all), "parallelism": f"dp{world} (independent games)"},
         "e2e": e2e,
         "roofline": roofline,
         "kernels": kernels,
