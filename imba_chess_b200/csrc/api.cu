@@ -7,6 +7,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <new>
+#include <type_traits>
 
 #include "gemm_tc.cuh"
 #include "kernels.cuh"
@@ -44,6 +45,7 @@ size_t workspace_layout(const imba_model* m, int32_t rows, void* base, Workspace
   w.hval = static_cast<float*>(take(R * (d.model_dim / 2 + 1) * 4));
   w.logits = static_cast<float*>(take(R * d.vocab * 4));
   w.pooled = static_cast<float*>(take(d.dtype == IMBA_DTYPE_BF16 ? R * IMBA_BOARD_DIM * 4 : 0));
+  w.counters = static_cast<int*>(take(kNumCounters * sizeof(int)));
   w.bytes = off;
   if (ws) *ws = w;
   return off;
@@ -121,6 +123,7 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
   } while (0)
 
   IMBA_CK(pm.mark(s));
+  IMBA_CK(cudaMemsetAsync(w.counters, 0, kNumCounters * sizeof(int), s));
   if (md.dtype == IMBA_DTYPE_BF16 && !m->simt_board) {
     // tensor-core board encoder -> pooled [R, 64]; projection + embeddings in the GEMM epilogue
     IMBA_CK(launch_board_mma(md, st, w.pooled, s));
@@ -144,14 +147,17 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
       return IMBA_ERR_CUDA;
     }
     IMBA_CK(pm.mark(s));
-    AttnArgs aa{w.q, pool.base, g, l, md.ps_w[l], md.max_pos, 1.0f / sqrtf((float)md.attention_dim), st, w.attn};
-    if (m->simt_attn || !launch_attn_mma(aa, md.num_layers, md, pool.num_pages, s, &e)) {
+    AttnArgs aa{w.q, pool.base, g, l, md.ps_w[l], md.max_pos, 1.0f / sqrtf((float)md.attention_dim), st, w.attn,
+                w.counters + l * kCountersPerLayer};
+    bool fused = false;
+    bf16* gated_bf = std::is_same<T, bf16>::value ? reinterpret_cast<bf16*>(w.gated) : nullptr;
+    if (m->simt_attn || !launch_attn_page(aa, md.num_layers, md, pool.num_pages, w.u, gated_bf, s, &e, &fused)) {
       IMBA_CK(launch_attn_simt<T>(aa, s));
     } else if (e != cudaSuccess) {
       return IMBA_ERR_CUDA;
     }
     IMBA_CK(pm.mark(s));
-    IMBA_CK(launch_gate<T>(w.attn, w.u, R, hdv, static_cast<T*>(w.gated), s));
+    if (!fused) IMBA_CK(launch_gate<T>(w.attn, w.u, R, hdv, static_cast<T*>(w.gated), s));
     IMBA_CK(pm.mark(s));
     EpiResidual er{w.x, md.o_b[l], d};
     if (!gemm_tc_launch_out(m, l, R, static_cast<const T*>(w.gated), er, st.status, s, &e)) {

@@ -95,6 +95,10 @@ struct imba_model {
 namespace imba {
 
 // Scratch buffers carved out of the caller's workspace for one step.
+// Work-queue counters per step: one per (layer, attention head group).
+constexpr int kCountersPerLayer = 16;
+constexpr int kNumCounters = IMBA_MAX_LAYERS * kCountersPerLayer;
+
 struct Workspace {
   float* x;        // [R, d]      residual stream
   void* xn;        // [R, d]      LN(x), model dtype
@@ -107,6 +111,7 @@ struct Workspace {
   float* hval;     // [R, d/2]    value-head hidden
   float* logits;   // [R, vocab]  used when the caller passes no logits buffer
   float* pooled;   // [R, 64]     bf16 models: mean-pooled board-encoder output
+  int* counters;   // [kNumCounters] work-queue counters, zeroed at the start of every step
   size_t bytes;
 };
 

@@ -15,6 +15,7 @@ struct AttnArgs {
   float scale;          // 1 / sqrt(d_qk)
   imba_step_desc st;
   float* out;           // [R, H dv]
+  int* counters;        // this layer's work-queue counters (zero at launch)
 };
 
 cudaError_t launch_embed(const imba_model_desc& md, const imba_step_desc& st, float* x, cudaStream_t s);
@@ -36,8 +37,10 @@ cudaError_t launch_gemm_simt(const TA* A, int lda, const TW* W, int ldw, int M, 
                              cudaStream_t s);
 template <typename T>
 cudaError_t launch_attn_simt(const AttnArgs& a, cudaStream_t s);
-// Tensor-core attention (bf16, head dims 64); false when it does not apply.
-bool launch_attn_mma(const AttnArgs& a, int num_layers, const imba_model_desc& md, int64_t num_pages,
-                     cudaStream_t s, cudaError_t* err);
+// Tensor-core paged attention (bf16, head dims 64); false when it does not
+// apply.  With every head in one CTA it also applies the attention-output
+// norm and the u gate, writes `gated` and sets *fused.
+bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& md, int64_t num_pages,
+                      const float* u, bf16* gated, cudaStream_t s, cudaError_t* err, bool* fused);
 
 }  // namespace imba

@@ -51,14 +51,19 @@ def piece_ids_from_tokens(tok: dict) -> np.ndarray:
     return p.astype(np.uint8)
 
 
-def build_chunks(row_group: np.ndarray, num_groups: int):
-    """Rows ordered by group (stable), split into chunks of <= 64 rows.  A
-    group with more than 64 rows is split into equal-size chunks."""
+def build_chunks(row_group: np.ndarray, num_groups: int, max_rows: int = 32, row_vis: np.ndarray | None = None):
+    """Rows ordered by group (stable), split into chunks of <= ``max_rows``
+    rows (the C ABI allows up to 64; 32 is one attention work item).  A group
+    with more rows is split into equal-size chunks.  With ``row_vis`` the
+    chunks are listed longest visible prefix first, so the attention kernel's
+    dynamic work queue starts the longest items first."""
+    if not 1 <= max_rows <= CHUNK:
+        raise ValueError(f"max_rows must be in [1, {CHUNK}]")
     row_group = np.asarray(row_group, dtype=np.int64)
     order = np.argsort(row_group, kind="stable").astype(np.int32)
     counts = np.bincount(row_group, minlength=num_groups).astype(np.int64)
     starts = np.concatenate([[0], np.cumsum(counts)[:-1]]).astype(np.int64)
-    nch = (counts + CHUNK - 1) // CHUNK
+    nch = (counts + max_rows - 1) // max_rows
     chunk_group = np.repeat(np.arange(num_groups, dtype=np.int64), nch)
     first = np.repeat(np.cumsum(nch) - nch, nch)
     cidx = np.arange(int(nch.sum()), dtype=np.int64) - first
@@ -70,6 +75,12 @@ def build_chunks(row_group: np.ndarray, num_groups: int):
     hi = (cidx + 1) * n_g // k_g
     chunk_row_off = starts[chunk_group] + lo
     chunk_nrows = hi - lo
+    if row_vis is not None and chunk_group.size:
+        vis_sorted = np.asarray(row_vis, dtype=np.int64)[order]
+        # longest visible prefix of each chunk (rows of a chunk are contiguous in `order`)
+        cost = np.maximum.reduceat(vis_sorted, chunk_row_off) if vis_sorted.size else np.zeros(0, np.int64)
+        by_cost = np.argsort(-cost, kind="stable")
+        chunk_group, chunk_row_off, chunk_nrows = chunk_group[by_cost], chunk_row_off[by_cost], chunk_nrows[by_cost]
     return (
         order,
         chunk_group.astype(np.int32),
@@ -105,7 +116,7 @@ class StepPlan:
 
     def finalize(self) -> "StepPlan":
         if self.chunks is None:
-            self.chunks = build_chunks(self.row_group, self.num_groups)
+            self.chunks = build_chunks(self.row_group, self.num_groups, row_vis=self.row_vis)
         return self
 
     def arrays(self) -> dict[str, np.ndarray]:

@@ -7,8 +7,11 @@ on a full grouped-decode step: final hidden state, logits, value logits.
 * gemm  - tcgen05/TMA GEMMs vs SIMT GEMMs: the same bf16 operands, fp32
           accumulation (the policy GEMM is exact fp32 in SIMT and split bf16 on
           the tensor cores);
-* attn  - mma.sync attention with TMA-loaded KV tiles vs the SIMT attention
-          (the tensor-core kernel rounds softmax weights to bf16 for P.V);
+* attn  - mma.sync paged attention (TMA-loaded KV pages, attention-output
+          norm and u gate fused into its epilogue) vs the SIMT attention and
+          the separate gate pass (the tensor-core kernel rounds softmax
+          weights to bf16 for P.V); the second wave's rows carry suffix
+          chains, so several gathered extra-key tiles per CTA are covered;
 * board - mma.sync board encoder (bf16 operands) vs the fp32 SIMT encoder.
 """
 

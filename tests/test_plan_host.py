@@ -30,7 +30,23 @@ def test_chunks_cover_every_row_once_grouped_and_bounded():
 
 def test_group_with_many_rows_is_split_evenly():
     perm, cg, co, cn = build_chunks(np.zeros(130, np.int64), 1)
+    assert cn.tolist() == [26] * 5
+    perm, cg, co, cn = build_chunks(np.zeros(130, np.int64), 1, max_rows=64)
     assert cn.tolist() == [43, 43, 44]
+
+
+def test_chunks_listed_longest_prefix_first():
+    rng = np.random.default_rng(2)
+    G = 9
+    row_group = rng.integers(0, G, 300)
+    group_vis = rng.integers(1, 400, G)
+    row_vis = group_vis[row_group]
+    perm, cg, co, cn = build_chunks(row_group, G, row_vis=row_vis)
+    cost = [int(row_vis[perm[o : o + n]].max()) for o, n in zip(co, cn)]
+    assert cost == sorted(cost, reverse=True)
+    assert int(cn.sum()) == 300 and (cn <= 32).all()
+    for c in range(len(cg)):
+        assert (row_group[perm[co[c] : co[c] + cn[c]]] == cg[c]).all()
 
 
 def _plan(R=5):
