@@ -82,7 +82,7 @@ struct EpiUVQK {
     if (c0 >= N) return;
     float y[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) y[i] = silu_fast(a[i]);
+    for (int i = 0; i < 32; ++i) y[i] = silu_tanh(a[i]);
     const int hdv = g.H * g.dv, hdq = g.H * g.dqk;
     if (c0 < hdv) {
       store32(u + (size_t)r * hdv + c0, y);

@@ -7,9 +7,10 @@
 // ring guarded by full / empty mbarriers.  Warp 0 (one thread) issues the TMA
 // copies, warp 1 (one thread) issues tcgen05.mma (M = 128, N = BN, K = 16 per
 // instruction) into one of two TMEM accumulators and releases each stage with
-// tcgen05.commit; four epilogue warps read the other accumulator back (TMEM
-// lane quadrant = warp % 4 = tile rows) and hand 32-column chunks to the
-// epilogue functor, so tile i's epilogue overlaps tile i + 1's main loop.
+// tcgen05.commit; eight epilogue warps read the other accumulator back (TMEM
+// lane quadrant = warp % 4 = tile rows; two warps per quadrant, one per
+// column half) and hand 32-column chunks to the epilogue functor, so tile i's
+// epilogue overlaps tile i + 1's main loop.
 // Out-of-range rows / columns of A / W are zero-filled by TMA and skipped by
 // the epilogue.
 //
@@ -37,13 +38,13 @@ struct TileShape {
   static constexpr size_t kSmem = 1024 + STAGES * (kABytes + kBBytes) + (2 * STAGES + 4) * 8 + 16;
 };
 
-constexpr int kEpiWarps = 4;
-constexpr int kGemmThreads = 64 + 32 * kEpiWarps;  // producer warp, MMA warp, 4 epilogue warps
+constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;  // producer warp, MMA warp, 8 epilogue warps
 
 // Persistent, warp-specialised: CTA b handles tiles b, b + gridDim.x, ...
 // (tile t -> m-tile t % mt, n-tile t / mt).  Warp 0 streams A / W tiles
 // through the smem ring; warp 1 issues the MMAs of tile i into TMEM buffer
-// i % 2 (2 x BN columns) and signals acc_full; warps 2..5 drain buffer i % 2
+// i % 2 (2 x BN columns) and signals acc_full; warps 2..9 drain buffer i % 2
 // while tile i + 1 is being loaded and multiplied, then signal acc_empty.
 template <int BN, int STAGES, class Epi>
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -131,8 +132,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!ok) break;
       }
     }
-  } else {  // epilogue warps
+  } else {  // epilogue warps: two per TMEM lane quadrant, one per column half
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int c_lo = (warp - 2) >= 4 ? BN / 2 : 0;
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     int i = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++i) {
@@ -144,9 +146,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int m0 = (tile % mt) * kBM, n0 = (tile / mt) * BN;
       const int row = m0 + quad * 32 + lane;
       typename Epi::Ctx cx{};
-      if (row < M) cx = epi.begin(row, n0, BN);
+      if (row < M) cx = epi.begin(row, n0 + c_lo, BN / 2);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = c_lo; c < c_lo + BN / 2; c += 32) {
         float v[32];
         tc::tmem_ld32(tmem + b * BN + lane_base + c, v);
         if (row < M && n0 + c < N) epi.chunk32(cx, row, n0 + c, N, v);

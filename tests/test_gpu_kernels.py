@@ -6,7 +6,7 @@ on a full grouped-decode step: final hidden state, logits, value logits.
 
 * gemm  - tcgen05/TMA GEMMs vs SIMT GEMMs: the same bf16 operands, fp32
           accumulation (the policy GEMM is exact fp32 in SIMT and split bf16 on
-          the tensor cores);
+          the tensor cores; the uvqk epilogue's SiLU uses the hardware tanh);
 * attn  - mma.sync paged attention (TMA-loaded KV pages, attention-output
           norm and u gate fused into its epilogue) vs the SIMT attention and
           the separate gate pass (the tensor-core kernel rounds softmax
@@ -29,8 +29,11 @@ from imba_chess_b200.steps import WaveGroup, root_plan, wave_plan
 
 pytestmark = pytest.mark.gpu
 
-# (hidden relative to its max magnitude, logits abs, value logits abs)
-TOL = {"gemm": (1e-4, 2e-3, 1e-3), "attn": (2e-3, 2e-2, 5e-3), "board": (2e-3, 3e-2, 1e-2)}
+# (hidden relative to its max magnitude, logits abs, value logits abs).  The
+# tensor-core uvqk epilogue computes SiLU through the hardware tanh (relative
+# error ~2^-11) where the SIMT epilogue uses the exact exponential form, so
+# the gemm bounds cover that as well as accumulation order.
+TOL = {"gemm": (2e-4, 5e-3, 2e-3), "attn": (2e-3, 2e-2, 5e-3), "board": (2e-3, 3e-2, 1e-2)}
 
 
 def _run_wave(model, dims, wave, depth2=True):
