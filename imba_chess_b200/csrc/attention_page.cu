@@ -26,9 +26,10 @@
 // ps_w[h, clamp(k - q + max - 1)], masks keys beyond each row's visible
 // prefix, updates the fp32 online softmax in registers and accumulates
 // O += P V.  The rows' extra keys (each row's suffix chain and the row
-// itself: scattered arena slots) are gathered with cp.async into 16-key
-// tiles of the same layout and go through the same step with an ownership
-// mask (key j is visible to row r only if it is one of r's extras).
+// itself: scattered arena slots, usually one to a few per row) are folded in
+// per row afterwards: the four lanes that share a row split the 64-dim dot
+// product (a quad reduction), update the row's online softmax and add p v to
+// their O columns, reading K / V straight from the pool.
 // Epilogue: O / l; when the CTA holds every head, LayerNorm over the row's
 // H dv outputs (no affine, eps 1e-6) times u, stored in bf16 for the output
 // projection; otherwise fp32 O is stored and the gate runs as its own pass.
@@ -56,16 +57,12 @@ constexpr int kMaxThreads = (2 * kMaxHC + 1) * 32;
 // Item buffer (int32 words): header, then per-row arrays.
 constexpr int kItN = 0;        // rows in the item (-1: no more items)
 constexpr int kItNpg = 1;      // visible pages (ceil of the longest row's prefix / 16)
-constexpr int kItNextra = 2;   // extra keys of the item's rows
 constexpr int kItRows = 8;     // [32] global row ids
 constexpr int kItVis = 40;     // [32] visible prefix tokens
 constexpr int kItQpos = 72;    // [32] query positions
 constexpr int kItXoff = 104;   // [32] first extra of the row
-constexpr int kItXstart = 136; // [33] exclusive scan of extras per row
-constexpr int kItXown = 172;   // [16] first extra tile: owner row (-1: none)
-constexpr int kItXpos = 188;   // [16] its position
-constexpr int kItXslot = 204;  // [16] its pool slot (-1: none)
-constexpr int kItemInts = 224;
+constexpr int kItXcnt = 136;   // [32] extras of the row
+constexpr int kItemInts = 168;
 
 struct PageParams {
   AttnArgs a;
@@ -161,14 +158,13 @@ struct RowState {
 
 // Scale / bias / mask one 16-row x 16-key score block, update the online
 // softmax of its rows and return P as the bf16 A fragment of P V.
-// kExtra: keys are gathered extras (owner row and position per key in smem).
-// Otherwise prefix tokens t0 .. t0 + 15; kFast: every key is visible to both
+// Keys are prefix tokens t0 .. t0 + 15; kFast: every key is visible to both
 // rows and no bias index needs clamping (the common case of a full page).
 // scale2 = scale * log2(e).
-template <bool kExtra, bool kFast, class Bias>
+template <bool kFast, class Bias>
 __device__ __forceinline__ void softmax16(RowState& rs, float (&sc)[2][4], uint32_t (&pa)[4], int t0, int vis0,
-                                          int vis1, int qp0, int qp1, int rl0, int rl1, const int* x_owner,
-                                          const int* x_pos, const Bias& psw, float scale2, int max_pos, int t) {
+                                          int vis1, int qp0, int qp1, const Bias& psw, float scale2, int max_pos,
+                                          int t) {
   float mx0 = -INFINITY, mx1 = -INFINITY;
   if (kFast) {
     const int b0 = t0 - qp0 + max_pos - 1 + 2 * t, b1 = t0 - qp1 + max_pos - 1 + 2 * t;
@@ -187,19 +183,8 @@ __device__ __forceinline__ void softmax16(RowState& rs, float (&sc)[2][4], uint3
     for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int j = 8 * nt + 2 * t + e;
-        bool v0, v1;
-        int kpos;
-        if (!kExtra) {
-          kpos = t0 + j;
-          v0 = kpos < vis0;
-          v1 = kpos < vis1;
-        } else {
-          const int own = x_owner[j];
-          kpos = x_pos[j];
-          v0 = own == rl0;
-          v1 = own == rl1;
-        }
+        const int kpos = t0 + 8 * nt + 2 * t + e;
+        const bool v0 = kpos < vis0, v1 = kpos < vis1;
         sc[nt][e] = v0 ? fmaf(sc[nt][e], scale2, psw(bias_index(kpos, qp0, max_pos))) : -INFINITY;
         sc[nt][2 + e] = v1 ? fmaf(sc[nt][2 + e], scale2, psw(bias_index(kpos, qp1, max_pos))) : -INFINITY;
         mx0 = fmaxf(mx0, sc[nt][e]);
@@ -249,10 +234,10 @@ __device__ __forceinline__ void softmax16(RowState& rs, float (&sc)[2][4], uint3
 
 // One 16-key block for the warp's 16 query rows: S = Q K^T (Q fragments
 // read from the shared Q tile with ldmatrix), softmax16, O += P V.
-template <bool kExtra, bool kFast, class Bias>
+template <bool kFast, class Bias>
 __device__ __forceinline__ void step16(RowState& rs, uint32_t qb, uint32_t kb, uint32_t vb, int t0, int vis0,
-                                       int vis1, int qp0, int qp1, int rl0, int rl1, const int* x_owner,
-                                       const int* x_pos, const Bias& psw, float scale2, int max_pos, int lane) {
+                                       int vis1, int qp0, int qp1, const Bias& psw, float scale2, int max_pos,
+                                       int lane) {
   const int t = lane & 3, r8 = lane & 7, mm = lane >> 3;
   float sc[2][4];
 #pragma unroll
@@ -266,14 +251,62 @@ __device__ __forceinline__ void step16(RowState& rs, uint32_t qb, uint32_t kb, u
     mma16816(sc[1], qa, f[2], f[3]);
   }
   uint32_t pa[4];
-  softmax16<kExtra, kFast, Bias>(rs, sc, pa, t0, vis0, vis1, qp0, qp1, rl0, rl1, x_owner, x_pos, psw, scale2,
-                                 max_pos, t);
+  softmax16<kFast, Bias>(rs, sc, pa, t0, vis0, vis1, qp0, qp1, psw, scale2, max_pos, t);
 #pragma unroll
   for (int np = 0; np < 4; ++np) {
     uint32_t f[4];
     ldsm_x4_t(f, vb + blk_off(r8 + 8 * (mm & 1), 2 * np + (mm >> 1)));
     mma16816(rs.o[2 * np], pa, f[0], f[1]);
     mma16816(rs.o[2 * np + 1], pa, f[2], f[3]);
+  }
+}
+
+// Fold one extra key (pool slot, position) into one row's online softmax.
+// The row's four lanes (t = 0..3) each take 16 of the 64 dims of q . k and
+// reduce across the quad; ol / oh: this lane's O columns 8 j + 2 t, +1 of the
+// row.  active is uniform across the quad.
+template <class Bias>
+__device__ __forceinline__ void extra_key(float& m, float& l, float (&o)[8][4], int ci, bool active, uint32_t qrow,
+                                          int qrow_sw, const bf16* kp, const bf16* vp, int kpos, int qpos,
+                                          const Bias& psw, float scale2, int max_pos, int t) {
+  float part = 0.f;
+  uint4 kv[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+  if (active) {
+    kv[0] = __ldg(reinterpret_cast<const uint4*>(kp + 16 * t));
+    kv[1] = __ldg(reinterpret_cast<const uint4*>(kp + 16 * t + 8));
+  }
+  uint32_t vv[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) vv[j] = active ? __ldg(reinterpret_cast<const uint32_t*>(vp + 8 * j + 2 * t)) : 0u;
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    uint4 qv;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(qv.x), "=r"(qv.y), "=r"(qv.z), "=r"(qv.w)
+                 : "r"(qrow + (uint32_t)(((2 * t + c) ^ qrow_sw) << 4)));
+    const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+    const uint32_t kw[4] = {kv[c].x, kv[c].y, kv[c].z, kv[c].w};
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float2 qf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qw[w]));
+      const float2 kf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kw[w]));
+      part = fmaf(qf.x, kf.x, part);
+      part = fmaf(qf.y, kf.y, part);
+    }
+  }
+  part += __shfl_xor_sync(0xffffffffu, part, 1);
+  part += __shfl_xor_sync(0xffffffffu, part, 2);
+  if (!active) return;
+  const float s2 = fmaf(part, scale2, psw(bias_index(kpos, qpos, max_pos)));
+  const float mn = fmaxf(m, s2);
+  const float c = exp2_approx(m - mn), p = exp2_approx(s2 - mn);
+  m = mn;
+  l = fmaf(l, c, t == 0 ? p : 0.f);  // the quad's partial sums: one lane counts the key
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float2 vf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vv[j]));
+    o[j][2 * ci] = fmaf(o[j][2 * ci], c, p * vf.x);
+    o[j][2 * ci + 1] = fmaf(o[j][2 * ci + 1], c, p * vf.y);
   }
 }
 
@@ -294,16 +327,12 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = base;                                    // S stages: [K: HC x 2 KB][V: HC x 2 KB]
-  uint8_t* xtile = ring + S * stage_bytes;                 // gathered extra keys, same layout
-  uint8_t* qtile = xtile + stage_bytes;                    // [HC][32 rows][128 B] queries, 128-byte swizzle
+  uint8_t* qtile = ring + S * stage_bytes;                 // [HC][32 rows][128 B] queries, 128-byte swizzle
   const int bias_w = 2 * a.max_pos - 1;                    // ps_w row length
   __half* bias_s = reinterpret_cast<__half*>(qtile + HC * kHalfRows * 128);  // [HC][bias_w] (kSmemBias)
   const int bias_bytes = kSmemBias ? (HC * bias_w * 2 + 15) / 16 * 16 : 0;
   int* items = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bias_s) + bias_bytes);  // [2][kItemInts]
-  int* x_owner = items + 2 * kItemInts;                    // [16] extra tiles after the first
-  int* x_pos = x_owner + 16;                               // [16]
-  int* x_slot = x_pos + 16;                                // [16]
-  float* red_sum = reinterpret_cast<float*>(x_slot + 16);  // [kMaxHC][32] per-(head, row) partial sums
+  float* red_sum = reinterpret_cast<float*>(items + 2 * kItemInts);  // [kMaxHC][32] per-(head, row) sums
   float* red_sq = red_sum + kMaxHC * kHalfRows;            // [kMaxHC][32]
   int* misc = reinterpret_cast<int*>(red_sq + kMaxHC * kHalfRows);  // [0] abort flag, [1] pad
   uint64_t* full = reinterpret_cast<uint64_t*>(misc + 2);           // 8-byte aligned: even int count precedes
@@ -407,50 +436,18 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         }
         cnt = e1 - e0;
       }
-      int incl = cnt;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int w = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += w;
-      }
       int vm = v;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) vm = max(vm, __shfl_xor_sync(0xffffffffu, vm, o));
       const int npg = (vm + IMBA_PAGE_TOKENS - 1) / IMBA_PAGE_TOKENS;
-      const int n_extra = __shfl_sync(0xffffffffu, incl, 31);
       item[kItRows + lane] = r;
       item[kItVis + lane] = v;
       item[kItQpos + lane] = qp;
       item[kItXoff + lane] = e0;
-      item[kItXstart + lane] = incl - cnt;
-      if (lane == 31) item[kItXstart + kHalfRows] = incl;
-      __syncwarp();
-      if (lane < IMBA_PAGE_TOKENS) {  // owners of the first extra tile
-        int own = -1, pos = 0, slot = -1;
-        if (lane < n_extra) {
-          int lo = 0, hi = n;  // last row with x_start[row] <= lane
-          while (hi - lo > 1) {
-            const int mid = (lo + hi) >> 1;
-            if (item[kItXstart + mid] <= lane) lo = mid; else hi = mid;
-          }
-          const int xi = item[kItXoff + lo] + (lane - item[kItXstart + lo]);
-          slot = st.extra_slot[xi];
-          pos = st.extra_pos[xi];
-          if (slot < 0 || slot >= a.g.num_slots) {
-            report(st.status, IMBA_ERR_RANGE);
-            slot = -1;
-          } else {
-            own = lo;
-          }
-        }
-        item[kItXown + lane] = own;
-        item[kItXpos + lane] = pos;
-        item[kItXslot + lane] = slot;
-      }
+      item[kItXcnt + lane] = cnt;
       if (lane == 0) {
         item[kItN] = n;
         item[kItNpg] = npg;
-        item[kItNextra] = n_extra;
       }
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&item_full[ib]);
@@ -503,26 +500,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
   else psw.p = a.ps_w + (size_t)h * bias_w;
   const bf16* Pool = static_cast<const bf16*>(a.pool);
   const bf16* Q = static_cast<const bf16*>(a.q);
-  const uint32_t ring_base = tc::smem_u32(ring), xb = tc::smem_u32(xtile), qtb = tc::smem_u32(qtile);
+  const uint32_t ring_base = tc::smem_u32(ring), qtb = tc::smem_u32(qtile);
   const uint32_t qb = qtb + hl * (kHalfRows * 128) + rb * (16 * 128);  // this warp's 16 query rows
-
-  // cp.async gather of one 16-key extra tile for the CTA's heads (slots[j]: pool slot of key j, -1: zeros).
-  auto gather = [&](const int* slots) {
-    for (int idx = tid; idx < IMBA_PAGE_TOKENS * HC * 16; idx += nct) {
-      const int part = idx & 15, rest = idx >> 4;
-      const int j = rest & 15, hh = rest >> 4;
-      const uint32_t dst = xb + (part < 8 ? 0u : (uint32_t)(HC * kPageBytes)) + hh * kPageBytes + blk_off(j, part & 7);
-      const int slot = slots[j];
-      if (slot >= 0) {
-        const bf16* src = Pool + (part < 8 ? a.g.k_off(slot, a.layer, h0 + hh) : a.g.v_off(slot, a.layer, h0 + hh)) +
-                          8 * (part & 7);
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
-      } else {
-        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};\n" ::"r"(dst), "r"(0u) : "memory");
-      }
-    }
-    asm volatile("cp.async.commit_group;\n" ::: "memory");
-  };
 
   int pc = 0;
   for (int it = 0;; ++it) {
@@ -536,8 +515,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     }
     const int n = item[kItN];
     if (n < 0) return;
-    const int npg = item[kItNpg], n_extra = item[kItNextra];
-    const int xtiles = (n_extra + IMBA_PAGE_TOKENS - 1) / IMBA_PAGE_TOKENS;
+    const int npg = item[kItNpg];
     // Query tile of the item: row r, head hh, 16-byte chunk c8 (rows past n are zero).
     for (int idx = tid; idx < kHalfRows * HC * 8; idx += nct) {
       const int c8 = idx & 7, rest = idx >> 3;
@@ -551,7 +529,6 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       }
     }
     asm volatile("cp.async.commit_group;\n" ::: "memory");
-    if (xtiles > 0) gather(item + kItXslot);
     const bool live = 16 * rb < n;
     // Rows past n mirror row 0 (never stored): they keep the fast path and
     // every bias index of a full page in range.
@@ -570,8 +547,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     int wvis = max(vis0, vis1);  // pages past every row of this warp are skipped
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) wvis = max(wvis, __shfl_xor_sync(0xffffffffu, wvis, o));
-    if (xtiles > 0) asm volatile("cp.async.wait_group 1;\n" ::: "memory");
-    else asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     bar_consumers(nct);  // the query tile is complete
     RowState rs;
 #pragma unroll
@@ -591,11 +567,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         const uint32_t kb = ring_base + s * stage_bytes + hl * kPageBytes;
         const int t0 = p * IMBA_PAGE_TOKENS;
         if (t0 >= fast_lo && t0 + IMBA_PAGE_TOKENS <= fast_hi)
-          step16<false, true, Bias>(rs, qb, kb, kb + HC * kPageBytes, t0, vis0, vis1, qp0, qp1, rl0, rl1, nullptr,
-                                    nullptr, psw, scale2, a.max_pos, lane);
+          step16<true, Bias>(rs, qb, kb, kb + HC * kPageBytes, t0, vis0, vis1, qp0, qp1, psw, scale2, a.max_pos,
+                             lane);
         else
-          step16<false, false, Bias>(rs, qb, kb, kb + HC * kPageBytes, t0, vis0, vis1, qp0, qp1, rl0, rl1, nullptr,
-                                     nullptr, psw, scale2, a.max_pos, lane);
+          step16<false, Bias>(rs, qb, kb, kb + HC * kPageBytes, t0, vis0, vis1, qp0, qp1, psw, scale2, a.max_pos,
+                              lane);
       }
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&empty[s]);
@@ -607,41 +583,36 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       asm volatile("cp.async.wait_all;\n" ::: "memory");
       return;  // the status word already holds the timeout
     }
-    for (int xt = 0; xt < xtiles; ++xt) {
-      const int* own = xt == 0 ? item + kItXown : x_owner;
-      const int* xps = xt == 0 ? item + kItXpos : x_pos;
-      asm volatile("cp.async.wait_all;\n" ::: "memory");
-      bar_consumers(nct);
-      if (live)
-        step16<true, false, Bias>(rs, qb, xb + hl * kPageBytes, xb + (HC + hl) * kPageBytes, 0, 0, 0, qp0, qp1, rl0,
-                                  rl1, own, xps, psw, scale2, a.max_pos, lane);
-      bar_consumers(nct);
-      if (xt + 1 < xtiles) {  // resolve the next tile's owners, then gather it
-        if (tid < IMBA_PAGE_TOKENS) {
-          const int q = (xt + 1) * IMBA_PAGE_TOKENS + tid;
-          int ow = -1, pos = 0, slot = -1;
-          if (q < n_extra) {
-            int lo = 0, hi = n;
-            while (hi - lo > 1) {
-              const int mid = (lo + hi) >> 1;
-              if (item[kItXstart + mid] <= q) lo = mid; else hi = mid;
-            }
-            const int xi = item[kItXoff + lo] + (q - item[kItXstart + lo]);
+    // Extra keys, per row: the suffix chain and the row itself.
+    {
+      const int c0 = rl0 < n ? item[kItXcnt + rl0] : 0, c1 = rl1 < n ? item[kItXcnt + rl1] : 0;
+      const int o0 = item[kItXoff + rl0], o1 = item[kItXoff + rl1];
+      int emax = max(c0, c1);
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) emax = max(emax, __shfl_xor_sync(0xffffffffu, emax, o));
+      const uint32_t qr0 = qb + g * 128, qr1 = qb + (g + 8) * 128;  // rows rl0, rl1 of the query tile
+      for (int e = 0; e < emax; ++e) {
+#pragma unroll
+        for (int ci = 0; ci < 2; ++ci) {
+          const int cnt = ci ? c1 : c0;
+          int slot = -1, kpos = 0;
+          if (e < cnt) {
+            const int xi = (ci ? o1 : o0) + e;
             slot = st.extra_slot[xi];
-            pos = st.extra_pos[xi];
+            kpos = st.extra_pos[xi];
             if (slot < 0 || slot >= a.g.num_slots) {
               report(st.status, IMBA_ERR_RANGE);
               slot = -1;
-            } else {
-              ow = lo;
             }
           }
-          x_owner[tid] = ow;
-          x_pos[tid] = pos;
-          x_slot[tid] = slot;
+          const bool act = slot >= 0;
+          const bf16* kp = Pool + (act ? a.g.k_off(slot, a.layer, h) : 0);
+          const bf16* vp = Pool + (act ? a.g.v_off(slot, a.layer, h) : 0);
+          if (ci == 0)
+            extra_key(rs.m0, rs.l0, rs.o, 0, act, qr0, g & 7, kp, vp, kpos, qp0, psw, scale2, a.max_pos, t);
+          else
+            extra_key(rs.m1, rs.l1, rs.o, 1, act, qr1, (g + 8) & 7, kp, vp, kpos, qp1, psw, scale2, a.max_pos, t);
         }
-        bar_consumers(nct);
-        gather(x_slot);
       }
     }
 
@@ -668,7 +639,18 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       }
     } else {
       // LayerNorm over the row's H dv outputs (two passes through shared
-      // per-(head, row) partial sums), then the gate by u.
+      // per-(head, row) partial sums), then the gate by u.  The u loads are
+      // issued first so that their latency overlaps the two barriers.
+      float2 uv0[8], uv1[8];
+      {
+        const float2* u0 = reinterpret_cast<const float2*>(prm.u + (size_t)(r0 >= 0 ? r0 : 0) * hdv + h * D + 2 * t);
+        const float2* u1 = reinterpret_cast<const float2*>(prm.u + (size_t)(r1 >= 0 ? r1 : 0) * hdv + h * D + 2 * t);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uv0[j] = r0 >= 0 ? __ldg(u0 + 4 * j) : make_float2(0.f, 0.f);
+          uv1[j] = r1 >= 0 ? __ldg(u1 + 4 * j) : make_float2(0.f, 0.f);
+        }
+      }
       float s0 = 0.f, s1 = 0.f;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -712,22 +694,17 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         v1 += red_sq[k * kHalfRows + rl1];
       }
       const float rs0 = 1.0f / sqrtf(v0 / (float)hdv + 1e-6f), rs1 = 1.0f / sqrtf(v1 / (float)hdv + 1e-6f);
-      // Every u load is issued before the first gated store: the two
-      // pointers may not be proven distinct, and interleaving would turn the
-      // loads into a chain of dependent round trips.
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
         const int r = i ? r1 : r0;
         if (r < 0) continue;
         const float mu = i ? mu1 : mu0, rsd = i ? rs1 : rs0;
-        const float2* ur = reinterpret_cast<const float2*>(prm.u + (size_t)r * hdv + h * D + 2 * t);
-        float2 uv[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) uv[j] = __ldg(ur + 4 * j);
         uint32_t* gr = reinterpret_cast<uint32_t*>(prm.gated + (size_t)r * hdv + h * D + 2 * t);
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          gr[4 * j] = pack_bf16(uv[j].x * ((rs.o[j][2 * i] - mu) * rsd), uv[j].y * ((rs.o[j][2 * i + 1] - mu) * rsd));
+        for (int j = 0; j < 8; ++j) {
+          const float2 uv = i ? uv1[j] : uv0[j];
+          gr[4 * j] = pack_bf16(uv.x * ((rs.o[j][2 * i] - mu) * rsd), uv.y * ((rs.o[j][2 * i + 1] - mu) * rsd));
+        }
       }
     }
     __syncwarp();
@@ -787,11 +764,11 @@ bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& 
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return false;
-  // Shared memory: alignment slack, KV ring, extra-key tile, query tile,
-  // optional fp16 bias table, item buffers and barriers.  The bias table is
+  // Shared memory: alignment slack, KV ring, query tile, optional fp16 bias
+  // table, item buffers and barriers.  The bias table is
   // kept in shared memory when at least 3 ring stages still fit.
   const size_t stage_bytes = 2 * (size_t)hc * kPageBytes;
-  const size_t fixed = 1024 + stage_bytes + (size_t)hc * kHalfRows * 128 + kMetaBytes;
+  const size_t fixed = 1024 + (size_t)hc * kHalfRows * 128 + kMetaBytes;
   const size_t bias_bytes = ((size_t)hc * (2 * md.max_pos - 1) * 2 + 15) / 16 * 16;
   const bool smem_bias = fixed + bias_bytes + 3 * stage_bytes <= kSmemMax;
   size_t stages = (kSmemMax - fixed - (smem_bias ? bias_bytes : 0)) / stage_bytes;
