@@ -62,7 +62,9 @@ constexpr int kItVis = 40;     // [32] visible prefix tokens
 constexpr int kItQpos = 72;    // [32] query positions
 constexpr int kItXoff = 104;   // [32] first extra of the row
 constexpr int kItXcnt = 136;   // [32] extras of the row
-constexpr int kItemInts = 168;
+constexpr int kItX0slot = 168; // [32] pool slot of the row's first extra (-1: none)
+constexpr int kItX0pos = 200;  // [32] its position
+constexpr int kItemInts = 232;
 
 struct PageParams {
   AttnArgs a;
@@ -445,6 +447,19 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       item[kItQpos + lane] = qp;
       item[kItXoff + lane] = e0;
       item[kItXcnt + lane] = cnt;
+      {
+        int slot0 = -1, pos0 = 0;
+        if (cnt > 0) {
+          slot0 = st.extra_slot[e0];
+          pos0 = st.extra_pos[e0];
+          if (slot0 < 0 || slot0 >= a.g.num_slots) {
+            report(st.status, IMBA_ERR_RANGE);
+            slot0 = -1;
+          }
+        }
+        item[kItX0slot + lane] = slot0;
+        item[kItX0pos + lane] = pos0;
+      }
       if (lane == 0) {
         item[kItN] = n;
         item[kItNpg] = npg;
@@ -491,7 +506,17 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
   const int rl0 = 16 * rb + g, rl1 = rl0 + 8;
   if (kSmemBias) {  // fp16 copy of this CTA's ps_w rows (contiguous heads h0 .. h0 + HC - 1)
     const float* src = a.ps_w + (size_t)h0 * bias_w;
-    for (int i = tid; i < HC * bias_w; i += nct) bias_s[i] = __float2half_rn(__ldg(src + i) * kLog2e);
+    const int total = HC * bias_w;
+    // Each thread loads 8 values before converting and storing them, so the
+    // loads of a round are in flight together.
+    for (int base = tid * 8; base < total; base += nct * 8) {
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = base + k < total ? __ldg(src + base + k) : 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (base + k < total) bias_s[base + k] = __float2half_rn(v[k] * kLog2e);
+    }
     // visible to every consumer warp after the first item's barrier
   }
   using Bias = typename std::conditional<kSmemBias, BiasShared, BiasGlobal>::type;
@@ -529,6 +554,17 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       }
     }
     asm volatile("cp.async.commit_group;\n" ::: "memory");
+    // Bring the K / V lines of each row's first extra key (usually the row
+    // itself, written by the preceding projection) into L1 while the pages
+    // stream: lane t of a quad takes (row rl0 | rl1) x (K | V).
+    {
+      const int rl = (t & 1) ? rl1 : rl0;
+      const int slot = rl < n ? item[kItX0slot + rl] : -1;
+      if (slot >= 0) {
+        const bf16* ln = Pool + ((t & 2) ? a.g.v_off(slot, a.layer, h) : a.g.k_off(slot, a.layer, h));
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(ln));
+      }
+    }
     const bool live = 16 * rb < n;
     // Rows past n mirror row 0 (never stored): they keep the fast path and
     // every bias index of a full page in range.
@@ -596,7 +632,13 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         for (int ci = 0; ci < 2; ++ci) {
           const int cnt = ci ? c1 : c0;
           int slot = -1, kpos = 0;
-          if (e < cnt) {
+          if (e == 0) {  // resolved (and range-checked) by the producer
+            const int rl = ci ? rl1 : rl0;
+            if (cnt > 0) {
+              slot = item[kItX0slot + rl];
+              kpos = item[kItX0pos + rl];
+            }
+          } else if (e < cnt) {
             const int xi = (ci ? o1 : o0) + e;
             slot = st.extra_slot[xi];
             kpos = st.extra_pos[xi];
