@@ -466,6 +466,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       }
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&item_full[ib]);
+      // The pages may hold KV written by the preceding projection kernel.
+      pdl_wait();
       // Stream the visible pages through the ring.
       for (int b0 = 0; b0 < npg; b0 += 32) {
         int pg = 0;
@@ -519,6 +521,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     }
     // visible to every consumer warp after the first item's barrier
   }
+  // The bias table (weights) and the producer's first item (host-written step
+  // metadata) overlap the previous kernel; queries, u, the rows' own K / V
+  // and the outputs are ordered after it.
+  pdl_wait();
+  pdl_trigger();
   using Bias = typename std::conditional<kSmemBias, BiasShared, BiasGlobal>::type;
   Bias psw;
   if constexpr (kSmemBias) psw.p = bias_s + (size_t)hl * bias_w;
@@ -829,8 +836,7 @@ bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& 
   PageParams prm{a, num_layers, hc, (int)stages, u, fuse ? gated : nullptr};
   const int ctas = a.st.num_chunks < sms ? a.st.num_chunks : sms;
   dim3 grid(ctas, 1, H / hc);
-  kern<<<grid, (2 * hc + 1) * 32, smem, s>>>(map, prm);
-  *err = cudaGetLastError();
+  *err = launch_pdl(kern, grid, dim3((2 * hc + 1) * 32), smem, s, map, prm);
   *fused = fuse && *err == cudaSuccess;
   return true;
 }

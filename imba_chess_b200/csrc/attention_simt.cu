@@ -30,6 +30,8 @@ __device__ __forceinline__ int bias_index(int kpos, int qpos, int max_pos) {
 
 template <typename T>
 __global__ void __launch_bounds__(128) attn_simt_kernel(AttnArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int c = blockIdx.x, h = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int dqk = a.g.dqk, dv = a.g.dv;
@@ -211,8 +213,7 @@ cudaError_t launch_attn_simt(const AttnArgs& a, cudaStream_t s) {
   cudaError_t e = cudaFuncSetAttribute(attn_simt_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid(a.st.num_chunks, a.g.H);
-  attn_simt_kernel<T><<<grid, 128, smem, s>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(attn_simt_kernel<T>, grid, dim3(128), smem, s, a);
 }
 template cudaError_t launch_attn_simt<float>(const AttnArgs&, cudaStream_t);
 template cudaError_t launch_attn_simt<bf16>(const AttnArgs&, cudaStream_t);

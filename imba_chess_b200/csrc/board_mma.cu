@@ -183,6 +183,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float* fin = params + 2 * IMBA_BOARD_BLOCK_FLOATS;
     for (int i = tid; i < 128; i += kThreads) sP[2 * kBlockP + i] = fin[i];
   }
+  // The weights above are step-invariant; piece ids and the pooled output
+  // are ordered after the previous kernel of the stream.
+  pdl_wait();
+  pdl_trigger();
   __syncthreads();
 
   const int pairs = (rows + kBoardsPerIter - 1) / kBoardsPerIter;
@@ -386,9 +390,8 @@ cudaError_t launch_board_mma(const imba_model_desc& md, const imba_step_desc& st
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int pairs = (st.num_rows + kBoardsPerIter - 1) / kBoardsPerIter;
   const int grid = pairs < sms ? pairs : sms;
-  board_mma_kernel<<<grid, kThreads, kSmemBytes, s>>>(md.piece_square, md.board_params, st.piece_ids, st.num_rows,
-                                                       pooled, st.status);
-  return cudaGetLastError();
+  return launch_pdl(board_mma_kernel, dim3(grid), dim3(kThreads), kSmemBytes, s, md.piece_square, md.board_params,
+                    st.piece_ids, st.num_rows, pooled, st.status);
 }
 
 }  // namespace imba

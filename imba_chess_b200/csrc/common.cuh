@@ -4,6 +4,8 @@
 // legal-move log-softmax, which the reference computes in float64).
 #pragma once
 
+#include <utility>
+
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -26,6 +28,18 @@ __device__ __forceinline__ bf16 from_f<bf16>(float x) { return __float2bfloat16_
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 // SiLU with the fast exponential / division intrinsics (bf16 tensor-core epilogues).
+// Programmatic dependent launch.  Step kernels are launched with
+// launch_pdl(), so a kernel may begin (CTA scheduling, barrier / TMEM set-up,
+// reads of weights and host-written step metadata) while the previous kernel
+// of the stream finishes.  pdl_wait() returns once that kernel has completed
+// and its writes are visible; every step kernel calls it before touching
+// memory that an earlier kernel of the step writes or reads, which keeps the
+// completion order transitive along the stream.  pdl_trigger() lets the next
+// kernel be scheduled.  Both are no-ops for kernels launched without the
+// attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 // x * sigmoid(x) with sigmoid(x) = (1 + tanh(x / 2)) / 2 on the hardware tanh
 // (one MUFU op instead of an exponential and a reciprocal; relative error
@@ -125,5 +139,21 @@ struct Workspace {
 };
 
 Workspace carve_workspace(const imba_model* m, int32_t rows, void* base);
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace imba

@@ -86,6 +86,8 @@ __device__ void linear64(const float* in, int ld_in, const float* __restrict__ W
 }
 
 __global__ void __launch_bounds__(kThreads) embed_kernel(imba_model_desc md, imba_step_desc st, float* x_out) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float sm[];
   float* X = sm;                 // [64][kLd] residual
   float* Hn = X + kSq * kLd;     // [64][kLd] LN output / attention output
@@ -205,8 +207,7 @@ cudaError_t launch_embed(const imba_model_desc& md, const imba_step_desc& st, fl
   const size_t smem = embed_smem_bytes();
   cudaError_t e = cudaFuncSetAttribute(embed_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  embed_kernel<<<st.num_rows, kThreads, smem, s>>>(md, st, x);
-  return cudaGetLastError();
+  return launch_pdl(embed_kernel, dim3(st.num_rows), dim3(kThreads), smem, s, md, st, x);
 }
 
 }  // namespace imba

@@ -13,6 +13,8 @@ constexpr int kBM = 64, kBN = 64, kBK = 16;
 template <typename TA, typename TW, class Epi>
 __global__ void __launch_bounds__(256) gemm_simt_kernel(const TA* __restrict__ A, int lda, const TW* __restrict__ W,
                                                         int ldw, int M, int N, int K, Epi epi) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float As[kBK][kBM + 4];
   __shared__ float Ws[kBK][kBN + 4];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
@@ -67,8 +69,7 @@ cudaError_t launch_gemm_simt(const TA* A, int lda, const TW* W, int ldw, int M, 
                              cudaStream_t s) {
   if (M <= 0 || N <= 0) return cudaSuccess;
   dim3 grid((N + kBN - 1) / kBN, (M + kBM - 1) / kBM);
-  gemm_simt_kernel<TA, TW, Epi><<<grid, 256, 0, s>>>(A, lda, W, ldw, M, N, K, epi);
-  return cudaGetLastError();
+  return launch_pdl(gemm_simt_kernel<TA, TW, Epi>, grid, dim3(256), 0, s, A, lda, W, ldw, M, N, K, epi);
 }
 
 #define IMBA_INST(TA, TW, EPI) \

@@ -90,6 +90,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
+  // Barrier / TMEM set-up and descriptor prefetch overlap the previous
+  // kernel; operand loads and epilogue memory accesses are ordered after it.
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {  // TMA producer
@@ -228,8 +232,7 @@ cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
   const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int sms = sm_count();
   const int grid = tiles < sms ? tiles : sms;
-  kern<<<grid, kGemmThreads, S::kSmem, s>>>(ta, tb, M, N, K, epi, status);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(grid), dim3(kGemmThreads), S::kSmem, s, ta, tb, M, N, K, epi, status);
 }
 
 }  // namespace

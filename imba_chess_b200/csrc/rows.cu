@@ -17,6 +17,8 @@ constexpr int kMaxPerLane = 32;  // supports row widths up to 1024
 
 template <typename TOut>
 __global__ void ln_rows_kernel(const float* __restrict__ x, int rows, int n, float eps, TOut* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= rows) return;
   const float* xr = x + (size_t)warp * n;
@@ -48,6 +50,8 @@ __global__ void ln_rows_kernel(const float* __restrict__ x, int rows, int n, flo
 template <typename TOut>
 __global__ void gate_kernel(const float* __restrict__ attn, const float* __restrict__ u, int rows, int n,
                             TOut* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= rows) return;
   const float* ar = attn + (size_t)warp * n;
@@ -83,6 +87,8 @@ __global__ void gate_kernel(const float* __restrict__ attn, const float* __restr
 template <typename T>
 __global__ void final_ln_kernel(const float* __restrict__ x, int rows, int n, const float* __restrict__ w,
                                 const float* __restrict__ b, float* __restrict__ out32, T* __restrict__ out3) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= rows) return;
   const float* xr = x + (size_t)warp * n;
@@ -156,6 +162,8 @@ __device__ __forceinline__ void row_stats4(const float4 (&v)[kMaxVec], int nv, i
 
 template <typename TOut>
 __global__ void ln_rows4_kernel(const float* __restrict__ x, int rows, int n, float eps, TOut* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= rows) return;
   const int nv = n >> 7;
@@ -176,6 +184,8 @@ __global__ void ln_rows4_kernel(const float* __restrict__ x, int rows, int n, fl
 template <typename TOut>
 __global__ void gate4_kernel(const float* __restrict__ attn, const float* __restrict__ u, int rows, int n,
                              TOut* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= rows) return;
   const int nv = n >> 7;
@@ -201,6 +211,8 @@ __global__ void gate4_kernel(const float* __restrict__ attn, const float* __rest
 template <typename T>
 __global__ void final_ln4_kernel(const float* __restrict__ x, int rows, int n, const float* __restrict__ w,
                                  const float* __restrict__ b, float* __restrict__ out32, T* __restrict__ out3) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= rows) return;
   const int nv = n >> 7;
@@ -234,6 +246,8 @@ __global__ void final_ln4_kernel(const float* __restrict__ x, int rows, int n, c
 // Value output layer + v + legal projection, one warp per row.
 __global__ void value_legal_kernel(imba_model_desc md, imba_step_desc st, const float* __restrict__ hval,
                                    const float* __restrict__ logits) {
+  pdl_wait();
+  pdl_trigger();
   const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (r >= st.num_rows) return;
   if (md.has_value_head) {
@@ -335,10 +349,8 @@ inline int warp_blocks(int rows) { return (rows + 7) / 8; }  // 8 warps per 256-
 template <typename T>
 cudaError_t launch_ln_rows(const float* x, int rows, int n, float eps, T* out, cudaStream_t s) {
   if (n % 128 == 0 && n <= 128 * kMaxVec)
-    ln_rows4_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(x, rows, n, eps, out);
-  else
-    ln_rows_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(x, rows, n, eps, out);
-  return cudaGetLastError();
+    return launch_pdl(ln_rows4_kernel<T>, dim3(warp_blocks(rows)), dim3(256), 0, s, x, rows, n, eps, out);
+  return launch_pdl(ln_rows_kernel<T>, dim3(warp_blocks(rows)), dim3(256), 0, s, x, rows, n, eps, out);
 }
 template cudaError_t launch_ln_rows<float>(const float*, int, int, float, float*, cudaStream_t);
 template cudaError_t launch_ln_rows<bf16>(const float*, int, int, float, bf16*, cudaStream_t);
@@ -346,10 +358,8 @@ template cudaError_t launch_ln_rows<bf16>(const float*, int, int, float, bf16*, 
 template <typename T>
 cudaError_t launch_gate(const float* attn, const float* u, int rows, int n, T* out, cudaStream_t s) {
   if (n % 128 == 0 && n <= 128 * kMaxVec)
-    gate4_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(attn, u, rows, n, out);
-  else
-    gate_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(attn, u, rows, n, out);
-  return cudaGetLastError();
+    return launch_pdl(gate4_kernel<T>, dim3(warp_blocks(rows)), dim3(256), 0, s, attn, u, rows, n, out);
+  return launch_pdl(gate_kernel<T>, dim3(warp_blocks(rows)), dim3(256), 0, s, attn, u, rows, n, out);
 }
 template cudaError_t launch_gate<float>(const float*, const float*, int, int, float*, cudaStream_t);
 template cudaError_t launch_gate<bf16>(const float*, const float*, int, int, bf16*, cudaStream_t);
@@ -358,10 +368,8 @@ template <typename T>
 cudaError_t launch_final_ln(const float* x, int rows, int n, const float* w, const float* b, float* out32, T* out3,
                             cudaStream_t s) {
   if (n % 128 == 0 && n <= 128 * kMaxVec)
-    final_ln4_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(x, rows, n, w, b, out32, out3);
-  else
-    final_ln_kernel<T><<<warp_blocks(rows), 256, 0, s>>>(x, rows, n, w, b, out32, out3);
-  return cudaGetLastError();
+    return launch_pdl(final_ln4_kernel<T>, dim3(warp_blocks(rows)), dim3(256), 0, s, x, rows, n, w, b, out32, out3);
+  return launch_pdl(final_ln_kernel<T>, dim3(warp_blocks(rows)), dim3(256), 0, s, x, rows, n, w, b, out32, out3);
 }
 template cudaError_t launch_final_ln<float>(const float*, int, int, const float*, const float*, float*, float*,
                                             cudaStream_t);
@@ -370,8 +378,7 @@ template cudaError_t launch_final_ln<bf16>(const float*, int, int, const float*,
 
 cudaError_t launch_value_legal(const imba_model_desc& md, const imba_step_desc& st, const float* hval,
                                const float* logits, cudaStream_t s) {
-  value_legal_kernel<<<warp_blocks(st.num_rows), 256, 0, s>>>(md, st, hval, logits);
-  return cudaGetLastError();
+  return launch_pdl(value_legal_kernel, dim3(warp_blocks(st.num_rows)), dim3(256), 0, s, md, st, hval, logits);
 }
 
 template <typename T>
