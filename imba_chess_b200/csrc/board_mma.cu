@@ -4,23 +4,26 @@
 // :275-278).  Output: the pooled 64-vector of every board (fp32); the 64 -> d
 // projection and the side / position embeddings follow in a GEMM epilogue.
 //
-// Persistent CTAs of 8 warps hold both blocks' weights in shared memory
-// (bf16, padded rows) and process two boards per iteration: warp w owns
+// Persistent CTAs of 16 warps hold both blocks' weights in shared memory
+// (bf16, padded rows) and process four boards per iteration: warp w owns
 // squares 16*(w%4) .. +15 of board w/4.  Every product is an
 // mma.sync.m16n8k16 (bf16 in, fp32 accumulate).  The residual stream stays in
 // fp32 registers in the accumulator layout; LayerNorms reduce across the four
 // lanes that share a row; accumulators convert directly into the next
-// product's A fragments.  Per block and head: S = Q K^T / 4 (keys of the own
-// board from shared memory), fp32 softmax, O = P V, then the output
-// projection accumulates straight into the residual; the MLP (64 -> 128 ->
-// 64, SiLU) runs in two 64-wide halves accumulating into the residual too.
+// product's A fragments.  Per block and head: S = Q K^T (queries pre-scaled
+// by log2(e) / 4, keys of the own board from shared memory), fp32 softmax in
+// the log2 domain, O = P V, and the head's 16 output columns go straight
+// through their slice of the output projection into the residual; the MLP
+// (64 -> 128 -> 64, SiLU) runs in two 64-wide halves accumulating into the
+// residual too.  Keeping only one head's state live holds a warp to 128
+// registers, so 16 warps (four boards) share an SM.
 #include "kernels.cuh"
 
 namespace imba {
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kBoardsPerIter = 2;
+constexpr int kThreads = 512;
+constexpr int kBoardsPerIter = 4;
 constexpr int LD64 = 72;    // padded bf16 row stride for 64-wide rows
 constexpr int LD128 = 136;  // padded bf16 row stride for 128-wide rows
 
@@ -79,6 +82,26 @@ __device__ __forceinline__ void gemm_k64(float (&acc)[NT][4], const uint32_t (&a
       mma16816(acc[nt + 1], a[kc], b[2], b[3]);
     }
   }
+}
+
+// acc[nt] += A(16 x 16, one k-chunk) . W[n0 + 8 nt .., kofs .. kofs + 15]^T.
+template <int NT>
+__device__ __forceinline__ void gemm_k16(float (&acc)[NT][4], const uint32_t (&a)[4], const bf16* W, int ld, int n0,
+                                         int kofs, int lane) {
+  const int r = lane & 7, m = lane >> 3;
+#pragma unroll
+  for (int nt = 0; nt < NT; nt += 2) {
+    uint32_t b[4];
+    ldsm_x4(b, W + (size_t)(n0 + 8 * nt + r + 8 * (m >> 1)) * ld + kofs + 8 * (m & 1));
+    mma16816(acc[nt], a, b[0], b[1]);
+    mma16816(acc[nt + 1], a, b[2], b[3]);
+  }
+}
+
+__device__ __forceinline__ float exp2_approx(float x) {  // hardware ex2
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // Accumulator tiles (8 n-tiles = 64 columns) -> bf16 A fragments (4 k-chunks).
@@ -152,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   bf16* sK = sW + 2 * kBlockW;                          // [2 boards][64][72]
   bf16* sV = sK + kKV;
   float* sP = reinterpret_cast<float*>(sV + kKV);       // 2 blocks of fp32 params, then final LN w,b
-  float* sPool = sP + 2 * kBlockP + 128;                // [2 boards][4 warps][64]
+  float* sPool = sP + 2 * kBlockP + 128;                // [kBoardsPerIter boards][4 warps][64]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -229,19 +252,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       uint32_t qa[4][4];
       {
+        // Q, pre-scaled by log2(e) / sqrt(16) so that the scores come out in
+        // the log2 domain; K and V go to the board's shared buffers.
+        constexpr float kQScale = 0.25f * 1.4426950408889634f;
+        // K and V first, so that the Q fragments are live only from here on.
         float acc[8][4];
-        zero(acc);
-        gemm_k64<8>(acc, ha, W + kOffQKV, LD64, 0, 0, lane);
-        to_afrag(acc, qa);
         zero(acc);
         gemm_k64<8>(acc, ha, W + kOffQKV, LD64, 64, 0, lane);
         store_rows(acc, myK, row0, g, t);
         zero(acc);
         gemm_k64<8>(acc, ha, W + kOffQKV, LD64, 128, 0, lane);
         store_rows(acc, myV, row0, g, t);
+        zero(acc);
+        gemm_k64<8>(acc, ha, W + kOffQKV, LD64, 0, 0, lane);
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+          acc[n][0] *= kQScale;
+          acc[n][1] *= kQScale;
+          acc[n][2] *= kQScale;
+          acc[n][3] *= kQScale;
+        }
+        to_afrag(acc, qa);
       }
       __syncthreads();
-      float o[8][4];
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         float s[8][4];
@@ -258,10 +291,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
-          s[n][0] *= 0.25f;
-          s[n][1] *= 0.25f;
-          s[n][2] *= 0.25f;
-          s[n][3] *= 0.25f;
           m0 = fmaxf(m0, fmaxf(s[n][0], s[n][1]));
           m1 = fmaxf(m1, fmaxf(s[n][2], s[n][3]));
         }
@@ -272,10 +301,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         float l0 = 0.f, l1 = 0.f;
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
-          s[n][0] = __expf(s[n][0] - m0);
-          s[n][1] = __expf(s[n][1] - m0);
-          s[n][2] = __expf(s[n][2] - m1);
-          s[n][3] = __expf(s[n][3] - m1);
+          s[n][0] = exp2_approx(s[n][0] - m0);
+          s[n][1] = exp2_approx(s[n][1] - m0);
+          s[n][2] = exp2_approx(s[n][2] - m1);
+          s[n][3] = exp2_approx(s[n][3] - m1);
           l0 += s[n][0] + s[n][1];
           l1 += s[n][2] + s[n][3];
         }
@@ -295,20 +324,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma16816(oh[1], pa[kc], b[2], b[3]);
         }
         const float i0 = __frcp_rn(l0), i1 = __frcp_rn(l1);
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          o[2 * h + j][0] = oh[j][0] * i0;
-          o[2 * h + j][1] = oh[j][1] * i0;
-          o[2 * h + j][2] = oh[j][2] * i1;
-          o[2 * h + j][3] = oh[j][3] * i1;
-        }
+        // The head's output (16 x 16) as one A k-chunk, through its slice of
+        // the output projection into the residual.
+        uint32_t oa[4];
+        oa[0] = pack_bf16(oh[0][0] * i0, oh[0][1] * i0);
+        oa[1] = pack_bf16(oh[0][2] * i1, oh[0][3] * i1);
+        oa[2] = pack_bf16(oh[1][0] * i0, oh[1][1] * i0);
+        oa[3] = pack_bf16(oh[1][2] * i1, oh[1][3] * i1);
+        gemm_k16<8>(x, oa, W + kOffOut, LD64, 0, 16 * h, lane);  // x += o_h . Wout[:, 16h .. 16h+15]^T
       }
       __syncthreads();  // the board's K / V are reused by the next block
-      {
-        uint32_t oa[4][4];
-        to_afrag(o, oa);
-        gemm_k64<8>(x, oa, W + kOffOut, LD64, 0, 0, lane);  // x += attn . Wout^T
-      }
       {
         float y[8][4];
         layer_norm(x, P + 128, P + 192, t, y);
@@ -324,10 +349,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
           const int c = 64 * half + 8 * n + 2 * t;
-          acc[n][0] = silu_fast(acc[n][0] + b1[c]);
-          acc[n][1] = silu_fast(acc[n][1] + b1[c + 1]);
-          acc[n][2] = silu_fast(acc[n][2] + b1[c]);
-          acc[n][3] = silu_fast(acc[n][3] + b1[c + 1]);
+          acc[n][0] = silu_tanh(acc[n][0] + b1[c]);
+          acc[n][1] = silu_tanh(acc[n][1] + b1[c + 1]);
+          acc[n][2] = silu_tanh(acc[n][2] + b1[c]);
+          acc[n][3] = silu_tanh(acc[n][3] + b1[c + 1]);
         }
         uint32_t ma[4][4];
         to_afrag(acc, ma);
