@@ -311,19 +311,22 @@ def algorithmic_work(dims, plan, eb=2):
     prefix_tokens = int(plan.row_vis[np.unique(plan.row_group, return_index=True)[1]].sum()) if R else 0
     kv_tok = H * (dqk + dv) * eb
     extras = int(plan.extra_slot.shape[0])
-    attn_bytes = prefix_tokens * kv_tok + extras * kv_tok + R * H * dqk * eb + R * H * dv * 4
     nl = 0 if plan.legal_ids is None else int(plan.legal_ids.shape[0])
+    # bf16 path: the attention kernel also applies the output norm and the u
+    # gate (reads q, u; writes gated bf16), and without a full-logits request
+    # the legal logits are fp32 gathers in the value / legal pass (policy rows
+    # of the legal ids, mostly served from L2), so those two phases launch
+    # nothing of their own.
+    attn_bytes = prefix_tokens * kv_tok + extras * kv_tok + R * H * dqk * eb + R * H * dv * (4 + eb)
     return {
         "embed": ("tensor", 2.0 * board_mac * R, 1),
         "ln": ("hbm", R * d * (4 + eb), L),
         "uvqk_gemm": ("tensor", 2.0 * R * d * uvqk_n, L),
         "attention": ("hbm", attn_bytes, L),
-        "gate": ("hbm", R * H * dv * (4 + 4 + eb), L),
         "out_gemm": ("tensor", 2.0 * R * H * dv * d, L),
         "final_ln": ("hbm", R * d * (4 + 4 + 2 * eb), 1),
-        "policy_gemm": ("tensor", 2.0 * R * d * V, 1),
         "value_gemm": ("tensor", 2.0 * R * d * (d // 2), 1),
-        "value_legal": ("hbm", R * (d // 2) * 4 + nl * 12 + R * 16, 1),
+        "value_legal": ("hbm", R * (d // 2) * 4 + nl * (d * 4 + 12) + R * (d * 4 + 16), 1),
     }
 
 
@@ -479,7 +482,7 @@ def run_b200(args):
             t_roof_ms += launches * amount / (peak * 1e9) * 1000.0
         kernels[k] = {"bound": bound, "ms_per_step": round(per_step[k], 4), "launches_per_step": launches,
                       "achieved": round(ach, 2), "unit": unit, "frac": round(ach / peak, 4)}
-    dom = max(per_step, key=per_step.get)
+    dom = max(work, key=lambda k: per_step[k])
     dk = kernels[dom]
     bound, amount, launches = work[dom]
     roofline = {

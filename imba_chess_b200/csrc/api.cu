@@ -173,9 +173,11 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
                              bf ? static_cast<T*>(w.xf3) : nullptr, s));
   IMBA_CK(pm.mark(s));
   if (st.hidden) IMBA_CK(cudaMemcpyAsync(st.hidden, w.x, (size_t)R * d * 4, cudaMemcpyDeviceToDevice, s));
-  float* logits = st.logits ? st.logits : w.logits;
-  const bool need_logits = st.logits || st.legal_off;
-  if (need_logits) {
+  // The full policy projection runs only when the caller asks for all
+  // logits; otherwise the legal entries are gathered in the value / legal
+  // pass (exact fp32 dot products).
+  float* logits = st.logits;
+  if (st.logits) {
     if (!gemm_tc_launch_policy(m, R, static_cast<const T*>(w.xf3), EpiStore{logits, md.vocab}, st.status, s, &e)) {
       IMBA_CK(launch_gemm_simt<float, float, EpiStore>(w.xf32, d, md.policy_w32, d, R, md.vocab, d,
                                                        EpiStore{logits, md.vocab}, s));
@@ -197,7 +199,7 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
     }
   }
   IMBA_CK(pm.mark(s));
-  IMBA_CK(launch_value_legal(md, st, w.hval, logits, s));
+  IMBA_CK(launch_value_legal(md, st, w.hval, logits, w.xf32, w.logits, s));
   IMBA_CK(pm.mark(s));
 #undef IMBA_CK
   return IMBA_OK;

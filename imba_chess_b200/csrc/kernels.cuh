@@ -27,8 +27,9 @@ cudaError_t launch_gate(const float* attn, const float* u, int rows, int n, T* o
 template <typename T>
 cudaError_t launch_final_ln(const float* x, int rows, int n, const float* w, const float* b, float* out32, T* out3,
                             cudaStream_t s);
+// logits == nullptr: legal logits as fp32 gathers of x32 . policy_w32[id] (scratch: [R, vocab] floats).
 cudaError_t launch_value_legal(const imba_model_desc& md, const imba_step_desc& st, const float* hval,
-                               const float* logits, cudaStream_t s);
+                               const float* logits, const float* x32, float* scratch, cudaStream_t s);
 template <typename T>
 cudaError_t launch_kv_copy(const PoolGeom& g, T* pool, int layer, int n, const int32_t* slots, T* dk, T* dv,
                            int to_pool, int32_t* status, cudaStream_t s);

@@ -243,9 +243,15 @@ __global__ void final_ln4_kernel(const float* __restrict__ x, int rows, int n, c
     }
 }
 
-// Value output layer + v + legal projection, one warp per row.
+// Value output layer + v + legal projection, one warp per row.  With
+// logits == nullptr the row's legal logits are computed here as exact fp32
+// dot products of the final-LN output x32 with the fp32 policy rows of the
+// legal ids (the reference's _gather_legal_logits,
+// src/imba_chess/eval/actor_server.py:176-203, only reads those entries of
+// the full projection), staged in scratch[r * vocab ..].
 __global__ void value_legal_kernel(imba_model_desc md, imba_step_desc st, const float* __restrict__ hval,
-                                   const float* __restrict__ logits) {
+                                   const float* __restrict__ logits, const float* __restrict__ x32,
+                                   float* __restrict__ scratch) {
   pdl_wait();
   pdl_trigger();
   const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -288,32 +294,87 @@ __global__ void value_legal_kernel(imba_model_desc md, imba_step_desc st, const 
     if (lane == 0) report(st.status, IMBA_ERR_RANGE);
     return;
   }
+  const bool gather = logits == nullptr;
+  float* sr = scratch + (size_t)r * md.vocab;  // gather mode: legal logit of entry i at sr[i - a]
+  if (gather) {
+    const int d = md.model_dim;
+    const float* xr = x32 + (size_t)r * d;
+    const float* W = md.policy_w32;
+    const bool vec = (d & 127) == 0 && d <= 128 * kMaxVec;
+    float4 xv[kMaxVec];
+#pragma unroll
+    for (int k = 0; k < kMaxVec; ++k)
+      xv[k] = vec && 128 * k < d ? *reinterpret_cast<const float4*>(xr + 128 * k + 4 * lane) : make_float4(0, 0, 0, 0);
+    for (int base = a; base < b; base += 4) {  // four legal ids per round, their loads in flight together
+      const float* wr[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        wr[q] = nullptr;
+        if (base + q < b) {
+          int id = st.legal_ids[base + q];
+          if (id < 0 || id >= md.vocab) {
+            if (lane == 0) report(st.status, IMBA_ERR_RANGE);
+            id = 0;
+          }
+          wr[q] = W + (size_t)id * d;
+        }
+      }
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      if (vec) {
+#pragma unroll
+        for (int k = 0; k < kMaxVec; ++k) {
+          if (128 * k >= d) break;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (!wr[q]) continue;
+            const float4 w = __ldg(reinterpret_cast<const float4*>(wr[q] + 128 * k + 4 * lane));
+            acc[q] = fmaf(xv[k].x, w.x, fmaf(xv[k].y, w.y, fmaf(xv[k].z, w.z, fmaf(xv[k].w, w.w, acc[q]))));
+          }
+        }
+      } else {
+        for (int c = lane; c < d; c += 32) {
+          const float xc = xr[c];
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (wr[q]) acc[q] = fmaf(xc, __ldg(wr[q] + c), acc[q]);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[q] = warp_sum(acc[q]);
+      if (lane == 0) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (base + q >= b) break;
+          sr[base + q - a] = acc[q];
+          if (st.legal_logits) st.legal_logits[base + q] = acc[q];
+        }
+      }
+    }
+    __syncwarp();
+  }
   const float* lr = logits + (size_t)r * md.vocab;
+  auto legal_logit = [&](int i) -> float {
+    if (gather) return sr[i - a];
+    int id = st.legal_ids[i];
+    id = (id < 0 || id >= md.vocab) ? 0 : id;
+    return lr[id];
+  };
   float mx = -INFINITY;
   for (int i = a + lane; i < b; i += 32) {
-    int id = st.legal_ids[i];
-    if (id < 0 || id >= md.vocab) {
-      report(st.status, IMBA_ERR_RANGE);
-      id = 0;
+    if (!gather) {
+      const int id = st.legal_ids[i];
+      if (id < 0 || id >= md.vocab) report(st.status, IMBA_ERR_RANGE);
     }
-    const float v = lr[id];
-    if (st.legal_logits) st.legal_logits[i] = v;
+    const float v = legal_logit(i);
+    if (st.legal_logits && !gather) st.legal_logits[i] = v;
     mx = fmaxf(mx, v);
   }
   mx = warp_max(mx);
   if (!st.legal_logprob || b == a) return;
   double se = 0.0;
-  for (int i = a + lane; i < b; i += 32) {
-    int id = st.legal_ids[i];
-    id = (id < 0 || id >= md.vocab) ? 0 : id;
-    se += exp((double)lr[id] - (double)mx);
-  }
+  for (int i = a + lane; i < b; i += 32) se += exp((double)legal_logit(i) - (double)mx);
   const double lse = log(warp_sum_d(se));
-  for (int i = a + lane; i < b; i += 32) {
-    int id = st.legal_ids[i];
-    id = (id < 0 || id >= md.vocab) ? 0 : id;
-    st.legal_logprob[i] = (float)(((double)lr[id] - (double)mx) - lse);
-  }
+  for (int i = a + lane; i < b; i += 32) st.legal_logprob[i] = (float)(((double)legal_logit(i) - (double)mx) - lse);
 }
 
 template <typename T>
@@ -377,8 +438,9 @@ template cudaError_t launch_final_ln<bf16>(const float*, int, int, const float*,
                                            cudaStream_t);
 
 cudaError_t launch_value_legal(const imba_model_desc& md, const imba_step_desc& st, const float* hval,
-                               const float* logits, cudaStream_t s) {
-  return launch_pdl(value_legal_kernel, dim3(warp_blocks(st.num_rows)), dim3(256), 0, s, md, st, hval, logits);
+                               const float* logits, const float* x32, float* scratch, cudaStream_t s) {
+  return launch_pdl(value_legal_kernel, dim3(warp_blocks(st.num_rows)), dim3(256), 0, s, md, st, hval, logits, x32,
+                    scratch);
 }
 
 template <typename T>
