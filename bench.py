@@ -569,9 +569,10 @@ def run_b200(args):
 
 
 def count_launches(dims, plan):
-    """Kernel launches of one step: embed, L x (LN, uvqk, attention, gate,
-    out), final LN, policy, value GEMM, value/legal."""
-    return 1 + 5 * dims.num_layers + 4
+    """Kernel launches of one bf16 wave step (legal logits only): board
+    encoder, content projection GEMM, L x (input LN, uvqk GEMM, attention with
+    the fused norm / gate, output GEMM), final LN, value GEMM, value / legal."""
+    return 2 + 4 * dims.num_layers + 3
 
 
 def service_api(args, dims, wave, sd, device):
