@@ -25,6 +25,29 @@ __device__ __forceinline__ void store32(bf16* dst, const float (&v)[32]) {
   for (int i = 0; i < 4; ++i) d[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
 }
 
+// Staged epilogues (kStaged): the tensor-core GEMM hands each epilogue warp
+// a 32 x 32 accumulator chunk (rows row0 .. row0 + 31, columns c0 .. c0 + 31)
+// in shared memory, element (r, c) at s[r * 32 + (c ^ r)] (conflict-free for
+// both the row-per-lane writes and the reads below), plus one per-row tag.
+// Lane l takes columns 4 (l & 7) .. +3 of rows (l >> 3) + 4 k, k = 0..7, so
+// the eight lanes of a row group write one row's 32 columns contiguously:
+// one or two full lines per row instead of eight 16-byte pieces from eight
+// different rows per instruction.
+__device__ __forceinline__ float4 staged4(const float* s, int r, int c4) {
+  return make_float4(s[r * 32 + ((c4) ^ r)], s[r * 32 + ((c4 + 1) ^ r)], s[r * 32 + ((c4 + 2) ^ r)],
+                     s[r * 32 + ((c4 + 3) ^ r)]);
+}
+__device__ __forceinline__ void put4(float* p, float a, float b, float c, float d) {
+  *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
+}
+__device__ __forceinline__ void put4(bf16* p, float a, float b, float c, float d) {
+  __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+  uint2 v;
+  v.x = *reinterpret_cast<uint32_t*>(&lo);
+  v.y = *reinterpret_cast<uint32_t*>(&hi);
+  *reinterpret_cast<uint2*>(p) = v;
+}
+
 // uvqk projection epilogue: SiLU, then the reference's split order u | v | q | k
 // (src/imba_chess/model/hstu_attention.py:310-325).  u goes to the fp32 gate
 // buffer, q to the query buffer, and k / v straight into the row's slot of the
@@ -76,6 +99,48 @@ struct EpiUVQK {
   };
   __device__ __forceinline__ Ctx begin(int r, int /*n0*/, int /*bn*/) const { return Ctx{(int64_t)dst_slot[r]}; }
 
+  // Per-thread rows measured faster than the staged chunk for this epilogue
+  // (its stores are 64-128 B per row and chunk; the staging round trip and
+  // the per-row slot lookups cost more than they save).
+  static constexpr bool kStaged = false;
+  __device__ __forceinline__ int row_tag(int r) const { return dst_slot[r]; }
+  // Staged chunk (see staged4); tags[rr] = KV slot of row row0 + rr.  A chunk
+  // never straddles a head or a region (d_qk, d_v multiples of 32).
+  __device__ __forceinline__ void tile32(const float* s, const int* tags, int row0, int c0, int M, int N,
+                                         int lane) const {
+    if (c0 >= N) return;
+    const int cg = 4 * (lane & 7), r4 = lane >> 3;
+    const int hdv = g.H * g.dv, hdq = g.H * g.dqk;
+    const int region = c0 < hdv ? 0 : (c0 < 2 * hdv ? 1 : (c0 < 2 * hdv + hdq ? 2 : 3));
+#pragma unroll 2
+    for (int k = 0; k < 8; ++k) {
+      const int rr = r4 + 4 * k, row = row0 + rr;
+      if (row >= M) continue;
+      const float4 a = staged4(s, rr, cg);
+      const float y0 = silu_tanh(a.x), y1 = silu_tanh(a.y), y2 = silu_tanh(a.z), y3 = silu_tanh(a.w);
+      if (region == 0) {
+        put4(u + (size_t)row * hdv + c0 + cg, y0, y1, y2, y3);
+      } else if (region == 2) {
+        put4(q + (size_t)row * hdq + (c0 - 2 * hdv) + cg, y0, y1, y2, y3);
+      } else {
+        const int64_t slot = tags[rr];
+        if (slot < 0 || slot >= g.num_slots) {
+          report(status, IMBA_ERR_RANGE);
+          continue;
+        }
+        T* dst;
+        if (region == 1) {
+          const int c = c0 - hdv;
+          dst = pool + g.v_off(slot, layer, c / g.dv) + (c % g.dv) + cg;
+        } else {
+          const int c = c0 - 2 * hdv - hdq;
+          dst = pool + g.k_off(slot, layer, c / g.dqk) + (c % g.dqk) + cg;
+        }
+        put4(dst, y0, y1, y2, y3);
+      }
+    }
+  }
+
   // 32 consecutive columns starting at c0 (a multiple of 32; d_qk and d_v
   // are multiples of 32, so a chunk never straddles a head or a region).
   __device__ __forceinline__ void chunk32(const Ctx& cx, int r, int c0, int N, const float (&a)[32]) const {
@@ -124,6 +189,34 @@ struct EpiResidual {
       asm volatile("prefetch.global.L1 [%0];" ::"l"(p + c));
     return Ctx{};
   }
+  static constexpr bool kStaged = true;
+  __device__ __forceinline__ int row_tag(int) const { return 0; }
+  // Staged chunk (see staged4): all residual and bias loads are issued
+  // before any store (the compiler cannot prove x and bias do not alias).
+  __device__ __forceinline__ void tile32(const float* s, const int*, int row0, int c0, int M, int N,
+                                         int lane) const {
+    if (c0 >= N) return;
+    const int cg = 4 * (lane & 7), r4 = lane >> 3;
+    const float4 b = __ldg(reinterpret_cast<const float4*>(bias + c0 + cg));
+    float* xc = x + (size_t)(row0 + r4) * ld + c0 + cg;  // row r4 of the chunk; rows step by 4
+#pragma unroll 1
+    for (int k0 = 0; k0 < 8; k0 += 4) {  // two batches of four rows (bounded register use)
+      float4 xv[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int row = row0 + r4 + 4 * (k0 + k);
+        xv[k] = row < M ? *reinterpret_cast<const float4*>(xc + (size_t)(4 * (k0 + k)) * ld) : make_float4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int rr = r4 + 4 * (k0 + k), row = row0 + rr;
+        if (row >= M) continue;
+        const float4 a = staged4(s, rr, cg);
+        put4(xc + (size_t)(4 * (k0 + k)) * ld, (a.x + b.x) + xv[k].x, (a.y + b.y) + xv[k].y, (a.z + b.z) + xv[k].z,
+             (a.w + b.w) + xv[k].w);
+      }
+    }
+  }
   // All loads are issued before any store: interleaving each load after the
   // previous store of the same row serialises them (the compiler cannot prove
   // x and bias do not alias) and was measured ~30x slower.
@@ -150,6 +243,7 @@ struct EpiResidual {
 };
 
 struct EpiStore {
+  static constexpr bool kStaged = false;
   float* out;
   int ld;
   __device__ __forceinline__ void operator()(int r, int c, float acc) const { out[(size_t)r * ld + c] = acc; }
@@ -180,6 +274,7 @@ struct EpiAccumulate {
 
 // Value-head hidden layer: SiLU(acc + bias)   (hstu_model.py:252-257)
 struct EpiBiasSilu {
+  static constexpr bool kStaged = false;
   float* out;
   const float* bias;
   int ld;

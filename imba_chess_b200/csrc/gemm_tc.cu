@@ -31,14 +31,18 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 
-template <int BN, int STAGES>
+constexpr int kEpiWarps = 8;
+// Staged epilogues: per epilogue warp a swizzled fp32 32 x 32 chunk plus 32
+// per-row tags.
+constexpr size_t kStageFloats = 32 * 32 + 32;
+
+template <int BN, int STAGES, bool STAGED>
 struct TileShape {
   static constexpr uint32_t kABytes = kBM * kBK * 2;
   static constexpr uint32_t kBBytes = BN * kBK * 2;
-  static constexpr size_t kSmem = 1024 + STAGES * (kABytes + kBBytes) + (2 * STAGES + 4) * 8 + 16;
+  static constexpr size_t kSmem =
+      1024 + STAGES * (kABytes + kBBytes) + (2 * STAGES + 4) * 8 + 16 + (STAGED ? kEpiWarps * kStageFloats * 4 : 0);
 };
-
-constexpr int kEpiWarps = 8;
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;  // producer warp, MMA warp, 8 epilogue warps
 
 // Persistent, warp-specialised: CTA b handles tiles b, b + gridDim.x, ...
@@ -50,7 +54,7 @@ template <int BN, int STAGES, class Epi>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
                    int K, Epi epi, int32_t* status) {
-  using S = TileShape<BN, STAGES>;
+  using S = TileShape<BN, STAGES, Epi::kStaged>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -60,6 +64,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  float* staging = reinterpret_cast<float*>(tmem_slot + 4);  // kEpiWarps x kStageFloats (staged epilogues)
   __shared__ int abort_flag;
   volatile int* abort = &abort_flag;
 
@@ -149,13 +154,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc::fence_after_sync();
       const int m0 = (tile % mt) * kBM, n0 = (tile / mt) * BN;
       const int row = m0 + quad * 32 + lane;
-      typename Epi::Ctx cx{};
-      if (row < M) cx = epi.begin(row, n0 + c_lo, BN / 2);
+      if constexpr (Epi::kStaged) {
+        // TMEM -> registers (thread = row) -> swizzled shared chunk -> rows
+        // written by groups of eight lanes.
+        float* stg = staging + (size_t)(warp - 2) * kStageFloats;
+        int* tags = reinterpret_cast<int*>(stg + 32 * 32);
+        tags[lane] = row < M ? epi.row_tag(row) : 0;
 #pragma unroll 1
-      for (int c = c_lo; c < c_lo + BN / 2; c += 32) {
-        float v[32];
-        tc::tmem_ld32(tmem + b * BN + lane_base + c, v);
-        if (row < M && n0 + c < N) epi.chunk32(cx, row, n0 + c, N, v);
+        for (int c = c_lo; c < c_lo + BN / 2; c += 32) {
+          float v[32];
+          tc::tmem_ld32(tmem + b * BN + lane_base + c, v);
+#pragma unroll
+          for (int k = 0; k < 32; ++k) stg[lane * 32 + (k ^ lane)] = v[k];
+          __syncwarp();
+          epi.tile32(stg, tags, m0 + quad * 32, n0 + c, M, N, lane);
+          __syncwarp();
+        }
+      } else {
+        typename Epi::Ctx cx{};
+        if (row < M) cx = epi.begin(row, n0 + c_lo, BN / 2);
+#pragma unroll 1
+        for (int c = c_lo; c < c_lo + BN / 2; c += 32) {
+          float v[32];
+          tc::tmem_ld32(tmem + b * BN + lane_base + c, v);
+          if (row < M && n0 + c < N) epi.chunk32(cx, row, n0 + c, N, v);
+        }
       }
       tc::fence_before_sync();
       __syncwarp();
@@ -225,7 +248,7 @@ template <int BN, class Epi>
 cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const Epi& epi, int32_t* status,
                    cudaStream_t s) {
   constexpr int kSt = BN == 256 ? 4 : 6;
-  using S = TileShape<BN, kSt>;
+  using S = TileShape<BN, kSt, Epi::kStaged>;
   auto kern = gemm_tc_kernel<BN, kSt, Epi>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::kSmem);
   if (e != cudaSuccess) return e;
