@@ -87,3 +87,34 @@ def test_tensor_core_kernel_matches_simt(component, dims, parents, monkeypatch):
     assert float((a["hidden"] - b["hidden"]).abs().max()) <= th * scale
     assert float((a["logits"] - b["logits"]).abs().max()) <= tl
     assert float((a["value_logits"] - b["value_logits"]).abs().max()) <= tv
+
+
+def test_attention_result_independent_of_chunking():
+    """The C ABI accepts chunks of up to 64 rows; the planner emits <= 32-row
+    chunks (one attention work item).  Re-chunking the same steps into 64-row
+    and 16-row chunks must give bit-identical results (each row's attention
+    depends only on its own keys; a 64-row chunk is processed as two items)."""
+    from imba_chess_b200.plan import build_chunks
+
+    dims = synth.D256
+    sd = synth.make_state_dict(dims, 5, profile="reference")
+    # groups of 30-60 siblings, so 64-row chunks hold two work items
+    wave = synth.grouped_wave(dims, n_parents=4, plies=(20, 140), siblings=(30, 60), seed=17)
+    outs = []
+    for max_rows in (32, 64, 16):
+        model = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
+        orig = build_chunks
+
+        def rechunk(row_group, num_groups, max_rows_=32, row_vis=None, _m=max_rows):
+            return orig(row_group, num_groups, max_rows=_m, row_vis=row_vis)
+
+        import imba_chess_b200.plan as plan_mod
+
+        plan_mod.build_chunks = rechunk
+        try:
+            outs.append(_run_wave(model, dims, wave))
+        finally:
+            plan_mod.build_chunks = orig
+    for o in outs[1:]:
+        for k in ("hidden", "logits", "value_logits"):
+            assert torch.equal(o[k], outs[0][k]), k
