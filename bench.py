@@ -317,7 +317,7 @@ def algorithmic_work(dims, plan, eb=2):
     # the legal logits are fp32 gathers in the value / legal pass (policy rows
     # of the legal ids, mostly served from L2), so those two phases launch
     # nothing of their own.
-    attn_bytes = prefix_tokens * kv_tok + extras * kv_tok + R * H * dqk * eb + R * H * dv * (4 + eb)
+    attn_bytes = prefix_tokens * kv_tok + extras * kv_tok + R * H * dqk * eb + R * H * dv * (eb + eb)
     return {
         "embed": ("tensor", 2.0 * board_mac * R, 1),
         "ln": ("hbm", R * d * (4 + eb), L),

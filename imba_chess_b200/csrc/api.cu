@@ -36,7 +36,7 @@ size_t workspace_layout(const imba_model* m, int32_t rows, void* base, Workspace
   Workspace w{};
   w.x = static_cast<float*>(take(R * d.model_dim * 4));
   w.xn = take(R * d.model_dim * eb);
-  w.u = static_cast<float*>(take(R * hdv * 4));
+  w.u = take(R * hdv * eb);
   w.q = take(R * hdq * eb);
   w.attn = static_cast<float*>(take(R * hdv * 4));
   w.gated = take(R * hdv * eb);
@@ -139,7 +139,7 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
   for (int l = 0; l < md.num_layers; ++l) {
     IMBA_CK(launch_ln_rows<T>(w.x, R, d, 1e-6f, static_cast<T*>(w.xn), s));
     IMBA_CK(pm.mark(s));
-    EpiUVQK<T> epi{w.u, static_cast<T*>(w.q), poolp, st.row_dst_slot, g, l, st.status};
+    EpiUVQK<T> epi{static_cast<T*>(w.u), static_cast<T*>(w.q), poolp, st.row_dst_slot, g, l, st.status};
     if (!gemm_tc_launch_uvqk(m, l, R, static_cast<const T*>(w.xn), epi, s, &e)) {
       IMBA_CK(launch_gemm_simt<T, T, EpiUVQK<T>>(static_cast<const T*>(w.xn), d,
                                                 static_cast<const T*>(md.uvqk_w[l]), d, R, m->uvqk_n, d, epi, s));
@@ -151,13 +151,14 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
                 w.counters + l * kCountersPerLayer};
     bool fused = false;
     bf16* gated_bf = std::is_same<T, bf16>::value ? reinterpret_cast<bf16*>(w.gated) : nullptr;
-    if (m->simt_attn || !launch_attn_page(aa, md.num_layers, md, pool.num_pages, w.u, gated_bf, s, &e, &fused)) {
+    if (m->simt_attn || !launch_attn_page(aa, md.num_layers, md, pool.num_pages, static_cast<const bf16*>(w.u),
+                                          gated_bf, s, &e, &fused)) {
       IMBA_CK(launch_attn_simt<T>(aa, s));
     } else if (e != cudaSuccess) {
       return IMBA_ERR_CUDA;
     }
     IMBA_CK(pm.mark(s));
-    if (!fused) IMBA_CK(launch_gate<T>(w.attn, w.u, R, hdv, static_cast<T*>(w.gated), s));
+    if (!fused) IMBA_CK(launch_gate<T>(w.attn, static_cast<const T*>(w.u), R, hdv, static_cast<T*>(w.gated), s));
     IMBA_CK(pm.mark(s));
     EpiResidual er{w.x, md.o_b[l], d};
     if (!gemm_tc_launch_out(m, l, R, static_cast<const T*>(w.gated), er, st.status, s, &e)) {

@@ -71,7 +71,7 @@ struct PageParams {
   int num_layers;
   int hc;         // heads per CTA
   int stages;
-  const float* u; // [R, H dv] fp32
+  const bf16* u;  // [R, H dv]
   bf16* gated;    // [R, H dv]: fused norm + gate output (nullptr: store fp32 O to a.out)
 };
 
@@ -690,14 +690,14 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       // LayerNorm over the row's H dv outputs (two passes through shared
       // per-(head, row) partial sums), then the gate by u.  The u loads are
       // issued first so that their latency overlaps the two barriers.
-      float2 uv0[8], uv1[8];
+      uint32_t uv0[8], uv1[8];  // bf16 pairs
       {
-        const float2* u0 = reinterpret_cast<const float2*>(prm.u + (size_t)(r0 >= 0 ? r0 : 0) * hdv + h * D + 2 * t);
-        const float2* u1 = reinterpret_cast<const float2*>(prm.u + (size_t)(r1 >= 0 ? r1 : 0) * hdv + h * D + 2 * t);
+        const uint32_t* u0 = reinterpret_cast<const uint32_t*>(prm.u + (size_t)(r0 >= 0 ? r0 : 0) * hdv + h * D + 2 * t);
+        const uint32_t* u1 = reinterpret_cast<const uint32_t*>(prm.u + (size_t)(r1 >= 0 ? r1 : 0) * hdv + h * D + 2 * t);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          uv0[j] = r0 >= 0 ? __ldg(u0 + 4 * j) : make_float2(0.f, 0.f);
-          uv1[j] = r1 >= 0 ? __ldg(u1 + 4 * j) : make_float2(0.f, 0.f);
+          uv0[j] = r0 >= 0 ? __ldg(u0 + 4 * j) : 0u;
+          uv1[j] = r1 >= 0 ? __ldg(u1 + 4 * j) : 0u;
         }
       }
       float s0 = 0.f, s1 = 0.f;
@@ -751,7 +751,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         uint32_t* gr = reinterpret_cast<uint32_t*>(prm.gated + (size_t)r * hdv + h * D + 2 * t);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float2 uv = i ? uv1[j] : uv0[j];
+          const uint32_t uw = i ? uv1[j] : uv0[j];
+          const float2 uv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&uw));
           gr[4 * j] = pack_bf16(uv.x * ((rs.o[j][2 * i] - mu) * rsd), uv.y * ((rs.o[j][2 * i + 1] - mu) * rsd));
         }
       }
@@ -785,7 +786,7 @@ EncodeTiledFn encode_fn() {
 // kernel.  *fused is set when the norm + gate was done in the epilogue (the
 // caller then skips its gate pass).  a.counters[0 .. H / hc) must be zero.
 bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& md, int64_t num_pages,
-                      const float* u, bf16* gated, cudaStream_t s, cudaError_t* err, bool* fused) {
+                      const bf16* u, bf16* gated, cudaStream_t s, cudaError_t* err, bool* fused) {
   *fused = false;
   if (md.dtype != IMBA_DTYPE_BF16 || md.attention_dim != 64 || md.linear_dim != 64) return false;
   const int H = md.num_heads;

@@ -125,7 +125,7 @@ constexpr int kNumCounters = IMBA_MAX_LAYERS * kCountersPerLayer;
 struct Workspace {
   float* x;        // [R, d]      residual stream
   void* xn;        // [R, d]      LN(x), model dtype
-  float* u;        // [R, H dv]   gate (post-SiLU u)
+  void* u;         // [R, H dv]   gate (post-SiLU u), model dtype
   void* q;         // [R, H dqk]  queries, model dtype
   float* attn;     // [R, H dv]   attention output
   void* gated;     // [R, H dv]   LN(attn) * u, model dtype

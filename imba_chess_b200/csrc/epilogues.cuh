@@ -54,7 +54,7 @@ __device__ __forceinline__ void put4(bf16* p, float a, float b, float c, float d
 // paged KV pool (the KV append, fused).
 template <typename T>
 struct EpiUVQK {
-  float* u;
+  T* u;
   T* q;
   T* pool;
   const int32_t* dst_slot;
@@ -66,7 +66,7 @@ struct EpiUVQK {
     const float y = silu_f(acc);
     const int hdv = g.H * g.dv, hdq = g.H * g.dqk;
     if (c < hdv) {
-      u[(size_t)r * hdv + c] = y;
+      u[(size_t)r * hdv + c] = from_f<T>(y);
       return;
     }
     c -= hdv;

@@ -7,10 +7,10 @@
 // ring guarded by full / empty mbarriers.  Warp 0 (one thread) issues the TMA
 // copies, warp 1 (one thread) issues tcgen05.mma (M = 128, N = BN, K = 16 per
 // instruction) into one of two TMEM accumulators and releases each stage with
-// tcgen05.commit; eight epilogue warps read the other accumulator back (TMEM
-// lane quadrant = warp % 4 = tile rows; two warps per quadrant, one per
-// column half) and hand 32-column chunks to the epilogue functor, so tile i's
-// epilogue overlaps tile i + 1's main loop.
+// tcgen05.commit; 8 or 16 epilogue warps read the other accumulator back
+// (TMEM lane quadrant = warp % 4 = tile rows; two or four warps per quadrant,
+// one column slice each) and hand 32-column chunks to the epilogue functor,
+// so tile i's epilogue overlaps tile i + 1's main loop.
 // Out-of-range rows / columns of A / W are zero-filled by TMA and skipped by
 // the epilogue.
 //
@@ -31,7 +31,13 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 
-constexpr int kEpiWarps = 8;
+// Epilogue warps: 8 (two per TMEM lane quadrant, one column half each).  16
+// warps measured no faster for the per-thread epilogues (their limit is the
+// SM's store path, not latency).
+template <bool STAGED>
+__host__ __device__ constexpr int epi_warps() { return 8; }
+template <bool STAGED>
+__host__ __device__ constexpr int gemm_threads() { return 64 + 32 * epi_warps<STAGED>(); }
 // Staged epilogues: per epilogue warp a swizzled fp32 32 x 32 chunk plus 32
 // per-row tags.
 constexpr size_t kStageFloats = 32 * 32 + 32;
@@ -40,21 +46,24 @@ template <int BN, int STAGES, bool STAGED>
 struct TileShape {
   static constexpr uint32_t kABytes = kBM * kBK * 2;
   static constexpr uint32_t kBBytes = BN * kBK * 2;
-  static constexpr size_t kSmem =
-      1024 + STAGES * (kABytes + kBBytes) + (2 * STAGES + 4) * 8 + 16 + (STAGED ? kEpiWarps * kStageFloats * 4 : 0);
+  static constexpr size_t kSmem = 1024 + STAGES * (kABytes + kBBytes) + (2 * STAGES + 4) * 8 + 16 +
+                                  (STAGED ? epi_warps<STAGED>() * kStageFloats * 4 : 0);
 };
-constexpr int kGemmThreads = 64 + 32 * kEpiWarps;  // producer warp, MMA warp, 8 epilogue warps
 
 // Persistent, warp-specialised: CTA b handles tiles b, b + gridDim.x, ...
 // (tile t -> m-tile t % mt, n-tile t / mt).  Warp 0 streams A / W tiles
 // through the smem ring; warp 1 issues the MMAs of tile i into TMEM buffer
-// i % 2 (2 x BN columns) and signals acc_full; warps 2..9 drain buffer i % 2
+// i % 2 (2 x BN columns) and signals acc_full; the epilogue warps drain buffer i % 2
 // while tile i + 1 is being loaded and multiplied, then signal acc_empty.
 template <int BN, int STAGES, class Epi>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(gemm_threads<Epi::kStaged>(), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
                    int K, Epi epi, int32_t* status) {
   using S = TileShape<BN, STAGES, Epi::kStaged>;
+  constexpr int kEpiWarps = epi_warps<Epi::kStaged>();
+  constexpr int kColGroups = kEpiWarps / 4;  // warps per TMEM lane quadrant
+  constexpr int kCols = BN / kColGroups;      // columns per epilogue warp
+  static_assert(kCols % 32 == 0, "epilogue column slice must be a multiple of 32");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -143,7 +152,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {  // epilogue warps: two per TMEM lane quadrant, one per column half
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
-    const int c_lo = (warp - 2) >= 4 ? BN / 2 : 0;
+    const int c_lo = ((warp - 2) >> 2) * kCols;  // kColGroups warps per quadrant, one slice each
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     int i = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++i) {
@@ -161,7 +170,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int* tags = reinterpret_cast<int*>(stg + 32 * 32);
         tags[lane] = row < M ? epi.row_tag(row) : 0;
 #pragma unroll 1
-        for (int c = c_lo; c < c_lo + BN / 2; c += 32) {
+        for (int c = c_lo; c < c_lo + kCols; c += 32) {
           float v[32];
           tc::tmem_ld32(tmem + b * BN + lane_base + c, v);
 #pragma unroll
@@ -172,9 +181,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       } else {
         typename Epi::Ctx cx{};
-        if (row < M) cx = epi.begin(row, n0 + c_lo, BN / 2);
+        if (row < M) cx = epi.begin(row, n0 + c_lo, kCols);
 #pragma unroll 1
-        for (int c = c_lo; c < c_lo + BN / 2; c += 32) {
+        for (int c = c_lo; c < c_lo + kCols; c += 32) {
           float v[32];
           tc::tmem_ld32(tmem + b * BN + lane_base + c, v);
           if (row < M && n0 + c < N) epi.chunk32(cx, row, n0 + c, N, v);
@@ -255,7 +264,7 @@ cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
   const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int sms = sm_count();
   const int grid = tiles < sms ? tiles : sms;
-  return launch_pdl(kern, dim3(grid), dim3(kGemmThreads), S::kSmem, s, ta, tb, M, N, K, epi, status);
+  return launch_pdl(kern, dim3(grid), dim3(gemm_threads<Epi::kStaged>()), S::kSmem, s, ta, tb, M, N, K, epi, status);
 }
 
 }  // namespace

@@ -23,7 +23,7 @@ cudaError_t launch_board_mma(const imba_model_desc& md, const imba_step_desc& st
 template <typename T>
 cudaError_t launch_ln_rows(const float* x, int rows, int n, float eps, T* out, cudaStream_t s);
 template <typename T>
-cudaError_t launch_gate(const float* attn, const float* u, int rows, int n, T* out, cudaStream_t s);
+cudaError_t launch_gate(const float* attn, const T* u, int rows, int n, T* out, cudaStream_t s);
 template <typename T>
 cudaError_t launch_final_ln(const float* x, int rows, int n, const float* w, const float* b, float* out32, T* out3,
                             cudaStream_t s);
@@ -42,6 +42,6 @@ cudaError_t launch_attn_simt(const AttnArgs& a, cudaStream_t s);
 // apply.  With every head in one CTA it also applies the attention-output
 // norm and the u gate, writes `gated` and sets *fused.
 bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& md, int64_t num_pages,
-                      const float* u, bf16* gated, cudaStream_t s, cudaError_t* err, bool* fused);
+                      const bf16* u, bf16* gated, cudaStream_t s, cudaError_t* err, bool* fused);
 
 }  // namespace imba

@@ -48,14 +48,14 @@ __global__ void ln_rows_kernel(const float* __restrict__ x, int rows, int n, flo
 }
 
 template <typename TOut>
-__global__ void gate_kernel(const float* __restrict__ attn, const float* __restrict__ u, int rows, int n,
+__global__ void gate_kernel(const float* __restrict__ attn, const TOut* __restrict__ u, int rows, int n,
                             TOut* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= rows) return;
   const float* ar = attn + (size_t)warp * n;
-  const float* ur = u + (size_t)warp * n;
+  const TOut* ur = u + (size_t)warp * n;
   float v[kMaxPerLane];
   float s = 0.f;
   const int per = (n + 31) / 32;
@@ -77,7 +77,7 @@ __global__ void gate_kernel(const float* __restrict__ attn, const float* __restr
 #pragma unroll
   for (int i = 0; i < kMaxPerLane; ++i) {
     const int c = lane + 32 * i;
-    if (i < per && c < n) o[c] = from_f<TOut>(ur[c] * ((v[i] - mu) * rs));
+    if (i < per && c < n) o[c] = from_f<TOut>(to_f(ur[c]) * ((v[i] - mu) * rs));
   }
 }
 
@@ -131,6 +131,13 @@ __global__ void final_ln_kernel(const float* __restrict__ x, int rows, int n, co
 // Lane l holds columns 128 i + 4 l .. +3 for i < n / 128.
 constexpr int kMaxVec = 8;
 
+__device__ __forceinline__ float4 load4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 load4(const bf16* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
 __device__ __forceinline__ void store4(float* p, float a, float b, float c, float d) {
   *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
 }
@@ -182,7 +189,7 @@ __global__ void ln_rows4_kernel(const float* __restrict__ x, int rows, int n, fl
 }
 
 template <typename TOut>
-__global__ void gate4_kernel(const float* __restrict__ attn, const float* __restrict__ u, int rows, int n,
+__global__ void gate4_kernel(const float* __restrict__ attn, const TOut* __restrict__ u, int rows, int n,
                              TOut* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
@@ -190,13 +197,13 @@ __global__ void gate4_kernel(const float* __restrict__ attn, const float* __rest
   if (warp >= rows) return;
   const int nv = n >> 7;
   const float* ar = attn + (size_t)warp * n + 4 * lane;
-  const float* ur = u + (size_t)warp * n + 4 * lane;
+  const TOut* ur = u + (size_t)warp * n + 4 * lane;
   float4 v[kMaxVec], w[kMaxVec];
 #pragma unroll
   for (int i = 0; i < kMaxVec; ++i)
     if (i < nv) {
       v[i] = *reinterpret_cast<const float4*>(ar + 128 * i);
-      w[i] = *reinterpret_cast<const float4*>(ur + 128 * i);
+      w[i] = load4(ur + 128 * i);
     }
   float mu, rs;
   row_stats4(v, nv, n, 1e-6f, mu, rs);
@@ -417,13 +424,13 @@ template cudaError_t launch_ln_rows<float>(const float*, int, int, float, float*
 template cudaError_t launch_ln_rows<bf16>(const float*, int, int, float, bf16*, cudaStream_t);
 
 template <typename T>
-cudaError_t launch_gate(const float* attn, const float* u, int rows, int n, T* out, cudaStream_t s) {
+cudaError_t launch_gate(const float* attn, const T* u, int rows, int n, T* out, cudaStream_t s) {
   if (n % 128 == 0 && n <= 128 * kMaxVec)
     return launch_pdl(gate4_kernel<T>, dim3(warp_blocks(rows)), dim3(256), 0, s, attn, u, rows, n, out);
   return launch_pdl(gate_kernel<T>, dim3(warp_blocks(rows)), dim3(256), 0, s, attn, u, rows, n, out);
 }
 template cudaError_t launch_gate<float>(const float*, const float*, int, int, float*, cudaStream_t);
-template cudaError_t launch_gate<bf16>(const float*, const float*, int, int, bf16*, cudaStream_t);
+template cudaError_t launch_gate<bf16>(const float*, const bf16*, int, int, bf16*, cudaStream_t);
 
 template <typename T>
 cudaError_t launch_final_ln(const float* x, int rows, int n, const float* w, const float* b, float* out32, T* out3,
