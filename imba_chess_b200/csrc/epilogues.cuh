@@ -3,6 +3,8 @@
 // and hands each fp32 accumulator to one of these functors.
 #pragma once
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace imba {
@@ -61,6 +63,40 @@ struct EpiUVQK {
   PoolGeom g;
   int layer;
   int32_t* status;
+  // Tensor-core path (bf16): u and q are written as [32 rows x 64 columns]
+  // boxes by TMA stores from a 128-byte-swizzled staging tile (bf16 [R, H dv]
+  // and [R, H dqk], encoded per launch); v and k go to the pool per thread.
+  CUtensorMap u_map, q_map;
+  static constexpr bool kBoxStore = true;
+  // 1: column c0 lies in u, 2: in q, 0: in v or k (pool rows).
+  __device__ __forceinline__ int box_region(int c0) const {
+    const int hdv = g.H * g.dv, hdq = g.H * g.dqk;
+    if (c0 < hdv) return 1;
+    if (c0 >= 2 * hdv && c0 < 2 * hdv + hdq) return 2;
+    return 0;
+  }
+  __device__ __forceinline__ const CUtensorMap* box_map(int region) const { return region == 1 ? &u_map : &q_map; }
+  __device__ __forceinline__ int box_x(int region, int c0) const {
+    return region == 1 ? c0 : c0 - 2 * g.H * g.dv;
+  }
+  // SiLU of one row's 32 columns (thread = row = lane of the box), as bf16
+  // into 16-byte chunks 4 h .. 4 h + 3 of the row's 128 bytes, 128-byte
+  // swizzle (chunk j of row r at j ^ (r % 8)).
+  __device__ __forceinline__ void box_stage32(uint8_t* box, int h, const float (&a)[32], int lane) const {
+    const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(box)) + lane * 128;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        __nv_bfloat162 p = __floats2bfloat162_rn(silu_tanh(a[8 * j + 2 * k]), silu_tanh(a[8 * j + 2 * k + 1]));
+        w[k] = *reinterpret_cast<uint32_t*>(&p);
+      }
+      const uint32_t dst = base + ((((uint32_t)(4 * h + j)) ^ (uint32_t)(lane & 7)) << 4);
+      asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+                   : "memory");
+    }
+  }
 
   __device__ __forceinline__ void operator()(int r, int c, float acc) const {
     const float y = silu_f(acc);
@@ -190,6 +226,7 @@ struct EpiResidual {
     return Ctx{};
   }
   static constexpr bool kStaged = true;
+  static constexpr bool kBoxStore = false;
   __device__ __forceinline__ int row_tag(int) const { return 0; }
   // Staged chunk (see staged4): all residual and bias loads are issued
   // before any store (the compiler cannot prove x and bias do not alias).
@@ -244,6 +281,7 @@ struct EpiResidual {
 
 struct EpiStore {
   static constexpr bool kStaged = false;
+  static constexpr bool kBoxStore = false;
   float* out;
   int ld;
   __device__ __forceinline__ void operator()(int r, int c, float acc) const { out[(size_t)r * ld + c] = acc; }
@@ -274,6 +312,7 @@ struct EpiAccumulate {
 
 // Value-head hidden layer: SiLU(acc + bias)   (hstu_model.py:252-257)
 struct EpiBiasSilu {
+  static constexpr bool kBoxStore = false;
   static constexpr bool kStaged = false;
   float* out;
   const float* bias;

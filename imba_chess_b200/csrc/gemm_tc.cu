@@ -42,12 +42,16 @@ __host__ __device__ constexpr int gemm_threads() { return 64 + 32 * epi_warps<ST
 // per-row tags.
 constexpr size_t kStageFloats = 32 * 32 + 32;
 
-template <int BN, int STAGES, bool STAGED>
+// Box-stored epilogues: per epilogue warp one 4 KB staging box (32 rows x
+// 128 B, 128-byte swizzle) for its TMA stores, 1024-aligned after the ring.
+constexpr size_t kBoxBytes = 32 * 128;
+
+template <int BN, int STAGES, bool STAGED, bool BOX = false>
 struct TileShape {
   static constexpr uint32_t kABytes = kBM * kBK * 2;
   static constexpr uint32_t kBBytes = BN * kBK * 2;
-  static constexpr size_t kSmem = 1024 + STAGES * (kABytes + kBBytes) + (2 * STAGES + 4) * 8 + 16 +
-                                  (STAGED ? epi_warps<STAGED>() * kStageFloats * 4 : 0);
+  static constexpr size_t kSmem = 1024 + STAGES * (kABytes + kBBytes) + (BOX ? epi_warps<STAGED>() * kBoxBytes : 0) +
+                                  (2 * STAGES + 4) * 8 + 16 + (STAGED ? epi_warps<STAGED>() * kStageFloats * 4 : 0);
 };
 
 // Persistent, warp-specialised: CTA b handles tiles b, b + gridDim.x, ...
@@ -58,8 +62,8 @@ struct TileShape {
 template <int BN, int STAGES, class Epi>
 __global__ void __launch_bounds__(gemm_threads<Epi::kStaged>(), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                   int K, Epi epi, int32_t* status) {
-  using S = TileShape<BN, STAGES, Epi::kStaged>;
+                   int K, const __grid_constant__ Epi epi, int32_t* status) {
+  using S = TileShape<BN, STAGES, Epi::kStaged, Epi::kBoxStore>;
   constexpr int kEpiWarps = epi_warps<Epi::kStaged>();
   constexpr int kColGroups = kEpiWarps / 4;  // warps per TMEM lane quadrant
   constexpr int kCols = BN / kColGroups;      // columns per epilogue warp
@@ -68,7 +72,8 @@ __global__ void __launch_bounds__(gemm_threads<Epi::kStaged>(), 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * S::kBBytes);
+  uint8_t* boxes = sB + STAGES * S::kBBytes;  // kEpiWarps x kBoxBytes (box-stored epilogues)
+  uint64_t* full = reinterpret_cast<uint64_t*>(boxes + (Epi::kBoxStore ? kEpiWarps * kBoxBytes : 0));
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -154,6 +159,7 @@ __global__ void __launch_bounds__(gemm_threads<Epi::kStaged>(), 1)
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int c_lo = ((warp - 2) >> 2) * kCols;  // kColGroups warps per quadrant, one slice each
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    bool box_pending = false;  // a TMA store of this warp may still be reading its box
     int i = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++i) {
       const int b = i & 1;
@@ -180,19 +186,50 @@ __global__ void __launch_bounds__(gemm_threads<Epi::kStaged>(), 1)
           __syncwarp();
         }
       } else {
-        typename Epi::Ctx cx{};
-        if (row < M) cx = epi.begin(row, n0 + c_lo, kCols);
+        int region = 0;
+        if constexpr (Epi::kBoxStore) region = epi.box_region(n0 + c_lo);
+        if (region != 0) {
+          if constexpr (Epi::kBoxStore) {
+            // 64-column boxes of this warp's 32 rows: TMEM -> SiLU -> bf16 ->
+            // swizzled staging box -> one TMA store (rows past M are clipped).
+            uint8_t* box = boxes + (size_t)(warp - 2) * kBoxBytes;
 #pragma unroll 1
-        for (int c = c_lo; c < c_lo + kCols; c += 32) {
-          float v[32];
-          tc::tmem_ld32(tmem + b * BN + lane_base + c, v);
-          if (row < M && n0 + c < N) epi.chunk32(cx, row, n0 + c, N, v);
+            for (int cb = 0; cb < kCols; cb += 64) {
+              if (box_pending) {  // the previous store from this box must have read it
+                if (lane == 0) tc::bulk_wait_read_all();
+                __syncwarp();
+              }
+#pragma unroll 1
+              for (int h = 0; h < 2; ++h) {
+                float v[32];
+                tc::tmem_ld32(tmem + b * BN + lane_base + c_lo + cb + 32 * h, v);
+                epi.box_stage32(box, h, v, lane);
+              }
+              tc::fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tc::tma_store_2d(epi.box_map(region), box, epi.box_x(region, n0 + c_lo + cb), m0 + quad * 32);
+                tc::bulk_commit();
+              }
+              box_pending = true;
+            }
+          }
+        } else {
+          typename Epi::Ctx cx{};
+          if (row < M) cx = epi.begin(row, n0 + c_lo, kCols);
+#pragma unroll 1
+          for (int c = c_lo; c < c_lo + kCols; c += 32) {
+            float v[32];
+            tc::tmem_ld32(tmem + b * BN + lane_base + c, v);
+            if (row < M && n0 + c < N) epi.chunk32(cx, row, n0 + c, N, v);
+          }
         }
       }
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
     }
+    if (box_pending && lane == 0) tc::bulk_wait_all();  // stores complete before the CTA exits
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -257,7 +294,7 @@ template <int BN, class Epi>
 cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const Epi& epi, int32_t* status,
                    cudaStream_t s) {
   constexpr int kSt = BN == 256 ? 4 : 6;
-  using S = TileShape<BN, kSt, Epi::kStaged>;
+  using S = TileShape<BN, kSt, Epi::kStaged, Epi::kBoxStore>;
   auto kern = gemm_tc_kernel<BN, kSt, Epi>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::kSmem);
   if (e != cudaSuccess) return e;
@@ -313,7 +350,13 @@ bool gemm_tc_launch_uvqk<bf16>(const imba_model* m, int layer, int rows, const b
   if (!t || rows <= 0) return false;
   CUtensorMap ta;
   if (!make_map(&ta, xn, rows, m->d.model_dim, (uint64_t)m->d.model_dim * 2, kBM)) return false;
-  *err = launch<kBNWide>(ta, t->uvqk[layer], rows, m->uvqk_n, m->d.model_dim, epi, epi.status, s);
+  // u / q as [rows, H d] bf16 with 64 x 32 boxes for the epilogue's TMA stores.
+  EpiUVQK<bf16> e = epi;
+  const int hdv = m->d.num_heads * m->d.linear_dim, hdq = m->d.num_heads * m->d.attention_dim;
+  if (!make_map(&e.u_map, e.u, rows, hdv, (uint64_t)hdv * 2, 32) ||
+      !make_map(&e.q_map, e.q, rows, hdq, (uint64_t)hdq * 2, 32))
+    return false;
+  *err = launch<kBNWide>(ta, t->uvqk[layer], rows, m->uvqk_n, m->d.model_dim, e, epi.status, s);
   return true;
 }
 

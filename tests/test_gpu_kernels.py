@@ -118,3 +118,27 @@ def test_attention_result_independent_of_chunking():
     for o in outs[1:]:
         for k in ("hidden", "logits", "value_logits"):
             assert torch.equal(o[k], outs[0][k]), k
+
+
+def test_attention_positions_past_max_pos():
+    """Prefixes longer than max_pos: relative-bias indices clamp at both ends
+    and the paged kernel leaves its fast path; TC attention vs SIMT."""
+    dims = synth.ModelDims(256, 2, 4, max_pos=96)
+    sd = synth.make_state_dict(dims, 21, profile="sharp")
+    wave = synth.grouped_wave(dims, n_parents=3, plies=(100, 230), siblings=(20, 40), seed=23)
+    model_tc = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
+    import os
+
+    os.environ["IMBA_SIMT"] = "attn"
+    try:
+        model_simt = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
+    finally:
+        del os.environ["IMBA_SIMT"]
+    a = _run_wave(model_tc, dims, wave)
+    b = _run_wave(model_simt, dims, wave)
+    th, tl, tv = TOL["attn"]
+    scale = float(b["hidden"].abs().max())
+    assert torch.isfinite(a["logits"]).all()
+    assert float((a["hidden"] - b["hidden"]).abs().max()) <= th * scale
+    assert float((a["logits"] - b["logits"]).abs().max()) <= tl
+    assert float((a["value_logits"] - b["value_logits"]).abs().max()) <= tv
