@@ -151,6 +151,13 @@ __device__ __forceinline__ void layer_norm(const float (&x)[8][4], const float* 
   }
 }
 
+// Barrier of one board's four warps (named barrier board + 1, 128 threads):
+// the boards of a CTA share only read-only weights, so each advances on its
+// own instead of waiting for the slowest board at every phase.
+__device__ __forceinline__ void board_barrier(int board) {
+  asm volatile("bar.sync %0, 128;" ::"r"(board + 1) : "memory");
+}
+
 __device__ __forceinline__ void zero(float (&c)[8][4]) {
 #pragma unroll
   for (int n = 0; n < 8; ++n) c[n][0] = c[n][1] = c[n][2] = c[n][3] = 0.f;
@@ -274,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         to_afrag(acc, qa);
       }
-      __syncthreads();
+      board_barrier(board_slot);
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         float s[8][4];
@@ -333,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         oa[3] = pack_bf16(oh[1][2] * i1, oh[1][3] * i1);
         gemm_k16<8>(x, oa, W + kOffOut, LD64, 0, 16 * h, lane);  // x += o_h . Wout[:, 16h .. 16h+15]^T
       }
-      __syncthreads();  // the board's K / V are reused by the next block
+      board_barrier(board_slot);  // the board's K / V are reused by the next block
       {
         float y[8][4];
         layer_norm(x, P + 128, P + 192, t, y);
@@ -392,7 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    __syncthreads();
+    board_barrier(board_slot);
     if (live && wq == 0) {
       const float* src = sPool + (size_t)board_slot * 4 * 64;
       for (int c = lane; c < 64; c += 32) {
@@ -400,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         pooled_out[(size_t)r * 64 + c] = s * (1.0f / 64.0f);
       }
     }
-    __syncthreads();
+    board_barrier(board_slot);
   }
 }
 
