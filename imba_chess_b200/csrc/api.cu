@@ -44,7 +44,7 @@ size_t workspace_layout(const imba_model* m, int32_t rows, void* base, Workspace
   w.xf3 = take(d.dtype == IMBA_DTYPE_BF16 ? R * 3 * d.model_dim * 2 : 0);
   w.hval = static_cast<float*>(take(R * (d.model_dim / 2 + 1) * 4));
   w.logits = static_cast<float*>(take(R * d.vocab * 4));
-  w.pooled = static_cast<float*>(take(d.dtype == IMBA_DTYPE_BF16 ? R * IMBA_BOARD_DIM * 4 : 0));
+  w.pooled = take(d.dtype == IMBA_DTYPE_BF16 ? R * 3 * IMBA_BOARD_DIM * 2 : 0);
   w.counters = static_cast<int*>(take(kNumCounters * sizeof(int)));
   w.bytes = off;
   if (ws) *ws = w;
@@ -125,13 +125,18 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
   IMBA_CK(pm.mark(s));
   IMBA_CK(cudaMemsetAsync(w.counters, 0, kNumCounters * sizeof(int), s));
   if (md.dtype == IMBA_DTYPE_BF16 && !m->simt_board) {
-    // tensor-core board encoder -> pooled [R, 64]; projection + embeddings in the GEMM epilogue
-    IMBA_CK(launch_board_mma(md, st, w.pooled, s));
+    // tensor-core board encoder -> pooled [R, 192] split bf16; projection + embeddings in the GEMM epilogue
+    IMBA_CK(launch_board_mma(md, st, static_cast<bf16*>(w.pooled), s));
     EpiContent ec{w.x, nullptr, md.board_out_b, md.emb_seq, md.emb_turn, md.emb_castle, md.emb_ep, md.emb_halfmove,
                   md.emb_fullmove, md.emb_prev_move, md.emb_pos, st.side_ids, st.positions, d, md.halfmove_vocab,
                   md.fullmove_vocab, md.vocab, md.max_pos, sqrtf((float)d), st.status};
-    IMBA_CK(launch_gemm_simt<float, float, EpiContent>(w.pooled, IMBA_BOARD_DIM, md.board_out_w, IMBA_BOARD_DIM, R, d,
-                                                       IMBA_BOARD_DIM, ec, s));
+    const bf16* p3 = static_cast<const bf16*>(w.pooled);
+    if (!gemm_tc_launch_content(m, R, p3, ec, st.status, s, &e)) {
+      IMBA_CK(launch_gemm_simt<bf16, bf16, EpiContent>(p3, 3 * IMBA_BOARD_DIM, static_cast<const bf16*>(m->board_proj3),
+                                                       3 * IMBA_BOARD_DIM, R, d, 3 * IMBA_BOARD_DIM, ec, s));
+    } else if (e != cudaSuccess) {
+      return IMBA_ERR_CUDA;
+    }
   } else {
     IMBA_CK(launch_embed(md, st, w.x, s));
   }
@@ -242,8 +247,26 @@ imba_status_t imba_model_create(const imba_model_desc* desc, imba_model** out) {
     m->simt_attn = strstr(sel, "attn") != nullptr;
     m->simt_board = strstr(sel, "board") != nullptr;
   }
+  if (desc->dtype == IMBA_DTYPE_BF16 && !m->simt_board) {
+    // Split bf16 copy of the board projection for the content GEMM.
+    void* w3 = nullptr;
+    if (cudaMalloc(&w3, (size_t)desc->model_dim * 3 * IMBA_BOARD_DIM * sizeof(imba::bf16)) != cudaSuccess) {
+      cudaGetLastError();
+      delete m;
+      return IMBA_ERR_OOM;
+    }
+    if (imba::build_board_proj_split(m->d, static_cast<imba::bf16*>(w3), 0) != cudaSuccess ||
+        cudaStreamSynchronize(0) != cudaSuccess) {
+      cudaGetLastError();
+      cudaFree(w3);
+      delete m;
+      return IMBA_ERR_CUDA;
+    }
+    m->board_proj3 = w3;
+  }
   const imba_status_t t = imba::gemm_tc_prepare(m);
   if (t != IMBA_OK) {
+    if (m->board_proj3) cudaFree(m->board_proj3);
     delete m;
     return t;
   }
@@ -254,6 +277,7 @@ imba_status_t imba_model_create(const imba_model_desc* desc, imba_model** out) {
 void imba_model_destroy(imba_model* model) {
   if (!model) return;
   imba::gemm_tc_release(model);
+  if (model->board_proj3) cudaFree(model->board_proj3);
   delete model;
 }
 

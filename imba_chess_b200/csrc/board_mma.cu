@@ -1,8 +1,10 @@
 // Board encoder on the tensor cores (bf16 models): the two pre-LN square-
 // attention blocks over the 64 squares of each position, the final LayerNorm
 // and the mean over squares (src/imba_chess/model/hstu_model.py:118-179,
-// :275-278).  Output: the pooled 64-vector of every board (fp32); the 64 -> d
-// projection and the side / position embeddings follow in a GEMM epilogue.
+// :275-278).  Output: the pooled 64-vector of every board as the split bf16
+// operand [hi | lo | hi] (192 values, hi + lo = the fp32 mean to ~2^-16); the
+// 64 -> d projection (against [W_hi | W_hi | W_lo]) and the side / position
+// embeddings follow in a GEMM epilogue.
 //
 // Persistent CTAs of 16 warps hold both blocks' weights in shared memory
 // (bf16, padded rows) and process four boards per iteration: warp w owns
@@ -175,7 +177,7 @@ __device__ __forceinline__ void store_rows(const float (&c)[8][4], bf16* dst, in
 
 __global__ void __launch_bounds__(kThreads, 1)
     board_mma_kernel(const float* __restrict__ table, const float* __restrict__ params,
-                     const uint8_t* __restrict__ piece_ids, int rows, float* __restrict__ pooled_out,
+                     const uint8_t* __restrict__ piece_ids, int rows, bf16* __restrict__ pooled_out,
                      int32_t* status) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   bf16* sW = reinterpret_cast<bf16*>(smem_raw);       // 2 blocks of weights
@@ -404,16 +406,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* src = sPool + (size_t)board_slot * 4 * 64;
       for (int c = lane; c < 64; c += 32) {
         const float s = src[c] + src[64 + c] + src[128 + c] + src[192 + c];
-        pooled_out[(size_t)r * 64 + c] = s * (1.0f / 64.0f);
+        const float v = s * (1.0f / 64.0f);
+        const bf16 hi = __float2bfloat16_rn(v), lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+        bf16* o = pooled_out + (size_t)r * 3 * 64;
+        o[c] = hi;
+        o[64 + c] = lo;
+        o[128 + c] = hi;
       }
     }
     board_barrier(board_slot);
   }
 }
 
+// [d, 64] fp32 projection -> [d, 192] bf16 [W_hi | W_hi | W_lo].
+__global__ void split_board_proj_kernel(const float* __restrict__ w, int d, bf16* __restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= d * 64) return;
+  const int row = i >> 6, c = i & 63;
+  const float v = w[i];
+  const bf16 hi = __float2bfloat16_rn(v), lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+  bf16* o = out + (size_t)row * 192;
+  o[c] = hi;
+  o[64 + c] = hi;
+  o[128 + c] = lo;
+}
+
 }  // namespace
 
-cudaError_t launch_board_mma(const imba_model_desc& md, const imba_step_desc& st, float* pooled, cudaStream_t s) {
+cudaError_t build_board_proj_split(const imba_model_desc& md, bf16* out, cudaStream_t s) {
+  const int n = md.model_dim * 64;
+  split_board_proj_kernel<<<(n + 255) / 256, 256, 0, s>>>(md.board_out_w, md.model_dim, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_board_mma(const imba_model_desc& md, const imba_step_desc& st, bf16* pooled, cudaStream_t s) {
   if (st.num_rows <= 0) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(board_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
   if (e != cudaSuccess) return e;

@@ -102,6 +102,9 @@ struct imba_model {
   // creation selects the SIMT kernel of a component, for cross-checking).
   bool simt_attn = false;
   bool simt_board = false;
+  // bf16 models with the tensor-core board encoder: [d, 192] bf16 split copy
+  // of the board projection (device memory owned by the handle), or null.
+  void* board_proj3 = nullptr;
   imba::PoolGeom geom(int64_t num_pages) const {
     imba::PoolGeom g;
     g.H = d.num_heads;
@@ -133,7 +136,7 @@ struct Workspace {
   void* xf3;       // [R, 3d]     bf16 only: final LN output as [hi | lo | hi]
   float* hval;     // [R, d/2]    value-head hidden
   float* logits;   // [R, vocab]  used when the caller passes no logits buffer
-  float* pooled;   // [R, 64]     bf16 models: mean-pooled board-encoder output
+  void* pooled;    // [R, 192]    bf16 models: mean-pooled board-encoder output, split bf16
   int* counters;   // [kNumCounters] work-queue counters, zeroed at the start of every step
   size_t bytes;
 };

@@ -354,7 +354,57 @@ struct EpiContent {
   float scale;
   int32_t* status;
 
+  static constexpr bool kStaged = false;
+  static constexpr bool kBoxStore = false;
   __device__ __forceinline__ static int clampi(int v, int n) { return v < 0 ? 0 : (v >= n ? n - 1 : v); }
+  // Tensor-core epilogue: the row's seven side-embedding rows and its
+  // position row, resolved once per tile.
+  struct Ctx {
+    const float* e[7];
+    const float* pos;
+  };
+  __device__ __forceinline__ Ctx begin(int r, int, int) const {
+    const int32_t* ids = side_ids + (size_t)r * IMBA_NUM_SIDE_IDS;
+    Ctx cx;
+    cx.e[0] = seq + (size_t)clampi(ids[0], 2) * d;
+    cx.e[1] = turn + (size_t)clampi(ids[1], 2) * d;
+    cx.e[2] = castle + (size_t)clampi(ids[2], 16) * d;
+    cx.e[3] = ep + (size_t)clampi(ids[3], 9) * d;
+    cx.e[4] = half + (size_t)clampi(ids[4], halfmove_vocab) * d;
+    cx.e[5] = full + (size_t)clampi(ids[5], fullmove_vocab) * d;
+    cx.e[6] = prev + (size_t)clampi(ids[6], vocab) * d;
+    int p = positions[r];
+    if (p < 0) {
+      report(status, IMBA_ERR_RANGE);
+      p = 0;
+    }
+    if (p > max_pos - 1) p = max_pos - 1;
+    cx.pos = pos_emb + (size_t)p * d;
+    return cx;
+  }
+  // 32 columns of one row, in the same summation order as operator(); the
+  // tables are read through the read-only path (never written by a step).
+  __device__ __forceinline__ void chunk32(const Ctx& cx, int r, int c0, int N, const float (&a)[32]) const {
+    if (c0 >= N) return;
+    float* xr = x + (size_t)r * d + c0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int c = c0 + 4 * i;
+      const float4 b = __ldg(reinterpret_cast<const float4*>(bias + c));
+      float4 v = make_float4(a[4 * i] + b.x, a[4 * i + 1] + b.y, a[4 * i + 2] + b.z, a[4 * i + 3] + b.w);
+#pragma unroll
+      for (int k = 0; k < 7; ++k) {
+        const float4 e = __ldg(reinterpret_cast<const float4*>(cx.e[k] + c));
+        v.x += e.x;
+        v.y += e.y;
+        v.z += e.z;
+        v.w += e.w;
+      }
+      const float4 pe = __ldg(reinterpret_cast<const float4*>(cx.pos + c));
+      *reinterpret_cast<float4*>(xr + 4 * i) =
+          make_float4(v.x * scale + pe.x, v.y * scale + pe.y, v.z * scale + pe.z, v.w * scale + pe.w);
+    }
+  }
   __device__ __forceinline__ void operator()(int r, int c, float acc) const {
     const int32_t* ids = side_ids + (size_t)r * IMBA_NUM_SIDE_IDS;
     float v = acc + bias[c];

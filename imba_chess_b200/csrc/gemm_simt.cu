@@ -82,6 +82,7 @@ IMBA_INST(float, float, EpiStore)
 IMBA_INST(float, float, EpiBiasSilu)
 IMBA_INST(bf16, bf16, EpiBiasSilu)
 IMBA_INST(float, float, EpiContent)
+IMBA_INST(bf16, bf16, EpiContent)
 #undef IMBA_INST
 
 }  // namespace imba

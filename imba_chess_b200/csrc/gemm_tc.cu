@@ -280,7 +280,9 @@ struct TCState {
   CUtensorMap o[IMBA_MAX_LAYERS];
   CUtensorMap policy;
   CUtensorMap value;
+  CUtensorMap content;  // [d, 192] split board projection
   bool has_value = false;
+  bool has_content = false;
 };
 
 int sm_count() {
@@ -330,6 +332,8 @@ imba_status_t gemm_tc_prepare(imba_model* m) {
     ok = make_map(&t->value, d.value0_w, d.model_dim / 2, d.model_dim, (uint64_t)d.model_dim * 2, kBNNarrow);
     t->has_value = ok;
   }
+  if (ok && m->board_proj3)
+    t->has_content = make_map(&t->content, m->board_proj3, d.model_dim, 192, 192 * 2, kBNNarrow);
   if (!ok) {
     delete t;
     return IMBA_OK;
@@ -357,6 +361,16 @@ bool gemm_tc_launch_uvqk<bf16>(const imba_model* m, int layer, int rows, const b
       !make_map(&e.q_map, e.q, rows, hdq, (uint64_t)hdq * 2, 32))
     return false;
   *err = launch<kBNWide>(ta, t->uvqk[layer], rows, m->uvqk_n, m->d.model_dim, e, epi.status, s);
+  return true;
+}
+
+bool gemm_tc_launch_content(const imba_model* m, int rows, const bf16* pooled3, const EpiContent& epi,
+                            int32_t* status, cudaStream_t s, cudaError_t* err) {
+  const TCState* t = static_cast<const TCState*>(m->tc);
+  if (!t || !t->has_content || rows <= 0) return false;
+  CUtensorMap ta;
+  if (!make_map(&ta, pooled3, rows, 192, 192 * 2, kBM)) return false;
+  *err = launch<kBNNarrow>(ta, t->content, rows, m->d.model_dim, 192, epi, status, s);
   return true;
 }
 

@@ -22,6 +22,10 @@ bool gemm_tc_launch_out(const imba_model* m, int layer, int rows, const T* gated
 template <typename T>
 bool gemm_tc_launch_policy(const imba_model* m, int rows, const T* xf3, const EpiStore& epi, int32_t* status,
                            cudaStream_t s, cudaError_t* err);
+// Board projection + embeddings: pooled3 [rows, 192] split bf16 against the
+// handle's [d, 192] split copy of the projection.
+bool gemm_tc_launch_content(const imba_model* m, int rows, const bf16* pooled3, const EpiContent& epi,
+                            int32_t* status, cudaStream_t s, cudaError_t* err);
 template <typename T>
 bool gemm_tc_launch_value(const imba_model* m, int rows, const T* xin, int lda, const EpiBiasSilu& epi,
                           int32_t* status, cudaStream_t s, cudaError_t* err);

@@ -19,7 +19,10 @@ struct AttnArgs {
 };
 
 cudaError_t launch_embed(const imba_model_desc& md, const imba_step_desc& st, float* x, cudaStream_t s);
-cudaError_t launch_board_mma(const imba_model_desc& md, const imba_step_desc& st, float* pooled, cudaStream_t s);
+// Board encoder -> pooled [R, 192] split bf16 ([hi | lo | hi] of the mean).
+cudaError_t launch_board_mma(const imba_model_desc& md, const imba_step_desc& st, bf16* pooled, cudaStream_t s);
+// [d, 64] fp32 board projection -> [d, 192] bf16 [W_hi | W_hi | W_lo].
+cudaError_t build_board_proj_split(const imba_model_desc& md, bf16* out, cudaStream_t s);
 template <typename T>
 cudaError_t launch_ln_rows(const float* x, int rows, int n, float eps, T* out, cudaStream_t s);
 template <typename T>
