@@ -189,7 +189,10 @@ IMBA_API int32_t imba_device_arch(void);
 /* Validate a model description and build a handle on the current device.
  * bf16 handles encode their TMA descriptors here and keep one small device
  * copy of the board projection split into bf16 hi / lo parts ([d, 192]
- * bf16, freed by imba_model_destroy). */
+ * bf16, freed by imba_model_destroy).  Environment, read here: IMBA_SIMT
+ * naming components (gemm, attn, board) selects their SIMT kernels (for
+ * cross-checks); IMBA_BOARD=tc selects the tcgen05 board encoder instead of
+ * the mma.sync one. */
 IMBA_API imba_status_t imba_model_create(const imba_model_desc* desc, imba_model** out);
 IMBA_API void imba_model_destroy(imba_model* model);
 
