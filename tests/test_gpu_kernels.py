@@ -148,3 +148,66 @@ def test_attention_positions_past_max_pos():
     assert float((a["hidden"] - b["hidden"]).abs().max()) <= th * scale
     assert float((a["logits"] - b["logits"]).abs().max()) <= tl
     assert float((a["value_logits"] - b["value_logits"]).abs().max()) <= tv
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["fp32", "bf16"])
+@pytest.mark.parametrize("max_rows", [32, 64])
+def test_legal_gather_matches_full_projection(dtype, max_rows):
+    """Legal logits without the full projection (fp32 dot products of the
+    final-LN output with the legal ids' fp32 policy rows) against the same
+    entries of the full 1,970-way logits of the same step, and the log-probs
+    against a float64 log-softmax of those.  Covers a row without legal ids,
+    repeated ids within a row and 64-row chunks."""
+    import imba_chess_b200.plan as plan_mod
+
+    dims = synth.D256
+    sd = synth.make_state_dict(dims, 13, profile="reference")
+    wave = synth.grouped_wave(dims, n_parents=4, plies=(20, 80), siblings=(30, 60), seed=31)
+    model = B200HSTUChessModel(sd, dtype=dtype, device="cuda:0")
+    orig = plan_mod.build_chunks
+
+    def rechunk(row_group, num_groups, max_rows_=32, row_vis=None):
+        return orig(row_group, num_groups, max_rows=max_rows, row_vis=row_vis)
+
+    plan_mod.build_chunks = rechunk
+    try:
+        pool = model.new_pool(4096)
+        seqs = [KVSequence(pool) for _ in wave.prefix_lens]
+        plan0, _ = root_plan(seqs, wave.prefix_tokens)
+        model.run(DeviceStep(plan0, model.device), pool)
+        order = np.argsort(wave.group_index, kind="stable")
+        counts = np.bincount(wave.group_index, minlength=len(seqs))
+        arenas = [KVSequence(pool) for _ in seqs]
+        tok = synth.slice_tokens(wave.row_tokens, order)
+        legal = [list(wave.legal_ids[i]) for i in order]
+        legal[0] = []
+        legal[1] = legal[1] + legal[1][:3]
+        groups = [WaveGroup(seqs[g], wave.prefix_lens[g], arenas[g], [[]] * int(counts[g])) for g in range(len(seqs))]
+        plan, _ = wave_plan(groups, piece_ids_from_tokens(tok), side_ids_from_tokens(tok), legal)
+    finally:
+        plan_mod.build_chunks = orig
+    R, NL = plan.num_rows, int(plan.legal_ids.shape[0])
+    dstep = DeviceStep(plan, model.device)
+    full = torch.empty((R, dims.vocab), device=model.device)
+    ll_a = torch.empty(NL, device=model.device)
+    ll_b = torch.empty(NL, device=model.device)
+    lp_b = torch.empty(NL, device=model.device)
+    model.run(dstep, pool, logits=full, legal_logits=ll_a)
+    model.run(dstep, pool, legal_logits=ll_b, legal_logprob=lp_b)
+    torch.cuda.synchronize()
+    model.check_status()
+    off = plan.legal_off.astype(np.int64)
+    ids = torch.as_tensor(plan.legal_ids.astype(np.int64), device=model.device)
+    rows = torch.as_tensor(np.repeat(np.arange(R), np.diff(off)), device=model.device)
+    ref = full[rows, ids]
+    atol = 1e-4 if dtype == torch.float32 else 2e-3
+    assert torch.equal(ll_a, ref)
+    assert float((ll_b - ref).abs().max()) <= atol
+    ll = ll_b.double().cpu().numpy()
+    for r in range(R):
+        a, b = int(off[r]), int(off[r + 1])
+        if a == b:
+            continue
+        z = ll[a:b]
+        lse = z.max() + np.log(np.exp(z - z.max()).sum())
+        assert np.abs(lp_b[a:b].double().cpu().numpy() - (z - lse)).max() <= 1e-5
