@@ -72,8 +72,8 @@ def _run_wave(model, dims, wave, depth2=True):
 
 
 @pytest.mark.parametrize("component", ["gemm", "attn", "board", "board_tc"])
-@pytest.mark.parametrize("dims,parents", [(synth.D512, 6), (synth.SMALL, 4), (synth.D256, 5)],
-                         ids=["d512", "d128", "d256"])
+@pytest.mark.parametrize("dims,parents", [(synth.D512, 6), (synth.SMALL, 4), (synth.D256, 5), (synth.D1024, 2)],
+                         ids=["d512", "d128", "d256", "d1024"])
 def test_tensor_core_kernel_matches_simt(component, dims, parents, monkeypatch):
     sd = synth.make_state_dict(dims, 9, profile="reference")
     plies = (20, 140) if component == "attn" else (20, 45)

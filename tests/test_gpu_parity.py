@@ -212,8 +212,9 @@ def _bf16_wave_check(dims, n_parents, plies, siblings, seed):
 
 @pytest.mark.parametrize(
     "dims,n_parents,plies,siblings",
-    [(synth.D512, 6, (20, 60), (20, 40)), (synth.D256, 8, (10, 120), (1, 4))],
-    ids=["d512-grouped", "d256-grouped"],
+    [(synth.D512, 6, (20, 60), (20, 40)), (synth.D256, 8, (10, 120), (1, 4)),
+     (synth.D1024, 3, (300, 420), (8, 12))],
+    ids=["d512-grouped", "d256-grouped", "d1024-16h-long-prefix"],
 )
 def test_bf16_wave_matches_fp32_oracle(dims, n_parents, plies, siblings):
     max_dl, max_dv, top1, n = _bf16_wave_check(dims, n_parents, plies, siblings, seed=1234)
