@@ -1,6 +1,10 @@
 #!/usr/bin/env python
 """Benchmark: positions evaluated per second on the grouped-decode wave.
 
+(--workload selects the headline wave below (default), the same wave shape on
+the d1024/16L/16H model with long prefixes, or sequential-halving search
+rounds with suffix chains.)
+
 Workload (one step = one wave): a bf16 HSTU chess model, d_model 512, 8
 layers, 8 heads (head dims 64/64), random-initialised with the reference's
 initialisers; 256 parent positions with game prefixes of U[20, 200] plies
@@ -51,6 +55,12 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "positions evaluated/sec (grouped decode)"
+# Per-workload defaults (per GPU; weak scaling under torchrun).
+WORKLOADS = {
+    "grouped": {"parents": 256, "plies": (20, 200), "siblings": (20, 40), "rounds": None},
+    "d1024": {"parents": 512, "plies": (300, 600), "siblings": (40, 40), "rounds": None},
+    "halving": {"parents": 1024, "plies": (40, 250), "siblings": None, "rounds": (32, 16, 8, 4, 2)},
+}
 UNIT = "positions/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
@@ -61,14 +71,23 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--parents", type=int, default=256)
-    ap.add_argument("--plies", type=int, nargs=2, default=(20, 200))
-    ap.add_argument("--siblings", type=int, nargs=2, default=(20, 40))
+    ap.add_argument("--workload", choices=list(WORKLOADS), default="grouped",
+                    help="grouped: the headline grouped-decode wave (d512/8L); d1024: the same wave shape on "
+                         "the d1024/16L/16H model with long prefixes; halving: sequential-halving search rounds "
+                         "with suffix chains (one step = every round of every game)")
+    ap.add_argument("--parents", type=int, default=None)
+    ap.add_argument("--plies", type=int, nargs=2, default=None)
+    ap.add_argument("--siblings", type=int, nargs=2, default=None)
+    ap.add_argument("--rounds", type=int, nargs="+", default=None, help="halving: arms per round")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-service", action="store_true")
     ap.add_argument("--cpu-sample-parents", type=int, default=4)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    return ap.parse_args()
+    args = ap.parse_args()
+    for k, v in WORKLOADS[args.workload].items():
+        if getattr(args, k) is None:
+            setattr(args, k, v)
+    return args
 
 
 def dist_env():
@@ -97,7 +116,7 @@ def workload(args, rank, world=1):
     from imba_chess_b200 import synth
     from imba_chess_b200.shard import shard_games
 
-    dims = synth.D512
+    dims = synth.D1024 if args.workload == "d1024" else synth.D512
     mine = shard_games(args.parents * world, rank, world)
     parts = [synth.grouped_wave(dims, n_parents=1, plies=tuple(args.plies), siblings=tuple(args.siblings),
                                 seed=1234 + i) for i in mine]
@@ -233,6 +252,10 @@ def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
         return
+    if args.workload == "halving":
+        print(json.dumps({"impl": "reference", "unavailable": "the CPU reference arm is timed on the grouped-decode "
+                                                              "wave workloads only"}), flush=True)
+        return
     dims, wave = workload(args, 0)
     n_rows, _ = cpu_oracle_rate(dims, wave, args.cpu_sample_parents, 0.0, steps=1)  # warm (imports, caches)
     for _ in range(max(args.warmup - 1, 0)):
@@ -264,14 +287,97 @@ def run_reference(args):
 
 
 def workload_config(args):
+    if args.workload == "halving":
+        return {
+            "workload": "sequential-halving search rounds: bf16 HSTU d512/8L/8H (max_pos 513), "
+                        f"{args.parents} games, prefixes U[{args.plies[0]},{args.plies[1]}] plies, rounds of "
+                        f"{'/'.join(str(k) for k in args.rounds)} surviving arms per game, round r evaluates one "
+                        "node per arm at depth r whose suffix is the arm's chain in the turn arena; "
+                        "one step = every round of every game",
+            "games_per_gpu": args.parents,
+            "page_tokens": 16,
+            "l2": "inputs larger than L2 (prefix KV read per round > 126 MB at full size)",
+        }
+    model = "d1024/16L/16H (max_pos 1024)" if args.workload == "d1024" else "d512/8L/8H (max_pos 513)"
     return {
-        "workload": "grouped-decode wave: bf16 HSTU d512/8L/8H (head dims 64/64, max_pos 513), "
+        "workload": f"grouped-decode wave: bf16 HSTU {model}, head dims 64/64, "
                     f"{args.parents} parents, prefixes U[{args.plies[0]},{args.plies[1]}] plies, "
                     f"U[{args.siblings[0]},{args.siblings[1]}] depth-0 siblings each, 16-token KV pages",
         "parents_per_gpu": args.parents,
         "page_tokens": 16,
         "l2": "inputs larger than L2 (prefix KV read per step > 126 MB at full size)",
     }
+
+
+def prefill(model, pool, seqs, tokens, device, max_tokens=32768):
+    """Prefill sequences in packed batches of at most max_tokens tokens (setup, untimed)."""
+    import torch
+
+    from imba_chess_b200.plan import DeviceStep
+    from imba_chess_b200.steps import root_plan
+
+    i = 0
+    while i < len(seqs):
+        j, n = i, 0
+        while j < len(seqs) and (j == i or n + int(tokens[j]["piece_ids"].shape[0]) <= max_tokens):
+            n += int(tokens[j]["piece_ids"].shape[0])
+            j += 1
+        plan, _ = root_plan(seqs[i:j], tokens[i:j])
+        model.run(DeviceStep(plan, device), pool)
+        i = j
+    torch.cuda.synchronize()
+    model.check_status()
+
+
+def build_waves(args, dims, model, device, rank, world):
+    """The plans of one timed step and the pool they run on.  grouped / d1024:
+    one wave of every parent's depth-0 siblings; halving: one wave per round,
+    round r evaluating one node per surviving arm at depth r (its parent chain
+    from the earlier rounds as suffix keys)."""
+    from imba_chess_b200 import synth
+    from imba_chess_b200.kvpool import KVSequence
+    from imba_chess_b200.plan import piece_ids_from_tokens, side_ids_from_tokens
+    from imba_chess_b200.shard import shard_games
+    from imba_chess_b200.steps import WaveGroup, wave_plan
+
+    if args.workload != "halving":
+        _, wave = workload(args, rank, world)
+        lens = wave.prefix_lens
+        B = wave.num_rows
+        pool = model.new_pool(sum(-(-n // 16) for n in lens) + 4 * (-(-B // 16)) + 64)
+        seqs = [KVSequence(pool) for _ in lens]
+        prefill(model, pool, seqs, wave.prefix_tokens, device)
+        order = np.argsort(wave.group_index, kind="stable")
+        arenas = [KVSequence(pool) for _ in lens]
+        counts = np.bincount(wave.group_index, minlength=len(lens))
+        groups = [WaveGroup(prefix=seqs[g], prefix_len=lens[g], arena=arenas[g], chains=[[]] * int(counts[g]))
+                  for g in range(len(lens))]
+        tok = synth.slice_tokens(wave.row_tokens, order)
+        plan, _ = wave_plan(groups, piece_ids_from_tokens(tok), side_ids_from_tokens(tok),
+                            [wave.legal_ids[i] for i in order])
+        return pool, [plan], wave
+    mine = shard_games(args.parents * world, rank, world)
+    rngs = [np.random.default_rng(1234 + i) for i in mine]
+    prefixes = [synth.game_tokens(r, int(r.integers(args.plies[0], args.plies[1] + 1)), dims) for r in rngs]
+    lens = [int(p["piece_ids"].shape[0]) for p in prefixes]
+    G, per_game = len(mine), sum(args.rounds)
+    pool = model.new_pool(sum(-(-n // 16) for n in lens) + G * (-(-per_game // 16) + 1) + 64)
+    seqs = [KVSequence(pool) for _ in lens]
+    prefill(model, pool, seqs, prefixes, device)
+    arenas = [KVSequence(pool) for _ in lens]
+    chains = [[[] for _ in range(args.rounds[0])] for _ in range(G)]
+    plans = []
+    for K in args.rounds:
+        groups = [WaveGroup(prefix=seqs[g], prefix_len=lens[g], arena=arenas[g], chains=[chains[g][a] for a in range(K)])
+                  for g in range(G)]
+        tok = synth.concat_tokens([synth.random_tokens(r, K, dims) for r in rngs])
+        legal = [synth.random_legal_ids(r, int(r.integers(20, 41)), dims.vocab) for r in rngs for _ in range(K)]
+        plan, own = wave_plan(groups, piece_ids_from_tokens(tok), side_ids_from_tokens(tok), legal)
+        for g in range(G):
+            for a in range(K):
+                chains[g][a] = chains[g][a] + [own[g][a]]
+        plans.append(plan)
+    return pool, plans, None
 
 
 # ----------------------------------------------------------------------
@@ -317,17 +423,25 @@ def algorithmic_work(dims, plan, eb=2):
     # the legal logits are fp32 gathers in the value / legal pass (policy rows
     # of the legal ids, mostly served from L2), so those two phases launch
     # nothing of their own.
-    attn_bytes = prefix_tokens * kv_tok + extras * kv_tok + R * H * dqk * eb + R * H * dv * (eb + eb)
-    return {
+    # With more than 8 heads a CTA holds half of them: attention writes fp32
+    # and the norm / gate is its own pass.
+    fused = H <= 8
+    attn_out = R * H * dv * (eb + eb) if fused else R * H * dv * 4
+    attn_bytes = prefix_tokens * kv_tok + extras * kv_tok + R * H * dqk * eb + attn_out
+    work = {
         "embed": ("tensor", 2.0 * board_mac * R, 1),
         "ln": ("hbm", R * d * (4 + eb), L),
         "uvqk_gemm": ("tensor", 2.0 * R * d * uvqk_n, L),
         "attention": ("hbm", attn_bytes, L),
+        "gate": ("hbm", R * H * dv * (4 + eb + eb), L),
         "out_gemm": ("tensor", 2.0 * R * H * dv * d, L),
         "final_ln": ("hbm", R * d * (4 + 4 + 2 * eb), 1),
         "value_gemm": ("tensor", 2.0 * R * d * (d // 2), 1),
         "value_legal": ("hbm", R * (d // 2) * 4 + nl * (d * 4 + 12) + R * (d * 4 + 16), 1),
     }
+    if fused:
+        del work["gate"]
+    return work
 
 
 def read_traffic():
@@ -363,40 +477,46 @@ def run_b200(args):
     from imba_chess_b200.shard import reduce_max, reduce_sum
     from imba_chess_b200.steps import WaveGroup, root_plan, wave_plan
 
-    dims, wave = workload(args, rank, world)
+    dims = synth.D1024 if args.workload == "d1024" else synth.D512
     sd = synth.make_state_dict(dims, 2, profile="reference")
     model = B200HSTUChessModel(sd, dtype=torch.bfloat16, device=device)
-    lens = wave.prefix_lens
-    B = wave.num_rows
-    pages_needed = sum(-(-n // 16) for n in lens) + 4 * (-(-B // 16)) + 64
-    pool = model.new_pool(pages_needed)
-    # Prefill every parent prefix (setup, untimed).
-    seqs = [KVSequence(pool) for _ in lens]
-    pplan, _ = root_plan(seqs, wave.prefix_tokens)
-    model.run(DeviceStep(pplan, device), pool)
-    torch.cuda.synchronize()
-    model.check_status()
-    # The wave: every parent's siblings at depth 0 in a fresh turn arena.
-    order = np.argsort(wave.group_index, kind="stable")
-    arenas = [KVSequence(pool) for _ in lens]
-    counts = np.bincount(wave.group_index, minlength=len(lens))
-    groups = [WaveGroup(prefix=seqs[g], prefix_len=lens[g], arena=arenas[g], chains=[[]] * int(counts[g]))
-              for g in range(len(lens))]
-    tok = synth.slice_tokens(wave.row_tokens, order)
-    from imba_chess_b200.plan import piece_ids_from_tokens, side_ids_from_tokens
-
-    plan, _ = wave_plan(groups, piece_ids_from_tokens(tok), side_ids_from_tokens(tok),
-                        [wave.legal_ids[i] for i in order])
-    R = plan.num_rows
-    NL = int(plan.legal_ids.shape[0])
-    dstep = DeviceStep(plan, device, pinned=True)
-    out = torch.empty(R + 2 * NL, dtype=torch.float32, device=device)
-    v_out, ll_out, lp_out = out[:R], out[R : R + NL], out[R + NL :]
+    pool, plans, wave = build_waves(args, dims, model, device, rank, world)
     stream = torch.cuda.current_stream(device)
     L = dims.num_layers
     n_ev = int(model._lib.imba_profile_event_count(model._handle))
 
     import ctypes
+
+    class Wave:
+        def __init__(self, plan):
+            self.plan = plan
+            self.R = plan.num_rows
+            self.NL = int(plan.legal_ids.shape[0])
+            self.dstep = DeviceStep(plan, device, pinned=True)
+            self.out = torch.empty(self.R + 2 * self.NL, dtype=torch.float32, device=device)
+            self.v, self.ll = self.out[: self.R], self.out[self.R : self.R + self.NL]
+            self.lp = self.out[self.R + self.NL :]
+            self.host_out = torch.empty(self.out.numel(), dtype=torch.float32, pin_memory=True)
+
+        def run(self):
+            model.run(self.dstep, pool, value_stm=self.v, legal_logits=self.ll, legal_logprob=self.lp)
+
+        def run_profiled(self, arr):
+            desc = self.dstep.desc
+            desc.value_stm = self.v.data_ptr()
+            desc.legal_logits = self.ll.data_ptr()
+            desc.legal_logprob = self.lp.data_ptr()
+            desc.logits = None
+            desc.value_logits = None
+            desc.hidden = None
+            desc.status = model._status.data_ptr()
+            ws = model.workspace(self.R)
+            code = model._lib.imba_step_profiled(model._handle, ctypes.byref(desc), ctypes.byref(pool.desc),
+                                                 ws.data_ptr(), ws.numel(), stream.cuda_stream, arr, n_ev)
+            _native.check(code, "imba_step_profiled")
+
+    waves = [Wave(p) for p in plans]
+    R = sum(w.R for w in waves)  # positions per step on this rank
 
     def make_events():
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
@@ -405,22 +525,9 @@ def run_b200(args):
         arr = (ctypes.c_void_p * n_ev)(*[e.cuda_event for e in evs])
         return evs, arr
 
-    def step_profiled(arr):
-        desc = dstep.desc
-        desc.value_stm = v_out.data_ptr()
-        desc.legal_logits = ll_out.data_ptr()
-        desc.legal_logprob = lp_out.data_ptr()
-        desc.logits = None
-        desc.value_logits = None
-        desc.hidden = None
-        desc.status = model._status.data_ptr()
-        ws = model.workspace(R)
-        code = model._lib.imba_step_profiled(model._handle, ctypes.byref(desc), ctypes.byref(pool.desc),
-                                             ws.data_ptr(), ws.numel(), stream.cuda_stream, arr, n_ev)
-        _native.check(code, "imba_step_profiled")
-
     def step_plain():
-        model.run(dstep, pool, value_stm=v_out, legal_logits=ll_out, legal_logprob=lp_out)
+        for w in waves:
+            w.run()
 
     for _ in range(args.warmup):
         step_plain()
@@ -446,10 +553,11 @@ def run_b200(args):
     # Per-phase breakdown: a separate pass of the same steps with CUDA events
     # between phases (the events add device time, so this pass is not the
     # headline number).
-    ev_sets = [make_events() for _ in range(args.steps)]
+    ev_sets = [[make_events() for _ in waves] for _ in range(args.steps)]
     torch.cuda.synchronize()
     for i in range(args.steps):
-        step_profiled(ev_sets[i][1])
+        for w, (_, arr) in zip(waves, ev_sets[i]):
+            w.run_profiled(arr)
     torch.cuda.synchronize()
     model.check_status()
     elapsed_ms = reduce_max(t_start.elapsed_time(t_end), device)
@@ -457,13 +565,21 @@ def run_b200(args):
     ms_per_step = elapsed_ms / args.steps
     value = rows_all * args.steps / (elapsed_ms / 1000.0)
 
-    # Per-phase device times (averaged over the timed steps).
+    # Per-phase device times (averaged over the timed steps, summed over the
+    # step's waves) and the algorithmic work of a step.
     acc = {p: 0.0 for p in PHASES}
-    for evs, _ in ev_sets:
-        for k, v in phase_times(evs, L).items():
-            acc[k] += v
+    for sets in ev_sets:
+        for evs, _ in sets:
+            for k, v in phase_times(evs, L).items():
+                acc[k] += v
     per_step = {k: v / args.steps for k, v in acc.items()}
-    work = algorithmic_work(dims, plan)
+    work = {}
+    for w in waves:
+        for k, (bound, amount, launches) in algorithmic_work(dims, w.plan).items():
+            b0, a0, l0 = work.get(k, (bound, 0.0, 0))
+            work[k] = (bound, a0 + amount * launches, l0 + launches)
+    # per-launch work: the step's total work over its launches
+    work = {k: (bnd, total / n, n) for k, (bnd, total, n) in work.items()}
     peaks, peak_src = load_peaks()
     traffic = read_traffic()
     kernels = {}
@@ -492,15 +608,16 @@ def run_b200(args):
         "peak": peaks["bf16_tflops_sustained"] if bound == "tensor" else peaks["hbm_gbs"],
         "unit": dk["unit"],
         "frac": dk["frac"],
-        "traffic": (traffic[dom] * R) if dom in traffic else None,
+        # the per-row DRAM traffic was captured on the grouped-decode wave
+        "traffic": traffic[dom] * R / len(waves) if dom in traffic and args.workload == "grouped" else None,
         "peak_source": f"{peak_src} (MEASURED_PEAKS.json: bf16 sustained / HBM copy)",
         "per_launch_work": amount,
         "step_roof_ms": round(t_roof_ms, 4),
         "step_frac": round(t_roof_ms / ms_per_step, 4),
     }
 
-    # End-to-end through the C ABI with host buffers, synchronised per wave.
-    host_out = torch.empty(R + 2 * NL, dtype=torch.float32, pin_memory=True)
+    # End-to-end through the C ABI with host buffers, synchronised per wave
+    # (a search reads each wave's results before it builds the next).
     lat = []
     e2e_start = torch.cuda.Event(enable_timing=True)
     e2e_end = torch.cuda.Event(enable_timing=True)
@@ -510,21 +627,22 @@ def run_b200(args):
                 dist.barrier()
             torch.cuda.synchronize()
             e2e_start.record(stream)
-        t0 = time.perf_counter()
-        dstep.buf.copy_(dstep.host, non_blocking=True)
-        step_plain()
-        host_out.copy_(out, non_blocking=True)
-        stream.synchronize()
-        if i >= args.warmup:
-            lat.append(time.perf_counter() - t0)
+        for w in waves:
+            t0 = time.perf_counter()
+            w.dstep.buf.copy_(w.dstep.host, non_blocking=True)
+            w.run()
+            w.host_out.copy_(w.out, non_blocking=True)
+            stream.synchronize()
+            if i >= args.warmup:
+                lat.append(time.perf_counter() - t0)
     e2e_end.record(stream)
     torch.cuda.synchronize()
     e2e_ms = reduce_max(e2e_start.elapsed_time(e2e_end), device)
     e2e = {
         "value": rows_all * args.steps / (e2e_ms / 1000.0),
         "unit": UNIT,
-        "h2d_bytes_per_step": int(dstep.h2d_bytes),
-        "d2h_bytes_per_step": int(host_out.numel() * 4),
+        "h2d_bytes_per_step": int(sum(w.dstep.h2d_bytes for w in waves)),
+        "d2h_bytes_per_step": int(sum(w.host_out.numel() * 4 for w in waves)),
         "p50_wave_latency_ms": round(1000.0 * statistics.median(lat), 3),
     }
 
@@ -546,12 +664,12 @@ def run_b200(args):
         "roofline": roofline,
         "kernels": kernels,
         "clocks": sampler.summary(),
-        "gpu_launches": int(args.steps * count_launches(dims, plan)),
+        "gpu_launches": int(args.steps * len(waves) * count_launches(dims, plans[0])),
     }
 
-    if rank == 0 and world == 1 and not args.no_service:
+    if rank == 0 and world == 1 and not args.no_service and wave is not None:
         line["service_api"] = service_api(args, dims, wave, sd, device)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and wave is not None:
         n_rows, times = cpu_oracle_rate(dims, wave, args.cpu_sample_parents, args.cpu_seconds)
         line["cpu_baseline"] = {
             "value": n_rows * len(times) / sum(times),
@@ -571,8 +689,9 @@ def run_b200(args):
 def count_launches(dims, plan):
     """Kernel launches of one bf16 wave step (legal logits only): board
     encoder, content projection GEMM, L x (input LN, uvqk GEMM, attention with
-    the fused norm / gate, output GEMM), final LN, value GEMM, value / legal."""
-    return 2 + 4 * dims.num_layers + 3
+    the fused norm / gate (a separate gate pass above 8 heads), output GEMM),
+    final LN, value GEMM, value / legal."""
+    return 2 + (4 if dims.num_heads <= 8 else 5) * dims.num_layers + 3
 
 
 def service_api(args, dims, wave, sd, device):
