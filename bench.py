@@ -21,8 +21,8 @@ Reported:
            CUDA events on the launching stream, max over ranks).
   e2e    - positions/s through the C-ABI step with host buffers: pinned
            host->device copy of the packed wave, the step, device->host copy
-           of value / legal logits / log-priors, synchronised every step; its
-           p50 per-wave latency.
+           of its results (v and the legal log-softmax), synchronised every
+           step; its p50 per-wave latency.
   service_api - the reference-compatible ActorInferenceServer.service() on
            the same wave (Python wire objects in and out), p50 latency.
   roofline - the dominant kernel's algorithmic work per launch over its
@@ -493,18 +493,19 @@ def run_b200(args):
             self.R = plan.num_rows
             self.NL = int(plan.legal_ids.shape[0])
             self.dstep = DeviceStep(plan, device, pinned=True)
-            self.out = torch.empty(self.R + 2 * self.NL, dtype=torch.float32, device=device)
-            self.v, self.ll = self.out[: self.R], self.out[self.R : self.R + self.NL]
-            self.lp = self.out[self.R + self.NL :]
+            # The step's results: v and the masked policy log-softmax at the
+            # legal ids (the workload's outputs), read back every e2e step.
+            self.out = torch.empty(self.R + self.NL, dtype=torch.float32, device=device)
+            self.v, self.lp = self.out[: self.R], self.out[self.R :]
             self.host_out = torch.empty(self.out.numel(), dtype=torch.float32, pin_memory=True)
 
         def run(self):
-            model.run(self.dstep, pool, value_stm=self.v, legal_logits=self.ll, legal_logprob=self.lp)
+            model.run(self.dstep, pool, value_stm=self.v, legal_logprob=self.lp)
 
         def run_profiled(self, arr):
             desc = self.dstep.desc
             desc.value_stm = self.v.data_ptr()
-            desc.legal_logits = self.ll.data_ptr()
+            desc.legal_logits = None
             desc.legal_logprob = self.lp.data_ptr()
             desc.logits = None
             desc.value_logits = None

@@ -1,11 +1,14 @@
-"""Build the in-tree shared library ``libimba_b200.so`` for sm_100a.
+"""Build the in-tree shared library ``libimba_b200.so`` for sm_100a and the
+host-path extension ``_hostpath``.
 
     python -m imba_chess_b200.build [--force] [--verbose]
 
 Each ``csrc/*.cu`` is compiled by nvcc in parallel into ``_build/`` and the
 objects are linked into ``imba_chess_b200/libimba_b200.so`` (a plain C-ABI
 library; no torch headers).  Objects are rebuilt only when a source or header
-is newer than the object.
+is newer than the object.  ``host/hostpath.cpp`` (CPython API, the wave
+service's request packing and response building) is compiled by g++ into
+``imba_chess_b200/_hostpath<EXT_SUFFIX>``.
 """
 
 from __future__ import annotations
@@ -17,6 +20,7 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
@@ -24,6 +28,8 @@ CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libimba_b200.so")
+HOST_SRC = os.path.join(PKG, "host", "hostpath.cpp")
+HOST_EXT = os.path.join(PKG, "_hostpath" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
@@ -86,12 +92,28 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIB
 
 
+def build_host(force: bool = False) -> str:
+    """Compile the CPython host-path extension (g++, -O2)."""
+    if not force and os.path.exists(HOST_EXT) and os.path.getmtime(HOST_EXT) >= os.path.getmtime(HOST_SRC):
+        return HOST_EXT
+    cxx = os.environ.get("CXX") or shutil.which("g++") or "g++"
+    inc = sysconfig.get_paths()["include"]
+    tmp = HOST_EXT + ".tmp"
+    cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden", "-I", inc, HOST_SRC, "-o", tmp]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        raise RuntimeError(f"host extension build failed:\n{proc.stdout}\n{proc.stderr}")
+    os.replace(tmp, HOST_EXT)
+    return HOST_EXT
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     a = ap.parse_args()
     print(build(force=a.force, verbose=a.verbose))
+    print(build_host(force=a.force))
 
 
 if __name__ == "__main__":

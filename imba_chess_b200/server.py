@@ -24,25 +24,24 @@ What changes relative to the reference, and what does not:
 
 from __future__ import annotations
 
+import gc
 import time
 from dataclasses import dataclass, field
-from itertools import chain
-from operator import itemgetter
 from typing import Any
 
 import numpy as np
 import torch
 
-from . import _native
+from . import _hostpath, _native
 from .kvpool import PAGE, KVPool, KVSequence
 from .model import B200HSTUChessModel
 from .plan import DeviceStep, StepPlan
-from .steps import WaveGroup, ids_csr, root_plan, wave_plan
+from .steps import WaveGroup, root_plan, wave_plan
 from .protocol import RootEvalResponse, WaveResponse, is_root_request, is_wave_request
 from .synth import EVENT_TOKEN_ID, TOKEN_FIELDS
 
 _TOKEN_FIELDS = TOKEN_FIELDS
-_STATE_FIELDS = itemgetter("turn_id", "castle_id", "ep_file_id", "halfmove_bucket_id", "fullmove_bucket_id")
+_NO_PARENT = -(2**63)  # parent id the host path reports for parent_id None
 
 
 @dataclass
@@ -298,9 +297,20 @@ class ActorInferenceServer:
     def _service_waves(self, requests: list) -> list:
         if not requests:
             return []
+        # A wave allocates ~R lists and ~R x n_legal floats for its responses;
+        # the cyclic collector is paused meanwhile (none of them form cycles).
+        paused = gc.isenabled()
+        if paused:
+            gc.disable()
+        try:
+            return self._service_waves_impl(requests)
+        finally:
+            if paused:
+                gc.enable()
+
+    def _service_waves_impl(self, requests: list) -> list:
         t0 = time.perf_counter()
         turns: list[_TurnState] = []
-        chains_per_req: list[list[list[int]]] = []
         for req in requests:
             key = (int(req.worker_id), int(req.turn_id))
             turn = self._turns.get(key)
@@ -309,35 +319,32 @@ class ActorInferenceServer:
                     f"WaveRequest for worker={req.worker_id} turn={req.turn_id} has no registered root eval -- "
                     "missing/out-of-order RootEvalRequest, or release_turn() already freed this turn."
                 )
-            chains = [turn.node_chains[row.parent_id] if row.parent_id is not None else [] for row in req.rows]
             turns.append(turn)
-            chains_per_req.append(chains)
-        # Tokens (one per row), in request order, converted with C-level iterators.
-        rows = [row for req in requests for row in req.rows]
-        R = len(rows)
-        states = [row.board_state for row in rows]
-        try:  # bytes() converts each 64-int list in C and rejects values outside 0..255
-            piece = np.frombuffer(b"".join([bytes(bs["piece_ids"]) for bs in states]), dtype=np.uint8)
-        except (ValueError, TypeError) as exc:
-            raise ValueError("piece_ids values must be in [0, 12]") from exc
-        if piece.size != R * 64:
-            raise ValueError("every board_state must carry 64 piece_ids")
-        piece = piece.reshape(R, 64)
-        if piece.size and piece.max() > 12:
-            raise ValueError("piece_ids values must be in [0, 12]")
-        side = np.empty((R, 7), dtype=np.int64)
+        # Rows in request order, packed by the C++ host path (ids, boards,
+        # legal CSR, node / parent ids) in one pass over the wire objects.
+        counts = [len(req.rows) for req in requests]
+        R = sum(counts)
+        piece = np.empty((R, 64), dtype=np.uint8)
+        side = np.empty((R, 7), dtype=np.int32)
+        _, loff_b, lids_b, node_b, parent_b = _hostpath.pack_wave_rows(requests, piece, side)
         side[:, 0] = EVENT_TOKEN_ID
-        if R:
-            side[:, 1:6] = np.array(list(map(_STATE_FIELDS, states)), dtype=np.int64).reshape(R, 5)
-            side[:, 6] = np.fromiter((row.prev_move_vocab_id for row in rows), dtype=np.int64, count=R)
+        node_ids = np.frombuffer(node_b, dtype=np.int64).tolist()
+        parent_ids = np.frombuffer(parent_b, dtype=np.int64).tolist()
+        chains_per_req: list[list[list[int]]] = []
+        r0 = 0
+        for turn, n in zip(turns, counts):
+            nc = turn.node_chains
+            chains_per_req.append([nc[p] if p != _NO_PARENT else [] for p in parent_ids[r0 : r0 + n]])
+            r0 += n
         # Arena rows (logical ids exactly as _KVArena.append mints them) and slots.
         groups = []
         for turn, chains in zip(turns, chains_per_req):
             if turn.arena is None:
                 turn.arena = KVSequence(self.pool)
             groups.append(WaveGroup(prefix=turn.seq, prefix_len=turn.prefix_len, arena=turn.arena, chains=chains))
-        plan, own_rows = wave_plan(groups, piece, side.clip(-(2**31), 2**31 - 1).astype(np.int32),
-                                   [row.legal_vocab_ids for row in rows])
+        plan, own_rows = wave_plan(groups, piece, side, None,
+                                   legal_csr=(np.frombuffer(loff_b, dtype=np.int32),
+                                              np.frombuffer(lids_b, dtype=np.int32)))
         loff = plan.legal_off
         self._sync_if_profiling()
         t1 = time.perf_counter()
@@ -348,17 +355,14 @@ class ActorInferenceServer:
         self.stats["wave_calls"] += 1
         self.stats["wave_reqs"] += len(requests)
         self.stats["wave_rows"] += R
+        rows_out = _hostpath.wave_responses(counts, value_stm, legal_flat, loff)
         responses = []
-        values = value_stm.tolist()
-        legal_all = legal_flat.tolist()
-        offs = loff.tolist()
         r0 = 0
-        for req, turn, chains, own in zip(requests, turns, chains_per_req, own_rows):
+        for turn, chains, own, n, rows_g in zip(turns, chains_per_req, own_rows, counts, rows_out):
             nc = turn.node_chains
-            for row, ch, own_row in zip(req.rows, chains, own):
-                nc[row.node_id] = ch + [own_row]
-            n = len(req.rows)
-            responses.append(WaveResponse(rows=[(values[i], legal_all[offs[i] : offs[i + 1]]) for i in range(r0, r0 + n)]))
+            for nid, ch, own_row in zip(node_ids[r0 : r0 + n], chains, own):
+                nc[nid] = ch + [own_row]
+            responses.append(WaveResponse(rows=rows_g))
             r0 += n
         self._sync_if_profiling()
         self.stats["wave_post_s"] += time.perf_counter() - t2

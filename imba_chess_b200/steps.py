@@ -98,9 +98,12 @@ class WaveGroup:
     chains: list[list[int]]
 
 
-def wave_plan(groups: list[WaveGroup], piece: np.ndarray, side: np.ndarray, legal_ids: list) -> tuple[StepPlan, list[list[int]]]:
+def wave_plan(groups: list[WaveGroup], piece: np.ndarray, side: np.ndarray, legal_ids: list | None,
+              legal_csr: tuple[np.ndarray, np.ndarray] | None = None) -> tuple[StepPlan, list[list[int]]]:
     """Grouped decode of every group's rows (rows ordered group by group).
-    Returns the plan and, per group, the arena rows minted for its rows."""
+    Legal ids come as per-row lists or, already packed, as ``legal_csr`` =
+    (int32 offsets [R+1], int32 ids).  Returns the plan and, per group, the
+    arena rows minted for its rows."""
     G = len(groups)
     counts = np.fromiter((len(g.chains) for g in groups), dtype=np.int64, count=G)
     R = int(counts.sum())
@@ -140,7 +143,7 @@ def wave_plan(groups: list[WaveGroup], piece: np.ndarray, side: np.ndarray, lega
         extra_pos[is_chain] = (np.repeat(prow, per_row) + j)[is_chain]
     gpo = np.zeros(G + 1, dtype=np.int64)
     np.cumsum([len(p) for p in pages], out=gpo[1:])
-    loff, lids = ids_csr(legal_ids)
+    loff, lids = legal_csr if legal_csr is not None else ids_csr(legal_ids)
     plan = StepPlan(
         piece_ids=piece,
         side_ids=side,
