@@ -111,6 +111,17 @@ class B200HSTUChessModel:
         dev = device if device is not None else "cuda"
         return cls(sd, dtype=dtype or torch.bfloat16, device=dev)
 
+    @classmethod
+    def from_checkpoint(cls, path, *, dtype: torch.dtype = torch.bfloat16, device=None,
+                        require_value_head: bool = False) -> "B200HSTUChessModel":
+        """Load a reference checkpoint file (plain or Ignite state dict) with
+        the reference loader's key normalisation, value-head guard and strict
+        key check (``weights.load_checkpoint_state_dict``)."""
+        from .weights import load_checkpoint_state_dict
+
+        sd = load_checkpoint_state_dict(path, require_value_head=require_value_head)
+        return cls(sd, dtype=dtype, device=device if device is not None else "cuda")
+
     def eval(self) -> "B200HSTUChessModel":
         return self
 

@@ -64,6 +64,57 @@ def normalize_state_dict(state_dict: Mapping[str, Any]) -> dict[str, torch.Tenso
     return out
 
 
+def load_checkpoint_state_dict(path, *, require_value_head: bool = False) -> dict[str, torch.Tensor]:
+    """A checkpoint file's normalised state dict, read like the reference's
+    ``load_hstu_checkpoint`` (src/imba_chess/eval/position_evaluator.py:118-167):
+    a plain state dict or an Ignite checkpoint holding it under ``"model"``
+    (``TypeError`` otherwise), ``module.`` / ``_orig_mod.`` prefixes stripped,
+    ``ValueError`` when a value head is required but absent, and a strict
+    key / shape check against the architecture the tensors describe
+    (``RuntimeError`` listing missing, unexpected and mis-shaped keys, as
+    ``load_state_dict(strict=True)`` would)."""
+    checkpoint = torch.load(path, map_location="cpu")
+    state_dict = checkpoint["model"] if isinstance(checkpoint, dict) and "model" in checkpoint else checkpoint
+    if not isinstance(state_dict, dict):
+        raise TypeError("Checkpoint must be a model state_dict or Ignite checkpoint containing key 'model'.")
+    for key in state_dict:
+        if not isinstance(key, str):
+            raise TypeError("Checkpoint state_dict keys must be strings")
+    sd = normalize_state_dict(state_dict)
+    has_value = any(k.startswith("value_head.") for k in sd)
+    if require_value_head and not has_value:
+        raise ValueError(
+            "model_move_policy in {value_rerank,value_search_d2} requires a checkpoint with value_head "
+            "parameters, but checkpoint contains no 'value_head.*' keys."
+        )
+    check_state_dict(sd)
+    return sd
+
+
+def check_state_dict(sd: Mapping[str, torch.Tensor]) -> None:
+    """Strict key and shape check of a normalised state dict against the
+    reference architecture its tensors describe."""
+    from .synth import ModelDims, state_dict_shapes
+
+    dims = infer_dims(sd)
+    expected = state_dict_shapes(ModelDims(
+        model_dim=dims.model_dim, num_layers=dims.num_layers, num_heads=dims.num_heads,
+        attention_dim=dims.attention_dim, linear_dim=dims.linear_dim, vocab=dims.vocab, max_pos=dims.max_pos,
+        halfmove_vocab=dims.halfmove_vocab, fullmove_vocab=dims.fullmove_vocab, value_head=dims.value_head))
+    missing = [k for k in expected if k not in sd]
+    unexpected = [k for k in sd if k not in expected]
+    shapes = [f"{k}: {tuple(sd[k].shape)} vs {v}" for k, v in expected.items() if k in sd and tuple(sd[k].shape) != v]
+    if missing or unexpected or shapes:
+        parts = []
+        if missing:
+            parts.append("Missing key(s): " + ", ".join(missing))
+        if unexpected:
+            parts.append("Unexpected key(s): " + ", ".join(unexpected))
+        if shapes:
+            parts.append("Size mismatch: " + "; ".join(shapes))
+        raise RuntimeError("Error(s) in loading state_dict for HSTUChessModel: " + " | ".join(parts))
+
+
 def infer_dims(sd: Mapping[str, torch.Tensor]) -> Dims:
     d = int(sd["final_norm.weight"].shape[0])
     L = 0
