@@ -51,9 +51,9 @@ __device__ __forceinline__ void put4(bf16* p, float a, float b, float c, float d
 }
 
 // uvqk projection epilogue: SiLU, then the reference's split order u | v | q | k
-// (src/imba_chess/model/hstu_attention.py:310-325).  u goes to the fp32 gate
-// buffer, q to the query buffer, and k / v straight into the row's slot of the
-// paged KV pool (the KV append, fused).
+// (src/imba_chess/model/hstu_attention.py:310-325).  u goes to the gate input
+// buffer, q to the query buffer (both in the model dtype), and k / v straight
+// into the row's slot of the paged KV pool (the KV append, fused).
 template <typename T>
 struct EpiUVQK {
   T* u;
@@ -135,47 +135,10 @@ struct EpiUVQK {
   };
   __device__ __forceinline__ Ctx begin(int r, int /*n0*/, int /*bn*/) const { return Ctx{(int64_t)dst_slot[r]}; }
 
-  // Per-thread rows measured faster than the staged chunk for this epilogue
-  // (its stores are 64-128 B per row and chunk; the staging round trip and
-  // the per-row slot lookups cost more than they save).
+  // Per-thread rows (kStaged false): a staged 32 x 32 chunk variant of this
+  // epilogue measured slower (its stores are 64-128 B per row and chunk; the
+  // staging round trip and the per-row slot lookups cost more than they save).
   static constexpr bool kStaged = false;
-  __device__ __forceinline__ int row_tag(int r) const { return dst_slot[r]; }
-  // Staged chunk (see staged4); tags[rr] = KV slot of row row0 + rr.  A chunk
-  // never straddles a head or a region (d_qk, d_v multiples of 32).
-  __device__ __forceinline__ void tile32(const float* s, const int* tags, int row0, int c0, int M, int N,
-                                         int lane) const {
-    if (c0 >= N) return;
-    const int cg = 4 * (lane & 7), r4 = lane >> 3;
-    const int hdv = g.H * g.dv, hdq = g.H * g.dqk;
-    const int region = c0 < hdv ? 0 : (c0 < 2 * hdv ? 1 : (c0 < 2 * hdv + hdq ? 2 : 3));
-#pragma unroll 2
-    for (int k = 0; k < 8; ++k) {
-      const int rr = r4 + 4 * k, row = row0 + rr;
-      if (row >= M) continue;
-      const float4 a = staged4(s, rr, cg);
-      const float y0 = silu_tanh(a.x), y1 = silu_tanh(a.y), y2 = silu_tanh(a.z), y3 = silu_tanh(a.w);
-      if (region == 0) {
-        put4(u + (size_t)row * hdv + c0 + cg, y0, y1, y2, y3);
-      } else if (region == 2) {
-        put4(q + (size_t)row * hdq + (c0 - 2 * hdv) + cg, y0, y1, y2, y3);
-      } else {
-        const int64_t slot = tags[rr];
-        if (slot < 0 || slot >= g.num_slots) {
-          report(status, IMBA_ERR_RANGE);
-          continue;
-        }
-        T* dst;
-        if (region == 1) {
-          const int c = c0 - hdv;
-          dst = pool + g.v_off(slot, layer, c / g.dv) + (c % g.dv) + cg;
-        } else {
-          const int c = c0 - 2 * hdv - hdq;
-          dst = pool + g.k_off(slot, layer, c / g.dqk) + (c % g.dqk) + cg;
-        }
-        put4(dst, y0, y1, y2, y3);
-      }
-    }
-  }
 
   // 32 consecutive columns starting at c0 (a multiple of 32; d_qk and d_v
   // are multiples of 32, so a chunk never straddles a head or a region).
