@@ -222,3 +222,87 @@ def test_bf16_wave_matches_fp32_oracle(dims, n_parents, plies, siblings):
     assert max_dl <= BF16_ATOL, max_dl
     assert max_dv <= BF16_DV, max_dv
     assert top1 >= BF16_TOP1, top1
+
+
+def test_bf16_halving_chains_match_fp32_oracle():
+    """Sequential-halving rounds through the server (arms 6 -> 3 -> 2 per
+    parent, round r evaluating one node per surviving arm at depth r whose
+    suffix is the arm's chain in the turn arena) against the fp32 oracle fed
+    the oracle's own KV of the chain nodes as suffix keys."""
+    from imba_chess_b200.protocol import RootEvalRequest, WaveRequest, WaveRow
+    from imba_chess_b200.server import ActorInferenceServer
+
+    dims = synth.D512
+    sd = synth.make_state_dict(dims, 3, profile="reference")
+    model = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
+    server = ActorInferenceServer(model=model, device="cuda:0", dtype=torch.bfloat16, kv_pool_pages=1024)
+    orc = OracleModel(sd, dims)
+    rng = np.random.default_rng(77)
+    G, rounds = 4, (6, 3, 2)
+    prefixes = [synth.game_tokens(rng, int(rng.integers(20, 60)), dims) for _ in range(G)]
+    lens = [int(p["piece_ids"].shape[0]) for p in prefixes]
+    roots = []
+    for g, pt in enumerate(prefixes):
+        ba = {k: v.tolist() for k, v in pt.items()}
+        ba.update(total_tokens=lens[g], seq_offsets=[0, lens[g]])
+        roots.append(RootEvalRequest(worker_id=g, turn_id=0, legal_vocab_ids=[2, 3], batch_arrays=ba))
+    server.service(roots)
+    pref = [orc.forward(pt, [0, lens[g]])["kv_caches"] for g, pt in enumerate(prefixes)]
+    max_p = max(lens)
+    grouped = []
+    for l in range(dims.num_layers):
+        ks = np.stack([np.pad(p[l][0], ((0, 0), (0, max_p - p[l][0].shape[1]), (0, 0))) for p in pref])
+        vs = np.stack([np.pad(p[l][1], ((0, 0), (0, max_p - p[l][1].shape[1]), (0, 0))) for p in pref])
+        grouped.append((ks, vs))
+    node_kv = {}  # node id -> per-layer (k [H, d], v [H, d]) from the oracle
+    keys = ("turn_id", "castle_id", "ep_file_id", "halfmove_bucket_id", "fullmove_bucket_id")
+    max_dl = max_dv = 0.0
+    agree = total = 0
+    for r, K in enumerate(rounds):
+        tok = synth.random_tokens(rng, G * K, dims)
+        legal = [synth.random_legal_ids(rng, int(rng.integers(20, 41)), dims.vocab) for _ in range(G * K)]
+        reqs, nodes, parents = [], [], []
+        for g in range(G):
+            rows = []
+            for a in range(K):
+                i = g * K + a
+                nid = 1000 * g + 100 * r + a
+                pid = None if r == 0 else 1000 * g + 100 * (r - 1) + a
+                bs = {"piece_ids": tok["piece_ids"][i].tolist(), **{k: int(tok[k][i]) for k in keys}}
+                rows.append(WaveRow(node_id=nid, parent_id=pid, prev_move_vocab_id=int(tok["prev_move_id"][i]),
+                                    board_state=bs, legal_vocab_ids=legal[i].tolist()))
+                nodes.append(nid)
+                parents.append(pid)
+            reqs.append(WaveRequest(worker_id=g, turn_id=0, rows=rows))
+        resp = server.service(reqs)
+        got = [row for wr in resp for row in wr.rows]
+        gi = np.repeat(np.arange(G), K)
+        kw = {}
+        if r > 0:
+            chains = []
+            for pid in parents:
+                ch, p = [], pid
+                while p is not None:  # the arm's nodes of rounds 0 .. r - 1
+                    ch.append(p)
+                    p = p - 100 if (p % 1000) >= 100 else None
+                chains.append(ch[::-1])
+            sk = [np.stack([np.stack([node_kv[n][l][0] for n in ch], axis=1) for ch in chains]) for l in range(dims.num_layers)]
+            sv = [np.stack([np.stack([node_kv[n][l][1] for n in ch], axis=1) for ch in chains]) for l in range(dims.num_layers)]
+            kw = dict(suffix_kv=list(zip(sk, sv)),
+                      suffix_positions=np.asarray(lens)[gi][:, None] + np.arange(r)[None, :],
+                      suffix_mask=np.ones((G * K, r), dtype=bool))
+        ref = orc.forward_decode_grouped(new_token_batch=tok, positions=np.asarray(lens)[gi] + r, group_index=gi,
+                                         prefix_kv_grouped=grouped, prefix_lens_list=lens, **kw)
+        for i, nid in enumerate(nodes):
+            node_kv[nid] = [(ref["kv"][l][0][i, :, 0], ref["kv"][l][1][i, :, 0]) for l in range(dims.num_layers)]
+        ref_v = value_stm(ref["value_logits"])
+        for i in range(G * K):
+            v_got, ll_got = got[i]
+            ll_ref = ref["logits"][i, legal[i]]
+            max_dl = max(max_dl, float(np.abs(np.asarray(ll_got) - ll_ref).max()))
+            max_dv = max(max_dv, abs(v_got - float(ref_v[i])))
+            agree += int(np.argmax(ll_got) == np.argmax(ll_ref))
+            total += 1
+    assert max_dl <= BF16_ATOL, max_dl
+    assert max_dv <= BF16_DV, max_dv
+    assert agree / total >= BF16_TOP1, agree / total
