@@ -60,6 +60,8 @@ WORKLOADS = {
     "grouped": {"parents": 256, "plies": (20, 200), "siblings": (20, 40), "rounds": None},
     "d1024": {"parents": 512, "plies": (300, 600), "siblings": (40, 40), "rounds": None},
     "halving": {"parents": 1024, "plies": (40, 250), "siblings": None, "rounds": (32, 16, 8, 4, 2)},
+    # games, plies log-uniform in [lo, hi], decode steps built (cycled when more are timed)
+    "prefill_decode": {"parents": 1024, "plies": (1, 300), "siblings": None, "rounds": (50,)},
 }
 UNIT = "positions/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -74,7 +76,9 @@ def parse_args():
     ap.add_argument("--workload", choices=list(WORKLOADS), default="grouped",
                     help="grouped: the headline grouped-decode wave (d512/8L); d1024: the same wave shape on "
                          "the d1024/16L/16H model with long prefixes; halving: sequential-halving search rounds "
-                         "with suffix chains (one step = every round of every game)")
+                         "with suffix chains (one step = every round of every game); prefill_decode: jagged "
+                         "prefill of every game (timed and reported apart), then one-token decode + KV append "
+                         "steps of every game (one step = one token per game)")
     ap.add_argument("--parents", type=int, default=None)
     ap.add_argument("--plies", type=int, nargs=2, default=None)
     ap.add_argument("--siblings", type=int, nargs=2, default=None)
@@ -252,7 +256,7 @@ def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
         return
-    if args.workload == "halving":
+    if args.workload in ("halving", "prefill_decode"):
         print(json.dumps({"impl": "reference", "unavailable": "the CPU reference arm is timed on the grouped-decode "
                                                               "wave workloads only"}), flush=True)
         return
@@ -287,6 +291,16 @@ def run_reference(args):
 
 
 def workload_config(args):
+    if args.workload == "prefill_decode":
+        return {
+            "workload": "jagged prefill + incremental decode: bf16 HSTU d512/8L/8H (max_pos 1024), "
+                        f"{args.parents} games, prefixes log-uniform in [{args.plies[0]},{args.plies[1]}] plies "
+                        "prefilled in packed batches of <= 32,768 tokens, then one-token decode + KV append "
+                        "steps of every game with its legal log-softmax and v (one step = one token per game)",
+            "games_per_gpu": args.parents,
+            "page_tokens": 16,
+            "l2": "inputs larger than L2 (prefix KV read per step > 126 MB at full size)",
+        }
     if args.workload == "halving":
         return {
             "workload": "sequential-halving search rounds: bf16 HSTU d512/8L/8H (max_pos 513), "
@@ -338,8 +352,34 @@ def build_waves(args, dims, model, device, rank, world):
     from imba_chess_b200.kvpool import KVSequence
     from imba_chess_b200.plan import piece_ids_from_tokens, side_ids_from_tokens
     from imba_chess_b200.shard import shard_games
-    from imba_chess_b200.steps import WaveGroup, wave_plan
+    from imba_chess_b200.steps import WaveGroup, root_plan, wave_plan
 
+    if args.workload == "prefill_decode":
+        mine = shard_games(args.parents * world, rank, world)
+        rngs = [np.random.default_rng(1234 + i) for i in mine]
+        lo, hi = np.log(args.plies[0]), np.log(args.plies[1])
+        plies = [int(np.exp(r.uniform(lo, hi))) for r in rngs]
+        prefixes = [synth.game_tokens(r, n, dims) for r, n in zip(rngs, plies)]
+        lens = [int(p["piece_ids"].shape[0]) for p in prefixes]
+        steps = args.rounds[0]
+        G = len(mine)
+        pool = model.new_pool(sum(-(-(n + steps) // 16) for n in lens) + G + 64)
+        seqs = [KVSequence(pool) for _ in lens]
+        prefill_plans = []
+        i = 0
+        while i < G:  # packed batches of <= 32,768 tokens
+            j, n = i, 0
+            while j < G and (j == i or n + lens[j] <= 32768):
+                n += lens[j]
+                j += 1
+            prefill_plans.append(root_plan(seqs[i:j], prefixes[i:j])[0])
+            i = j
+        plans = []
+        for _ in range(steps):
+            tok = [synth.random_tokens(r, 1, dims) for r in rngs]
+            legal = [synth.random_legal_ids(r, int(r.integers(20, 41)), dims.vocab) for r in rngs]
+            plans.append(root_plan(seqs, tok, legal_last=legal)[0])
+        return pool, plans, prefill_plans
     if args.workload != "halving":
         _, wave = workload(args, rank, world)
         lens = wave.prefix_lens
@@ -477,10 +517,16 @@ def run_b200(args):
     from imba_chess_b200.shard import reduce_max, reduce_sum
     from imba_chess_b200.steps import WaveGroup, root_plan, wave_plan
 
-    dims = synth.D1024 if args.workload == "d1024" else synth.D512
+    if args.workload == "d1024":
+        dims = synth.D1024
+    elif args.workload == "prefill_decode":
+        dims = synth.ModelDims(512, 8, 8, max_pos=1024)
+    else:
+        dims = synth.D512
     sd = synth.make_state_dict(dims, 2, profile="reference")
     model = B200HSTUChessModel(sd, dtype=torch.bfloat16, device=device)
-    pool, plans, wave = build_waves(args, dims, model, device, rank, world)
+    pool, plans, extra = build_waves(args, dims, model, device, rank, world)
+    wave = extra if args.workload in ("grouped", "d1024") else None
     stream = torch.cuda.current_stream(device)
     L = dims.num_layers
     n_ev = int(model._lib.imba_profile_event_count(model._handle))
@@ -517,7 +563,29 @@ def run_b200(args):
             _native.check(code, "imba_step_profiled")
 
     waves = [Wave(p) for p in plans]
-    R = sum(w.R for w in waves)  # positions per step on this rank
+    cycle = args.workload == "prefill_decode"  # one prebuilt decode step per bench step
+
+    def step_waves(i):
+        return [waves[i % len(waves)]] if cycle else waves
+
+    R = sum(w.R for w in step_waves(0))  # positions per step on this rank
+    prefill_info = None
+    if args.workload == "prefill_decode":
+        # The jagged prefill, timed apart (device time of its packed batches).
+        psteps = [DeviceStep(p, device) for p in extra]
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for ds in psteps:
+            model.run(ds, pool)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        model.check_status()
+        ntok = sum(p.num_rows for p in extra)
+        pms = e0.elapsed_time(e1)
+        prefill_info = {"tokens": int(ntok), "batches": len(extra), "ms": round(pms, 3),
+                        "tokens_per_s": ntok / (pms / 1000.0)}
 
     def make_events():
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
@@ -526,12 +594,12 @@ def run_b200(args):
         arr = (ctypes.c_void_p * n_ev)(*[e.cuda_event for e in evs])
         return evs, arr
 
-    def step_plain():
-        for w in waves:
+    def step_plain(i):
+        for w in step_waves(i):
             w.run()
 
-    for _ in range(args.warmup):
-        step_plain()
+    for i in range(args.warmup):
+        step_plain(i)
     torch.cuda.synchronize()
     model.check_status()
     sampler = ClockSampler(local)
@@ -544,7 +612,7 @@ def run_b200(args):
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
     for i in range(args.steps):
-        step_plain()
+        step_plain(i)
     t_end.record(stream)
     torch.cuda.synchronize()
     if world > 1:
@@ -554,10 +622,10 @@ def run_b200(args):
     # Per-phase breakdown: a separate pass of the same steps with CUDA events
     # between phases (the events add device time, so this pass is not the
     # headline number).
-    ev_sets = [[make_events() for _ in waves] for _ in range(args.steps)]
+    ev_sets = [[make_events() for _ in step_waves(i)] for i in range(args.steps)]
     torch.cuda.synchronize()
     for i in range(args.steps):
-        for w, (_, arr) in zip(waves, ev_sets[i]):
+        for w, (_, arr) in zip(step_waves(i), ev_sets[i]):
             w.run_profiled(arr)
     torch.cuda.synchronize()
     model.check_status()
@@ -575,12 +643,13 @@ def run_b200(args):
                 acc[k] += v
     per_step = {k: v / args.steps for k, v in acc.items()}
     work = {}
-    for w in waves:
-        for k, (bound, amount, launches) in algorithmic_work(dims, w.plan).items():
-            b0, a0, l0 = work.get(k, (bound, 0.0, 0))
-            work[k] = (bound, a0 + amount * launches, l0 + launches)
-    # per-launch work: the step's total work over its launches
-    work = {k: (bnd, total / n, n) for k, (bnd, total, n) in work.items()}
+    for i in range(args.steps):
+        for w in step_waves(i):
+            for k, (bound, amount, launches) in algorithmic_work(dims, w.plan).items():
+                b0, a0, l0 = work.get(k, (bound, 0.0, 0))
+                work[k] = (bound, a0 + amount * launches, l0 + launches)
+    # per-launch work: the timed steps' total work over their launches; launches per step
+    work = {k: (bnd, total / n, n // args.steps) for k, (bnd, total, n) in work.items()}
     peaks, peak_src = load_peaks()
     traffic = read_traffic()
     kernels = {}
@@ -610,7 +679,7 @@ def run_b200(args):
         "unit": dk["unit"],
         "frac": dk["frac"],
         # the per-row DRAM traffic was captured on the grouped-decode wave
-        "traffic": traffic[dom] * R / len(waves) if dom in traffic and args.workload == "grouped" else None,
+        "traffic": traffic[dom] * R if dom in traffic and args.workload == "grouped" else None,
         "peak_source": f"{peak_src} (MEASURED_PEAKS.json: bf16 sustained / HBM copy)",
         "per_launch_work": amount,
         "step_roof_ms": round(t_roof_ms, 4),
@@ -628,7 +697,7 @@ def run_b200(args):
                 dist.barrier()
             torch.cuda.synchronize()
             e2e_start.record(stream)
-        for w in waves:
+        for w in step_waves(i):
             t0 = time.perf_counter()
             w.dstep.buf.copy_(w.dstep.host, non_blocking=True)
             w.run()
@@ -642,8 +711,8 @@ def run_b200(args):
     e2e = {
         "value": rows_all * args.steps / (e2e_ms / 1000.0),
         "unit": UNIT,
-        "h2d_bytes_per_step": int(sum(w.dstep.h2d_bytes for w in waves)),
-        "d2h_bytes_per_step": int(sum(w.host_out.numel() * 4 for w in waves)),
+        "h2d_bytes_per_step": int(sum(w.dstep.h2d_bytes for w in step_waves(0))),
+        "d2h_bytes_per_step": int(sum(w.host_out.numel() * 4 for w in step_waves(0))),
         "p50_wave_latency_ms": round(1000.0 * statistics.median(lat), 3),
     }
 
@@ -665,9 +734,11 @@ def run_b200(args):
         "roofline": roofline,
         "kernels": kernels,
         "clocks": sampler.summary(),
-        "gpu_launches": int(args.steps * len(waves) * count_launches(dims, plans[0])),
+        "gpu_launches": int(args.steps * len(step_waves(0)) * count_launches(dims, plans[0])),
     }
 
+    if prefill_info is not None:
+        line["prefill"] = prefill_info
     if rank == 0 and world == 1 and not args.no_service and wave is not None:
         line["service_api"] = service_api(args, dims, wave, sd, device)
     if rank == 0 and world == 1 and not args.no_cpu_baseline and wave is not None:
