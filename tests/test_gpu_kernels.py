@@ -211,3 +211,27 @@ def test_legal_gather_matches_full_projection(dtype, max_rows):
         z = ll[a:b]
         lse = z.max() + np.log(np.exp(z - z.max()).sum())
         assert np.abs(lp_b[a:b].double().cpu().numpy() - (z - lse)).max() <= 1e-5
+
+
+@pytest.mark.parametrize("dims", [synth.D512, synth.D1024], ids=["d512", "d1024"])
+def test_small_group_steps_match_simt(dims, monkeypatch):
+    """Steps of one or two rows per group (one token per game): the paged
+    attention's work items then hold a single live row block; it must match
+    the SIMT attention (IMBA_SIMT=attn) on the same steps, including the
+    second wave's one-token suffix chains."""
+    sd = synth.make_state_dict(dims, 19, profile="reference")
+    wave = synth.grouped_wave(dims, n_parents=40 if dims is synth.D512 else 12, plies=(20, 140), siblings=(1, 2),
+                              seed=41)
+    assert wave.num_rows <= 2 * len(wave.prefix_lens)
+    model_tc = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
+    monkeypatch.setenv("IMBA_SIMT", "attn")
+    model_simt = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
+    monkeypatch.delenv("IMBA_SIMT")
+    a = _run_wave(model_tc, dims, wave)
+    b = _run_wave(model_simt, dims, wave)
+    th, tl, tv = TOL["attn"]
+    scale = float(b["hidden"].abs().max())
+    assert torch.isfinite(a["logits"]).all()
+    assert float((a["hidden"] - b["hidden"]).abs().max()) <= th * scale
+    assert float((a["logits"] - b["logits"]).abs().max()) <= tl
+    assert float((a["value_logits"] - b["value_logits"]).abs().max()) <= tv
