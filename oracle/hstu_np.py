@@ -1,9 +1,10 @@
 """CPU oracle: a numpy (float32) restatement of the reference HSTU chess
 model's inference paths.
 
-TEST INFRASTRUCTURE ONLY.  This module is the checker for the CUDA path: only
-``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
-``bench.py`` may import it.  The product (``imba_chess_b200``) never does.
+TEST INFRASTRUCTURE ONLY.  This module is the oracle the CUDA path is tested
+against: only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline
+leg of ``bench.py`` may import it.  The product (``imba_chess_b200``) never
+does.
 
 Pinned against the reference itself: ``tests/golden/make_golden.py`` imports
 the reference package, runs it on seeded weights and inputs, and stores its
