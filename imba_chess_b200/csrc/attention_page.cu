@@ -30,9 +30,11 @@
 // per row afterwards: the four lanes that share a row split the 64-dim dot
 // product (a quad reduction), update the row's online softmax and add p v to
 // their O columns, reading K / V straight from the pool.
-// Epilogue: O / l; when the CTA holds every head, LayerNorm over the row's
-// H dv outputs (no affine, eps 1e-6) times u, stored in bf16 for the output
-// projection; otherwise fp32 O is stored and the gate runs as its own pass.
+// Epilogue: O / l; when the CTA holds every head, O is staged in shared
+// memory and after one barrier each warp takes whole rows: LayerNorm over the
+// row's H dv outputs (no affine, eps 1e-6, warp reductions) times u, stored
+// in bf16 for the output projection; otherwise fp32 O is stored and the gate
+// runs as its own pass.
 // Every wait is bounded; a timeout sets the status word and ends the CTA.
 // Semantics: src/imba_chess/model/hstu_attention.py :64-76, :81-132,
 // :134-148, :327-413 (attention), :185-190 (norm and gate).
@@ -74,6 +76,11 @@ struct PageParams {
   const bf16* u;  // [R, H dv]
   bf16* gated;    // [R, H dv]: fused norm + gate output (nullptr: store fp32 O to a.out)
 };
+
+// Row stride (floats) of the staged O tile: 4 floats of padding keep the
+// per-lane float2 writes of eight different rows in different banks.
+__host__ __device__ constexpr int otile_ld(int hdv) { return hdv + 4; }
+__host__ __device__ constexpr int otile_bytes(int hdv) { return kHalfRows * otile_ld(hdv) * 4; }
 
 __device__ __forceinline__ int bias_index(int kpos, int qpos, int max_pos) {
   int idx = kpos - qpos + (max_pos - 1);
@@ -331,12 +338,13 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
   uint8_t* ring = base;                                    // S stages: [K: HC x 2 KB][V: HC x 2 KB]
   uint8_t* qtile = ring + S * stage_bytes;                 // [HC][32 rows][128 B] queries, 128-byte swizzle
   const int bias_w = 2 * a.max_pos - 1;                    // ps_w row length
-  __half* bias_s = reinterpret_cast<__half*>(qtile + HC * kHalfRows * 128);  // [HC][bias_w] (kSmemBias)
+  // Fused epilogue: the item's O [32 rows][H dv + 4] fp32, staged.
+  float* otile = reinterpret_cast<float*>(qtile + HC * kHalfRows * 128);
+  const int otile_size = prm.gated ? otile_bytes(hdv) : 0;
+  __half* bias_s = reinterpret_cast<__half*>(qtile + HC * kHalfRows * 128 + otile_size);  // [HC][bias_w] (kSmemBias)
   const int bias_bytes = kSmemBias ? (HC * bias_w * 2 + 15) / 16 * 16 : 0;
   int* items = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bias_s) + bias_bytes);  // [2][kItemInts]
-  float* red_sum = reinterpret_cast<float*>(items + 2 * kItemInts);  // [kMaxHC][32] per-(head, row) sums
-  float* red_sq = red_sum + kMaxHC * kHalfRows;            // [kMaxHC][32]
-  int* misc = reinterpret_cast<int*>(red_sq + kMaxHC * kHalfRows);  // [0] abort flag, [1] pad
+  int* misc = items + 2 * kItemInts;                       // [0] abort flag, [1] pad
   uint64_t* full = reinterpret_cast<uint64_t*>(misc + 2);           // 8-byte aligned: even int count precedes
   uint64_t* empty = full + kMaxStages;
   uint64_t* item_full = empty + kMaxStages;
@@ -687,73 +695,67 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         if (r1 >= 0) *reinterpret_cast<float2*>(a.out + (size_t)r1 * hdv + col) = make_float2(rs.o[j][2], rs.o[j][3]);
       }
     } else {
-      // LayerNorm over the row's H dv outputs (two passes through shared
-      // per-(head, row) partial sums), then the gate by u.  The u loads are
-      // issued first so that their latency overlaps the two barriers.
-      uint32_t uv0[8], uv1[8];  // bf16 pairs
-      {
-        const uint32_t* u0 = reinterpret_cast<const uint32_t*>(prm.u + (size_t)(r0 >= 0 ? r0 : 0) * hdv + h * D + 2 * t);
-        const uint32_t* u1 = reinterpret_cast<const uint32_t*>(prm.u + (size_t)(r1 >= 0 ? r1 : 0) * hdv + h * D + 2 * t);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          uv0[j] = r0 >= 0 ? __ldg(u0 + 4 * j) : 0u;
-          uv1[j] = r1 >= 0 ? __ldg(u1 + 4 * j) : 0u;
-        }
-      }
-      float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        s0 += rs.o[j][0] + rs.o[j][1];
-        s1 += rs.o[j][2] + rs.o[j][3];
-      }
-      s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
-      s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
-      s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-      s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-      if (t == 0) {
-        red_sum[hl * kHalfRows + rl0] = s0;
-        red_sum[hl * kHalfRows + rl1] = s1;
-      }
-      bar_consumers(nct);
-      float mu0 = 0.f, mu1 = 0.f;
-      for (int k = 0; k < HC; ++k) {
-        mu0 += red_sum[k * kHalfRows + rl0];
-        mu1 += red_sum[k * kHalfRows + rl1];
-      }
-      mu0 /= (float)hdv;
-      mu1 /= (float)hdv;
-      float q0 = 0.f, q1 = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        q0 += (rs.o[j][0] - mu0) * (rs.o[j][0] - mu0) + (rs.o[j][1] - mu0) * (rs.o[j][1] - mu0);
-        q1 += (rs.o[j][2] - mu1) * (rs.o[j][2] - mu1) + (rs.o[j][3] - mu1) * (rs.o[j][3] - mu1);
-      }
-      q0 += __shfl_xor_sync(0xffffffffu, q0, 1);
-      q0 += __shfl_xor_sync(0xffffffffu, q0, 2);
-      q1 += __shfl_xor_sync(0xffffffffu, q1, 1);
-      q1 += __shfl_xor_sync(0xffffffffu, q1, 2);
-      if (t == 0) {
-        red_sq[hl * kHalfRows + rl0] = q0;
-        red_sq[hl * kHalfRows + rl1] = q1;
-      }
-      bar_consumers(nct);
-      float v0 = 0.f, v1 = 0.f;
-      for (int k = 0; k < HC; ++k) {
-        v0 += red_sq[k * kHalfRows + rl0];
-        v1 += red_sq[k * kHalfRows + rl1];
-      }
-      const float rs0 = 1.0f / sqrtf(v0 / (float)hdv + 1e-6f), rs1 = 1.0f / sqrtf(v1 / (float)hdv + 1e-6f);
+      // LayerNorm over the row's H dv outputs, then the gate by u: O goes to
+      // the shared O tile, and after one barrier each warp normalises whole
+      // rows (2 of the 32) with warp reductions; u and the gated output move
+      // as coalesced 8-byte pieces.  The u loads are issued first.
+      // Lane l owns columns 128 k + 4 l .. +3 (k < 4) of a row; warp w
+      // normalises rows w, w + 2 HC, ... (two rows when HC = 8).
+      const int ld = otile_ld(hdv);
+      auto col_ok = [&](int k) { return 128 * k + 4 * lane < hdv; };
+      uint2 uw[2][4];  // u of this warp's first two rows, loaded before the barrier
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
-        const int r = i ? r1 : r0;
-        if (r < 0) continue;
-        const float mu = i ? mu1 : mu0, rsd = i ? rs1 : rs0;
-        uint32_t* gr = reinterpret_cast<uint32_t*>(prm.gated + (size_t)r * hdv + h * D + 2 * t);
+        const int rr = warp + i * ncw;
+        const int gr = rr < n ? item[kItRows + rr] : -1;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t uw = i ? uv1[j] : uv0[j];
-          const float2 uv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&uw));
-          gr[4 * j] = pack_bf16(uv.x * ((rs.o[j][2 * i] - mu) * rsd), uv.y * ((rs.o[j][2 * i + 1] - mu) * rsd));
+        for (int k = 0; k < 4; ++k)
+          uw[i][k] = (gr >= 0 && col_ok(k))
+                         ? __ldg(reinterpret_cast<const uint2*>(prm.u + (size_t)gr * hdv + 128 * k + 4 * lane))
+                         : make_uint2(0u, 0u);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int col = hl * D + 8 * j + 2 * t;
+        *reinterpret_cast<float2*>(otile + rl0 * ld + col) = make_float2(rs.o[j][0], rs.o[j][1]);
+        *reinterpret_cast<float2*>(otile + rl1 * ld + col) = make_float2(rs.o[j][2], rs.o[j][3]);
+      }
+      bar_consumers(nct);
+      for (int i = 0, rr = warp; rr < n; ++i, rr += ncw) {
+        const int gr = item[kItRows + rr];
+        uint2 ur[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          ur[k] = i < 2 ? (i ? uw[1][k] : uw[0][k])
+                        : (col_ok(k) ? __ldg(reinterpret_cast<const uint2*>(prm.u + (size_t)gr * hdv + 128 * k +
+                                                                            4 * lane))
+                                     : make_uint2(0u, 0u));
+        float4 v[4];
+        float sum = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          v[k] = col_ok(k) ? *reinterpret_cast<const float4*>(otile + rr * ld + 128 * k + 4 * lane)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+          sum += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+        }
+        const float mu = warp_sum(sum) / (float)hdv;
+        float sq = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (col_ok(k))
+            sq += (v[k].x - mu) * (v[k].x - mu) + (v[k].y - mu) * (v[k].y - mu) + (v[k].z - mu) * (v[k].z - mu) +
+                  (v[k].w - mu) * (v[k].w - mu);
+        }
+        const float rsd = 1.0f / sqrtf(warp_sum(sq) / (float)hdv + 1e-6f);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (!col_ok(k)) continue;
+          const float2 u01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ur[k].x));
+          const float2 u23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ur[k].y));
+          uint2 o;
+          o.x = pack_bf16(u01.x * ((v[k].x - mu) * rsd), u01.y * ((v[k].y - mu) * rsd));
+          o.y = pack_bf16(u23.x * ((v[k].z - mu) * rsd), u23.y * ((v[k].w - mu) * rsd));
+          *reinterpret_cast<uint2*>(prm.gated + (size_t)gr * hdv + 128 * k + 4 * lane) = o;
         }
       }
     }
@@ -818,7 +820,7 @@ bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& 
   // table, item buffers and barriers.  The bias table is
   // kept in shared memory when at least 3 ring stages still fit.
   const size_t stage_bytes = 2 * (size_t)hc * kPageBytes;
-  const size_t fixed = 1024 + (size_t)hc * kHalfRows * 128 + kMetaBytes;
+  const size_t fixed = 1024 + (size_t)hc * kHalfRows * 128 + (fuse ? (size_t)otile_bytes(H * 64) : 0) + kMetaBytes;
   const size_t bias_bytes = ((size_t)hc * (2 * md.max_pos - 1) * 2 + 15) / 16 * 16;
   const bool smem_bias = fixed + bias_bytes + 3 * stage_bytes <= kSmemMax;
   size_t stages = (kSmemMax - fixed - (smem_bias ? bias_bytes : 0)) / stage_bytes;
