@@ -126,10 +126,12 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
   IMBA_CK(cudaMemsetAsync(w.counters, 0, kNumCounters * sizeof(int), s));
   if (md.dtype == IMBA_DTYPE_BF16 && !m->simt_board) {
     // tensor-core board encoder -> pooled [R, 192] split bf16; projection + embeddings in the GEMM epilogue
-    if (m->tc_board && board_tc_applies(md))
+    if (m->board_kind == 2 && board_tc_applies(md))
       IMBA_CK(launch_board_tc(md, st, static_cast<bf16*>(w.pooled), s));
-    else
+    else if (m->board_kind == 1)
       IMBA_CK(launch_board_mma(md, st, static_cast<bf16*>(w.pooled), s));
+    else
+      IMBA_CK(launch_board_hybrid(md, st, static_cast<bf16*>(w.pooled), s));
     EpiContent ec{w.x, nullptr, md.board_out_b, md.emb_seq, md.emb_turn, md.emb_castle, md.emb_ep, md.emb_halfmove,
                   md.emb_fullmove, md.emb_prev_move, md.emb_pos, st.side_ids, st.positions, d, md.halfmove_vocab,
                   md.fullmove_vocab, md.vocab, md.max_pos, sqrtf((float)d), st.status};
@@ -250,7 +252,7 @@ imba_status_t imba_model_create(const imba_model_desc* desc, imba_model** out) {
     m->simt_attn = strstr(sel, "attn") != nullptr;
     m->simt_board = strstr(sel, "board") != nullptr;
   }
-  if (const char* sel = getenv("IMBA_BOARD")) m->tc_board = strcmp(sel, "tc") == 0;
+  if (const char* sel = getenv("IMBA_BOARD")) m->board_kind = strcmp(sel, "tc") == 0 ? 2 : strcmp(sel, "mma") == 0 ? 1 : 0;
   if (desc->dtype == IMBA_DTYPE_BF16 && !m->simt_board) {
     // Split bf16 copy of the board projection for the content GEMM.
     void* w3 = nullptr;

@@ -102,7 +102,7 @@ struct imba_model {
   // creation selects the SIMT kernel of a component, for cross-checking).
   bool simt_attn = false;
   bool simt_board = false;
-  bool tc_board = false;  // tcgen05 board encoder (IMBA_BOARD=tc) instead of mma.sync
+  int board_kind = 0;  // board encoder: 0 tcgen05 + mma.sync (default), 1 mma.sync (IMBA_BOARD=mma), 2 tcgen05 (IMBA_BOARD=tc)
   // bf16 models with the tensor-core board encoder: [d, 192] bf16 split copy
   // of the board projection (device memory owned by the handle), or null.
   void* board_proj3 = nullptr;

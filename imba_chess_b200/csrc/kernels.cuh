@@ -20,11 +20,13 @@ struct AttnArgs {
 
 cudaError_t launch_embed(const imba_model_desc& md, const imba_step_desc& st, float* x, cudaStream_t s);
 // Board encoder -> pooled [R, 192] split bf16 ([hi | lo | hi] of the mean):
-// mma.sync (board_mma.cu, the default) or tcgen05 (board_tc.cu, selected
-// with IMBA_BOARD=tc when board_tc_applies).
+// tcgen05 projections + mma.sync attention (board_hybrid.cu, the default),
+// mma.sync only (board_mma.cu, IMBA_BOARD=mma) or tcgen05 only (board_tc.cu,
+// IMBA_BOARD=tc when board_tc_applies).
 bool board_tc_applies(const imba_model_desc& md);
 cudaError_t launch_board_tc(const imba_model_desc& md, const imba_step_desc& st, bf16* pooled, cudaStream_t s);
 cudaError_t launch_board_mma(const imba_model_desc& md, const imba_step_desc& st, bf16* pooled, cudaStream_t s);
+cudaError_t launch_board_hybrid(const imba_model_desc& md, const imba_step_desc& st, bf16* pooled, cudaStream_t s);
 // [d, 64] fp32 board projection -> [d, 192] bf16 [W_hi | W_hi | W_lo].
 cudaError_t build_board_proj_split(const imba_model_desc& md, bf16* out, cudaStream_t s);
 template <typename T>

@@ -12,7 +12,10 @@ on a full grouped-decode step: final hidden state, logits, value logits.
           the separate gate pass (the tensor-core kernel rounds softmax
           weights to bf16 for P.V); the second wave's rows carry suffix
           chains, so several gathered extra-key tiles per CTA are covered;
-* board - mma.sync board encoder (bf16 operands) vs the fp32 SIMT encoder;
+* board - the default board encoder (tcgen05 projections from TMEM in the
+          mma.sync fragment layout, mma.sync attention; bf16 operands) vs the
+          fp32 SIMT encoder;
+* board_mma - the mma.sync-only board encoder (IMBA_BOARD=mma) vs SIMT;
 * board_tc - the tcgen05 board encoder (IMBA_BOARD=tc: TMEM accumulators,
           two boards per M = 128 tile) vs the SIMT encoder.
 """
@@ -36,7 +39,7 @@ pytestmark = pytest.mark.gpu
 # error ~2^-11) where the SIMT epilogue uses the exact exponential form, so
 # the gemm bounds cover that as well as accumulation order.
 TOL = {"gemm": (2e-4, 5e-3, 2e-3), "attn": (2e-3, 2e-2, 5e-3), "board": (2e-3, 3e-2, 1e-2),
-       "board_tc": (2e-3, 3e-2, 1e-2)}
+       "board_mma": (2e-3, 3e-2, 1e-2), "board_tc": (2e-3, 3e-2, 1e-2)}
 
 
 def _run_wave(model, dims, wave, depth2=True):
@@ -71,18 +74,18 @@ def _run_wave(model, dims, wave, depth2=True):
     return out
 
 
-@pytest.mark.parametrize("component", ["gemm", "attn", "board", "board_tc"])
+@pytest.mark.parametrize("component", ["gemm", "attn", "board", "board_mma", "board_tc"])
 @pytest.mark.parametrize("dims,parents", [(synth.D512, 6), (synth.SMALL, 4), (synth.D256, 5), (synth.D1024, 2)],
                          ids=["d512", "d128", "d256", "d1024"])
 def test_tensor_core_kernel_matches_simt(component, dims, parents, monkeypatch):
     sd = synth.make_state_dict(dims, 9, profile="reference")
     plies = (20, 140) if component == "attn" else (20, 45)
     wave = synth.grouped_wave(dims, n_parents=parents, plies=plies, siblings=(20, 40), seed=99)
-    if component == "board_tc":
-        monkeypatch.setenv("IMBA_BOARD", "tc")
+    if component in ("board_tc", "board_mma"):
+        monkeypatch.setenv("IMBA_BOARD", component[6:])
     model_tc = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
     monkeypatch.delenv("IMBA_BOARD", raising=False)
-    monkeypatch.setenv("IMBA_SIMT", "board" if component == "board_tc" else component)
+    monkeypatch.setenv("IMBA_SIMT", "board" if component.startswith("board") else component)
     model_simt = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
     monkeypatch.delenv("IMBA_SIMT")
     a = _run_wave(model_tc, dims, wave)
