@@ -97,16 +97,23 @@ __device__ __forceinline__ uint32_t exp2_bf16x2(uint32_t x) {
   return y;
 }
 
-// SiLU of a bf16 pair as v / 2 * (1 + tanh(v / 2)) with the hardware tanh
-// (the hidden activations are bf16 operands of the second MLP product).
-__device__ __forceinline__ uint32_t silu_bf16x2(float v0, float v1) {
-  const uint32_t h = pack_bf16(0.5f * v0, 0.5f * v1);
+// SiLU of a bf16 pair given h = v / 2: h (1 + tanh(h)) with the hardware
+// tanh (the hidden activations are bf16 operands of the second MLP product;
+// W1 and b1 are staged halved, which is exact).
+__device__ __forceinline__ uint32_t silu_half_bf16x2(float h0, float h1) {
+  const uint32_t h = pack_bf16(h0, h1);
   uint32_t t, y;
   asm("tanh.approx.bf16x2 %0, %1;" : "=r"(t) : "r"(h));
   asm("fma.rn.bf16x2 %0, %1, %2, %1;" : "=r"(y) : "r"(h), "r"(t));
   return y;
 }
 constexpr uint32_t kOnesBf16x2 = 0x3F803F80u;  // (1.0, 1.0)
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // 16 TMEM lanes x 64 fp32 columns in the mma.sync accumulator layout:
 // c[n] = (lane g, column 8 n + 2 t, +1), (lane g + 8, same columns).
@@ -177,7 +184,7 @@ __device__ __forceinline__ void layer_norm(const float (&x)[8][4], const float* 
   q0 += __shfl_xor_sync(0xffffffffu, q0, 2);
   q1 += __shfl_xor_sync(0xffffffffu, q1, 1);
   q1 += __shfl_xor_sync(0xffffffffu, q1, 2);
-  const float r0 = 1.0f / sqrtf(q0 * (1.0f / 64.0f) + 1e-5f), r1 = 1.0f / sqrtf(q1 * (1.0f / 64.0f) + 1e-5f);
+  const float r0 = rsqrtf(q0 * (1.0f / 64.0f) + 1e-5f), r1 = rsqrtf(q1 * (1.0f / 64.0f) + 1e-5f);
 #pragma unroll
   for (int n = 0; n < 8; ++n) {
     const int c = 8 * n + 2 * t;
@@ -202,16 +209,17 @@ __device__ __forceinline__ void tile_barrier(int tile) {
   asm volatile("bar.sync %0, 256;" ::"r"(tile + 5) : "memory");
 }
 
-// fp32 [rows, kdim] row-major -> bf16 K-major swizzled tile (64-wide atom
-// columns rows * 128 bytes apart).
-__device__ void stage_weights(uint32_t dst, const float* __restrict__ w, int rows, int kdim, int tid) {
+// fp32 [rows, kdim] row-major, times `scale` (a power of two) -> bf16
+// K-major swizzled tile (64-wide atom columns rows * 128 bytes apart).
+__device__ void stage_weights(uint32_t dst, const float* __restrict__ w, int rows, int kdim, int tid,
+                              float scale = 1.f) {
   const int cpr = kdim >> 3;
   for (int i = tid; i < rows * cpr; i += kThreads) {
     const int n = i / cpr, j = i - n * cpr;
     const float* s = w + (size_t)n * kdim + 8 * j;
     uint32_t p[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) p[k] = pack_bf16(__ldg(s + 2 * k), __ldg(s + 2 * k + 1));
+    for (int k = 0; k < 4; ++k) p[k] = pack_bf16(scale * __ldg(s + 2 * k), scale * __ldg(s + 2 * k + 1));
     asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(dst + (uint32_t)(j >> 3) * (uint32_t)(rows * 128) +
                                                                  sw(n, j & 7)),
                  "r"(p[0]), "r"(p[1]), "r"(p[2]), "r"(p[3])
@@ -248,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 *mn_b = mn_w + 64, *w1 = mn_b + 64, *b1 = w1 + 128 * 64, *w2 = b1 + 128, *b2 = w2 + 64 * 128;
     const uint32_t wb = sb + (uint32_t)b * kWBlock;
     stage_weights(wb + kOffWqkv, qkv, 192, 64, tid);
-    stage_weights(wb + kOffW1, w1, 128, 64, tid);
+    stage_weights(wb + kOffW1, w1, 128, 64, tid, 0.5f);  // SiLU takes v / 2
     stage_weights(wb + kOffW2, w2, 64, 128, tid);
     stage_weights(wb + kOffWo, ao, 64, 64, tid);
     float* P = sPar + b * kParBlock;
@@ -259,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       P[192 + i] = mn_b[i];
       P[384 + i] = b2[i];
     }
-    for (int i = tid; i < 128; i += kThreads) P[256 + i] = b1[i];
+    for (int i = tid; i < 128; i += kThreads) P[256 + i] = 0.5f * b1[i];
   }
   for (int i = tid; i < 128; i += kThreads) sPar[kParFinal + i] = params[2 * IMBA_BOARD_BLOCK_FLOATS + i];
   if (tid == 0) {
@@ -418,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma16816(oh[1], pa[kc], b[2], b[3]);
           mma16816(oh[2], pa[kc], kOnesBf16x2, kOnesBf16x2);
         }
-        const float i0 = __frcp_rn(oh[2][0]), i1 = __frcp_rn(oh[2][2]);
+        const float i0 = rcp_approx(oh[2][0]), i1 = rcp_approx(oh[2][2]);
         // The head's output (16 x 16) as one A k-chunk, through its slice of
         // the output projection into the residual.
         uint32_t oa[4];
@@ -449,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k = 0; k < 4; ++k) tc::umma_f16(tmem_tile, dT + 2 * k, dW + 2 * k, idN128, k);
       });
-      {  // hidden = SiLU(. + b1) -> tile (two 64-wide atom columns)
+      {  // hidden = SiLU(v), v / 2 = . + b1 / 2 (halved W1, b1) -> tile (two 64-wide atom columns)
         const float* b1 = P + 256;
 #pragma unroll 1
         for (int half = 0; half < 2; ++half) {
@@ -460,10 +468,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 4; ++j) {
             const float2 c0 = *reinterpret_cast<const float2*>(b1 + 64 * half + 16 * j + 2 * t);
             const float2 c1 = *reinterpret_cast<const float2*>(b1 + 64 * half + 16 * j + 8 + 2 * t);
-            a[j][0] = silu_bf16x2(acc[2 * j][0] + c0.x, acc[2 * j][1] + c0.y);
-            a[j][1] = silu_bf16x2(acc[2 * j][2] + c0.x, acc[2 * j][3] + c0.y);
-            a[j][2] = silu_bf16x2(acc[2 * j + 1][0] + c1.x, acc[2 * j + 1][1] + c1.y);
-            a[j][3] = silu_bf16x2(acc[2 * j + 1][2] + c1.x, acc[2 * j + 1][3] + c1.y);
+            a[j][0] = silu_half_bf16x2(acc[2 * j][0] + c0.x, acc[2 * j][1] + c0.y);
+            a[j][1] = silu_half_bf16x2(acc[2 * j][2] + c0.x, acc[2 * j][3] + c0.y);
+            a[j][2] = silu_half_bf16x2(acc[2 * j + 1][0] + c1.x, acc[2 * j + 1][1] + c1.y);
+            a[j][3] = silu_half_bf16x2(acc[2 * j + 1][2] + c1.x, acc[2 * j + 1][3] + c1.y);
           }
           store_tile(tb + 16384u * half, a, r0, lane);
         }
