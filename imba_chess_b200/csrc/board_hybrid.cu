@@ -139,6 +139,22 @@ __device__ __forceinline__ void tmem_ld_frag(uint32_t taddr, float (&c)[8][4]) {
   }
 }
 
+// 16 TMEM lanes x 16 fp32 columns, times `scale`, as one bf16 A fragment
+// (k-chunk) of the mma.sync layout.
+__device__ __forceinline__ void tmem_ld_afrag16(uint32_t taddr, float scale, uint32_t (&a)[4]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+  a[0] = pack_bf16(scale * __uint_as_float(r[0]), scale * __uint_as_float(r[1]));
+  a[1] = pack_bf16(scale * __uint_as_float(r[2]), scale * __uint_as_float(r[3]));
+  a[2] = pack_bf16(scale * __uint_as_float(r[4]), scale * __uint_as_float(r[5]));
+  a[3] = pack_bf16(scale * __uint_as_float(r[6]), scale * __uint_as_float(r[7]));
+}
+
 // Accumulator tiles (8 n-tiles = 64 columns) -> bf16 A fragments (4 k-chunks).
 __device__ __forceinline__ void to_afrag(const float (&c)[8][4], uint32_t (&a)[4][4]) {
 #pragma unroll
@@ -358,12 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k = 0; k < 4; ++k) tc::umma_f16(tmem_tile, dT + 2 * k, dW + 2 * k, idN192, k);
       });
-      uint32_t qa[4][4];
-      {
-        // K and V rows of the board -> shared memory; Q, pre-scaled by
-        // log2(e) / sqrt(16) so that the scores come out in the log2 domain,
-        // -> A fragments.
-        constexpr float kQScale = 0.25f * 1.4426950408889634f;
+      {  // K and V rows of the board -> shared memory
         float acc[8][4];
         uint32_t a[4][4];
         tmem_ld_frag(tl + 64, acc);
@@ -372,20 +383,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_frag(tl + 128, acc);
         to_afrag(acc, a);
         store_tile(vb, a, sq0, lane);
-        tmem_ld_frag(tl, acc);
-#pragma unroll
-        for (int n = 0; n < 8; ++n) {
-          acc[n][0] *= kQScale;
-          acc[n][1] *= kQScale;
-          acc[n][2] *= kQScale;
-          acc[n][3] *= kQScale;
-        }
-        to_afrag(acc, qa);
       }
       board_barrier(bslot);  // the board's K / V are complete
       const int rr = lane & 7, m = lane >> 3;
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
+        // The head's Q columns stay in TMEM until the MLP product: read as
+        // the A fragment, pre-scaled by log2(e) / sqrt(16) so that the scores
+        // come out in the log2 domain.
+        uint32_t qh[4];
+        tmem_ld_afrag16(tl + 16 * h, 0.25f * 1.4426950408889634f, qh);
         float s[8][4];
         zero(s);
 #pragma unroll
@@ -393,8 +400,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t b[4];
           // keys 8 nt .. (and +8), dims 16 h .. 16 h + 15
           ldsm_x4(b, kb + sw(8 * nt + rr + 8 * (m >> 1), 2 * h + (m & 1)));
-          mma16816(s[nt], qa[h], b[0], b[1]);
-          mma16816(s[nt + 1], qa[h], b[2], b[3]);
+          mma16816(s[nt], qh, b[0], b[1]);
+          mma16816(s[nt + 1], qh, b[2], b[3]);
         }
         float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
