@@ -48,7 +48,7 @@ constexpr uint32_t kOffWo = 57344;      //   [64 x 64] output projection (mma.sy
 constexpr uint32_t kOffTile = 2 * kWBlock;  // 32 KB per tile: LN output [128 x 64] at +0, or
 constexpr uint32_t kTileBytes = 32768;      // K / V of board b at +16 KB b, +8 KB, or hidden [128 x 128]
 constexpr uint32_t kOffPar = kOffTile + 2 * kTileBytes;
-constexpr int kParBlock = 448;  // ln1 w, b | ln2 w, b | b1 (128) | b2 (64)
+constexpr int kParBlock = 448;  // ln1 w, b | (unused 128) | b1' (128, folded and halved) | b2 (64)
 constexpr int kParFinal = 2 * kParBlock;
 constexpr uint32_t kOffPool = kOffPar + (2 * kParBlock + 128) * 4;  // [4 boards][4 warps][64] floats
 constexpr uint32_t kOffBar = kOffPool + 4 * 4 * 64 * 4;             // one mbarrier per tile
@@ -211,6 +211,42 @@ __device__ __forceinline__ void layer_norm(const float (&x)[8][4], const float* 
   }
 }
 
+// LayerNorm without the affine part, (x - mean) / std: used where the
+// affine weights are folded into what follows (the MLP's first product, the
+// pooled mean).
+__device__ __forceinline__ void layer_norm_plain(const float (&x)[8][4], float (&y)[8][4]) {
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int n = 0; n < 8; ++n) {
+    s0 += x[n][0] + x[n][1];
+    s1 += x[n][2] + x[n][3];
+  }
+  s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+  s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+  s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+  s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+  const float mu0 = s0 * (1.0f / 64.0f), mu1 = s1 * (1.0f / 64.0f);
+  float q0 = 0.f, q1 = 0.f;
+#pragma unroll
+  for (int n = 0; n < 8; ++n) {
+    q0 += (x[n][0] - mu0) * (x[n][0] - mu0) + (x[n][1] - mu0) * (x[n][1] - mu0);
+    q1 += (x[n][2] - mu1) * (x[n][2] - mu1) + (x[n][3] - mu1) * (x[n][3] - mu1);
+  }
+  q0 += __shfl_xor_sync(0xffffffffu, q0, 1);
+  q0 += __shfl_xor_sync(0xffffffffu, q0, 2);
+  q1 += __shfl_xor_sync(0xffffffffu, q1, 1);
+  q1 += __shfl_xor_sync(0xffffffffu, q1, 2);
+  const float r0 = rsqrtf(q0 * (1.0f / 64.0f) + 1e-5f), r1 = rsqrtf(q1 * (1.0f / 64.0f) + 1e-5f);
+  const float z0 = -mu0 * r0, z1 = -mu1 * r1;
+#pragma unroll
+  for (int n = 0; n < 8; ++n) {
+    y[n][0] = fmaf(x[n][0], r0, z0);
+    y[n][1] = fmaf(x[n][1], r0, z0);
+    y[n][2] = fmaf(x[n][2], r1, z1);
+    y[n][3] = fmaf(x[n][3], r1, z1);
+  }
+}
+
 __device__ __forceinline__ void zero(float (&c)[8][4]) {
 #pragma unroll
   for (int n = 0; n < 8; ++n) c[n][0] = c[n][1] = c[n][2] = c[n][3] = 0.f;
@@ -225,17 +261,21 @@ __device__ __forceinline__ void tile_barrier(int tile) {
   asm volatile("bar.sync %0, 256;" ::"r"(tile + 5) : "memory");
 }
 
-// fp32 [rows, kdim] row-major, times `scale` (a power of two) -> bf16
-// K-major swizzled tile (64-wide atom columns rows * 128 bytes apart).
+// fp32 [rows, kdim] row-major, times `scale` and (when given) the per-input
+// factors colw[k] -> bf16 K-major swizzled tile (64-wide atom columns
+// rows * 128 bytes apart).
 __device__ void stage_weights(uint32_t dst, const float* __restrict__ w, int rows, int kdim, int tid,
-                              float scale = 1.f) {
+                              float scale = 1.f, const float* __restrict__ colw = nullptr) {
   const int cpr = kdim >> 3;
   for (int i = tid; i < rows * cpr; i += kThreads) {
     const int n = i / cpr, j = i - n * cpr;
     const float* s = w + (size_t)n * kdim + 8 * j;
+    float f[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) f[k] = scale * __ldg(s + k) * (colw ? __ldg(colw + 8 * j + k) : 1.f);
     uint32_t p[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) p[k] = pack_bf16(scale * __ldg(s + 2 * k), scale * __ldg(s + 2 * k + 1));
+    for (int k = 0; k < 4; ++k) p[k] = pack_bf16(f[2 * k], f[2 * k + 1]);
     asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(dst + (uint32_t)(j >> 3) * (uint32_t)(rows * 128) +
                                                                  sw(n, j & 7)),
                  "r"(p[0]), "r"(p[1]), "r"(p[2]), "r"(p[3])
@@ -272,18 +312,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 *mn_b = mn_w + 64, *w1 = mn_b + 64, *b1 = w1 + 128 * 64, *w2 = b1 + 128, *b2 = w2 + 64 * 128;
     const uint32_t wb = sb + (uint32_t)b * kWBlock;
     stage_weights(wb + kOffWqkv, qkv, 192, 64, tid);
-    stage_weights(wb + kOffW1, w1, 128, 64, tid, 0.5f);  // SiLU takes v / 2
+    // The MLP LayerNorm's affine part folds into the first product:
+    // W1 diag(w) and b1 + W1 b, both halved (the SiLU takes v / 2).
+    stage_weights(wb + kOffW1, w1, 128, 64, tid, 0.5f, mn_w);
     stage_weights(wb + kOffW2, w2, 64, 128, tid);
     stage_weights(wb + kOffWo, ao, 64, 64, tid);
     float* P = sPar + b * kParBlock;
     for (int i = tid; i < 64; i += kThreads) {
       P[i] = an_w[i];
       P[64 + i] = an_b[i];
-      P[128 + i] = mn_w[i];
-      P[192 + i] = mn_b[i];
       P[384 + i] = b2[i];
     }
-    for (int i = tid; i < 128; i += kThreads) P[256 + i] = 0.5f * b1[i];
+    for (int i = tid; i < 128; i += kThreads) {
+      float acc = b1[i];
+      for (int k = 0; k < 64; ++k) acc = fmaf(w1[(size_t)i * 64 + k], mn_b[k], acc);
+      P[256 + i] = 0.5f * acc;
+    }
   }
   for (int i = tid; i < 128; i += kThreads) sPar[kParFinal + i] = params[2 * IMBA_BOARD_BLOCK_FLOATS + i];
   if (tid == 0) {
@@ -332,14 +376,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint64_t dT = tc::smem_desc_k128(sm + kOffTile + tile * kTileBytes);
 
   const int iters = (rows + 3) >> 2;
+  const int s0 = sq0 + g, s1 = sq0 + g + 8;  // this lane's squares
+  // Piece ids are loaded one iteration ahead (two registers), so that only
+  // the embedding gather waits on memory at the start of an iteration.
+  int pn0 = 0, pn1 = 0;
+  if (4 * (int)blockIdx.x + bslot < rows) {
+    pn0 = piece_ids[(size_t)(4 * blockIdx.x + bslot) * 64 + s0];
+    pn1 = piece_ids[(size_t)(4 * blockIdx.x + bslot) * 64 + s1];
+  }
   for (int it = blockIdx.x; it < iters; it += gridDim.x) {
     const int r = 4 * it + bslot;
     const bool live = r < rows;
+    int p0 = pn0, p1 = pn1;
+    if (r + 4 * (int)gridDim.x < rows) {
+      pn0 = piece_ids[(size_t)(r + 4 * gridDim.x) * 64 + s0];
+      pn1 = piece_ids[(size_t)(r + 4 * gridDim.x) * 64 + s1];
+    }
     // ---- gather the joint (piece, square) embeddings ----
     float x[8][4];
     {
-      const int s0 = sq0 + g, s1 = sq0 + g + 8;
-      int p0 = live ? piece_ids[(size_t)r * 64 + s0] : 0, p1 = live ? piece_ids[(size_t)r * 64 + s1] : 0;
       if (p0 > 12 || p1 > 12) {
         report(status, IMBA_ERR_RANGE);
         p0 = p0 > 12 ? 0 : p0;
@@ -455,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       {
         float y[8][4];
         uint32_t a[4][4];
-        layer_norm(x, P + 128, P + 192, t, y);
+        layer_norm_plain(x, y);
         to_afrag(y, a);
         store_tile(tb, a, r0, lane);
       }
@@ -507,8 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- final LayerNorm and mean over the 64 squares ----
     {
       float y[8][4];
-      const float* fin = sPar + kParFinal;
-      layer_norm(x, fin, fin + 64, t, y);
+      layer_norm_plain(x, y);  // the affine part applies to the mean
       float cs[8][2];
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
@@ -534,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* src = sPool + (size_t)bslot * 4 * 64;
       for (int c = lane; c < 64; c += 32) {
         const float s = src[c] + src[64 + c] + src[128 + c] + src[192 + c];
-        const float v = s * (1.0f / 64.0f);
+        const float v = fmaf(s * (1.0f / 64.0f), sPar[kParFinal + c], sPar[kParFinal + 64 + c]);
         const bf16 hi = __float2bfloat16_rn(v), lo = __float2bfloat16_rn(v - __bfloat162float(hi));
         bf16* o = pooled_out + (size_t)r * 3 * 64;
         o[c] = hi;
