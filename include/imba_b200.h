@@ -191,8 +191,9 @@ IMBA_API int32_t imba_device_arch(void);
  * copy of the board projection split into bf16 hi / lo parts ([d, 192]
  * bf16, freed by imba_model_destroy).  Environment, read here: IMBA_SIMT
  * naming components (gemm, attn, board) selects their SIMT kernels (for
- * cross-checks); IMBA_BOARD=tc selects the tcgen05 board encoder instead of
- * the mma.sync one. */
+ * cross-checks); IMBA_BOARD=mma or IMBA_BOARD=tc selects the mma.sync-only
+ * or tcgen05-only board encoder instead of the default one (tcgen05
+ * projections, mma.sync attention). */
 IMBA_API imba_status_t imba_model_create(const imba_model_desc* desc, imba_model** out);
 IMBA_API void imba_model_destroy(imba_model* model);
 
