@@ -64,6 +64,14 @@ struct Ref {
 };
 
 bool as_long(PyObject* o, long long* out) {
+#if PY_VERSION_HEX >= 0x030C0000
+  // Exact ints that fit one digit (every id and piece code on the wire) are
+  // read inline, without the general conversion.
+  if (PyLong_CheckExact(o) && PyUnstable_Long_IsCompact(reinterpret_cast<PyLongObject*>(o))) {
+    *out = (long long)PyUnstable_Long_CompactValue(reinterpret_cast<PyLongObject*>(o));
+    return true;
+  }
+#endif
   if (!PyLong_Check(o)) {
     // numpy integers and other __index__ types
     Ref i(PyNumber_Index(o));
