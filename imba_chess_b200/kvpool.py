@@ -24,6 +24,8 @@ holder releases them.
 
 from __future__ import annotations
 
+from itertools import chain
+
 import numpy as np
 import torch
 
@@ -107,6 +109,33 @@ class KVSequence:
             self.pages.extend(self.pool.alloc(need_pages))
         self.length = start + n
         return self.slots(start, start + n)
+
+    @staticmethod
+    def reserve_many(seqs: "list[KVSequence]", counts) -> np.ndarray:
+        """``seqs[i].reserve(counts[i])`` for every i, in order; returns all
+        the new slots concatenated (int64), computed in one pass over the
+        sequences' page lists instead of one small array per sequence."""
+        n = len(seqs)
+        starts = np.empty(n, dtype=np.int64)
+        for i, (s, c) in enumerate(zip(seqs, counts)):
+            start = s.length
+            need = -(-(start + int(c)) // PAGE) - len(s.pages)
+            if need > 0:
+                s.pages.extend(s.pool.alloc(need))
+            s.length = start + int(c)
+            starts[i] = start
+        cnt = np.asarray(counts, dtype=np.int64).reshape(n)
+        total = int(cnt.sum())
+        if total == 0:
+            return np.zeros(0, dtype=np.int64)
+        npg = np.fromiter((len(s.pages) for s in seqs), dtype=np.int64, count=n)
+        pbase = np.zeros(n, dtype=np.int64)
+        np.cumsum(npg[:-1], out=pbase[1:])
+        cat = np.fromiter(chain.from_iterable(s.pages for s in seqs), dtype=np.int64, count=int(npg.sum()))
+        rbase = np.zeros(n, dtype=np.int64)
+        np.cumsum(cnt[:-1], out=rbase[1:])
+        t = np.repeat(starts, cnt) + np.arange(total, dtype=np.int64) - np.repeat(rbase, cnt)
+        return cat[np.repeat(pbase, cnt) + t // PAGE] * PAGE + t % PAGE
 
     def slots(self, start: int, stop: int) -> np.ndarray:
         t = np.arange(start, stop, dtype=np.int64)

@@ -21,7 +21,7 @@ from itertools import chain
 
 import numpy as np
 
-from .kvpool import KVSequence
+from .kvpool import PAGE, KVSequence
 from .plan import StepPlan
 from .synth import TOKEN_FIELDS
 
@@ -107,14 +107,19 @@ def wave_plan(groups: list[WaveGroup], piece: np.ndarray, side: np.ndarray, lega
     G = len(groups)
     counts = np.fromiter((len(g.chains) for g in groups), dtype=np.int64, count=G)
     R = int(counts.sum())
+    starts = [g.arena.length for g in groups]
+    dst = KVSequence.reserve_many([g.arena for g in groups], counts)
+    # A group's own rows: the arena rows just reserved (an arena listed twice
+    # continues where its previous group stopped).
     own_rows: list[list[int]] = []
-    dst_parts, pages = [], []
-    for g in groups:
-        start = g.arena.length
-        dst_parts.append(g.arena.reserve(len(g.chains)))
-        own_rows.append(list(range(start, start + len(g.chains))))
-        pages.append(g.prefix.page_array(g.prefix_len))
-    dst = np.concatenate(dst_parts) if dst_parts else np.zeros(0, np.int64)
+    seen: dict[int, int] = {}
+    for g, start, n in zip(groups, starts, counts.tolist()):
+        start = seen.get(id(g.arena), start)
+        own_rows.append(list(range(start, start + n)))
+        seen[id(g.arena)] = start + n
+    npre = [min(-(-g.prefix_len // PAGE), len(g.prefix.pages)) for g in groups]  # as page_array slices
+    pages_cat = np.fromiter(chain.from_iterable(g.prefix.pages[:k] for g, k in zip(groups, npre)), dtype=np.int64,
+                            count=sum(npre))
     row_group = np.repeat(np.arange(G), counts)
     plen = np.fromiter((g.prefix_len for g in groups), dtype=np.int64, count=G)
     all_chains = [c for g in groups for c in g.chains]
@@ -142,7 +147,7 @@ def wave_plan(groups: list[WaveGroup], piece: np.ndarray, side: np.ndarray, lega
         j = np.arange(E) - np.repeat(eoff[:-1], per_row)  # index within the row's extras
         extra_pos[is_chain] = (np.repeat(prow, per_row) + j)[is_chain]
     gpo = np.zeros(G + 1, dtype=np.int64)
-    np.cumsum([len(p) for p in pages], out=gpo[1:])
+    np.cumsum(npre, out=gpo[1:])
     loff, lids = legal_csr if legal_csr is not None else ids_csr(legal_ids)
     plan = StepPlan(
         piece_ids=piece,
@@ -155,7 +160,7 @@ def wave_plan(groups: list[WaveGroup], piece: np.ndarray, side: np.ndarray, lega
         extra_pos=extra_pos.astype(np.int32),
         row_dst_slot=dst.astype(np.int32),
         group_page_off=gpo.astype(np.int32),
-        group_pages=np.concatenate(pages).astype(np.int32) if pages else np.zeros(0, np.int32),
+        group_pages=pages_cat.astype(np.int32),
         legal_off=loff,
         legal_ids=lids,
     )
