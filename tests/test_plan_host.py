@@ -103,3 +103,32 @@ def test_kv_sequence_slots_and_refcounts():
     c = KVSequence(pool)
     with pytest.raises(KVPoolExhausted):
         c.reserve(16 * 7)
+
+
+def test_reserve_many_matches_sequential_reserves():
+    """KVSequence.reserve_many (one vectorised pass, used by the wave planner)
+    gives the same slots, page lists and lengths as calling reserve() on each
+    sequence in turn, including a sequence listed more than once."""
+    torch = pytest.importorskip("torch")
+    from imba_chess_b200.kvpool import KVPool, KVSequence
+
+    rng = np.random.default_rng(3)
+    for _ in range(20):
+        pools = [KVPool(num_layers=1, num_heads=1, attention_dim=8, linear_dim=8, num_pages=400,
+                        dtype=torch.float32, device=torch.device("cpu")) for _ in range(2)]
+        pre = [int(x) for x in rng.integers(0, 40, 4)]
+        order = [int(x) for x in rng.integers(0, 4, 7)]
+        counts = [int(x) for x in rng.integers(0, 35, 7)]
+        out = []
+        for k, pool in enumerate(pools):
+            seqs = [KVSequence(pool) for _ in range(4)]
+            for s, n in zip(seqs, pre):
+                s.reserve(n)
+            listed = [seqs[i] for i in order]
+            if k == 0:
+                slots = np.concatenate([s.reserve(c) for s, c in zip(listed, counts)])
+            else:
+                slots = KVSequence.reserve_many(listed, counts)
+            out.append((slots, [s.pages for s in seqs], [s.length for s in seqs]))
+        assert np.array_equal(out[0][0], out[1][0])
+        assert out[0][1] == out[1][1] and out[0][2] == out[1][2]
