@@ -30,6 +30,8 @@ INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libimba_b200.so")
 HOST_SRC = os.path.join(PKG, "host", "hostpath.cpp")
 HOST_EXT = os.path.join(PKG, "_hostpath" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
+CHESS_SRC = os.path.join(PKG, "host", "chess.cpp")
+CHESS_EXT = os.path.join(PKG, "_chess" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
@@ -92,19 +94,25 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIB
 
 
-def build_host(force: bool = False) -> str:
-    """Compile the CPython host-path extension (g++, -O2)."""
-    if not force and os.path.exists(HOST_EXT) and os.path.getmtime(HOST_EXT) >= os.path.getmtime(HOST_SRC):
-        return HOST_EXT
+def _build_ext(src: str, ext: str, force: bool) -> str:
+    if not force and os.path.exists(ext) and os.path.getmtime(ext) >= os.path.getmtime(src):
+        return ext
     cxx = os.environ.get("CXX") or shutil.which("g++") or "g++"
     inc = sysconfig.get_paths()["include"]
-    tmp = HOST_EXT + ".tmp"
-    cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden", "-I", inc, HOST_SRC, "-o", tmp]
+    tmp = ext + ".tmp"
+    cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden", "-I", inc, src, "-o", tmp]
     proc = subprocess.run(cmd, capture_output=True, text=True)
     if proc.returncode != 0:
-        raise RuntimeError(f"host extension build failed:\n{proc.stdout}\n{proc.stderr}")
-    os.replace(tmp, HOST_EXT)
-    return HOST_EXT
+        raise RuntimeError(f"host extension build failed ({src}):\n{proc.stdout}\n{proc.stderr}")
+    os.replace(tmp, ext)
+    return ext
+
+
+def build_host(force: bool = False) -> str:
+    """Compile the CPython host extensions (g++, -O2): the wave service's
+    host path (``_hostpath``) and worker-side chess (``_chess``)."""
+    _build_ext(CHESS_SRC, CHESS_EXT, force)
+    return _build_ext(HOST_SRC, HOST_EXT, force)
 
 
 def main() -> None:
