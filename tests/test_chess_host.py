@@ -130,3 +130,24 @@ def test_bad_input_raises():
         wc.perft("not a fen", 1)
     with pytest.raises(ValueError):
         wc.BoardStateEncoder(wc.BoardTokenConfig(en_passant="bogus"))
+
+
+def test_random_games_self_consistent():
+    """Random playouts: at every position the two-ply leaf count computed
+    inside the generator equals the sum of one-ply counts of the children
+    reached through FEN text (push_uci writes the FEN, the child is parsed
+    back), so FEN writing and parsing keep castling rights, en passant,
+    counters and side to move; every legal move is in the vocabulary; each
+    side keeps one king."""
+    rng = np.random.default_rng(11)
+    for _ in range(8):
+        fen = START
+        for _ in range(int(rng.integers(20, 100))):
+            _, ucis = wc.legal_vocab_projection(fen)
+            assert len(ucis) == wc.perft(fen, 1)
+            if not ucis:
+                break
+            assert wc.perft(fen, 2) == sum(wc.perft(wc.push_uci(fen, u), 1) for u in ucis)
+            s = wc.BoardStateEncoder().encode_fen(fen)
+            assert s.piece_ids.count(6) == 1 and s.piece_ids.count(12) == 1
+            fen = wc.push_uci(fen, ucis[int(rng.integers(0, len(ucis)))])
