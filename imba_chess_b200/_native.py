@@ -34,6 +34,11 @@ STATUS_NAMES = {
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
+# imba_model_desc.flags: SIMT test hooks of a bf16 handle (cross-checks only)
+FLAG_SIMT_GEMM = 1
+FLAG_SIMT_ATTN = 2
+FLAG_SIMT_BOARD = 4
+SIMT_FLAGS = {"gemm": FLAG_SIMT_GEMM, "attn": FLAG_SIMT_ATTN, "board": FLAG_SIMT_BOARD}
 MAX_LAYERS = 32
 PAGE_TOKENS = 16
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -54,6 +59,7 @@ EXPORTED_SYMBOLS = (
     "imba_step_profiled",
     "imba_kv_scatter",
     "imba_kv_gather",
+    "imba_selftest_wait_timeout",
 )
 
 _P = ctypes.c_void_p
@@ -83,7 +89,7 @@ class ModelDesc(ctypes.Structure):
         ("fullmove_vocab", _I32),
         ("has_value_head", _I32),
         ("dtype", _I32),
-        ("reserved", _I32),
+        ("flags", _I32),
         ("piece_square", _P),
         ("board_params", _P),
         ("board_out_w", _P),
@@ -195,6 +201,8 @@ def load() -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = [_P, ctypes.POINTER(PoolDesc), _I32, _I32, _P, _P, _P, _P, _P]
             fn.restype = _I32
+        lib.imba_selftest_wait_timeout.argtypes = [ctypes.c_int64, _P, _P]
+        lib.imba_selftest_wait_timeout.restype = _I32
         _lib = lib
         return lib
 

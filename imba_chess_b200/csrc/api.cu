@@ -61,6 +61,7 @@ imba_status_t validate_desc(const imba_model_desc* d) {
   if ((int64_t)d->num_heads * d->linear_dim > 1024) return IMBA_ERR_UNSUPPORTED;
   if (d->vocab <= 0 || d->max_pos <= 0 || d->halfmove_vocab <= 0 || d->fullmove_vocab <= 0) return IMBA_ERR_ARG;
   if (d->dtype != IMBA_DTYPE_F32 && d->dtype != IMBA_DTYPE_BF16) return IMBA_ERR_ARG;
+  if (d->flags & ~(IMBA_FLAG_SIMT_GEMM | IMBA_FLAG_SIMT_ATTN | IMBA_FLAG_SIMT_BOARD)) return IMBA_ERR_ARG;
   const void* req[] = {d->piece_square, d->board_params, d->board_out_w, d->board_out_b, d->emb_seq,
                        d->emb_turn,     d->emb_castle,   d->emb_ep,      d->emb_halfmove, d->emb_fullmove,
                        d->emb_prev_move, d->emb_pos,     d->final_norm_w, d->final_norm_b, d->policy_w,
@@ -73,6 +74,18 @@ imba_status_t validate_desc(const imba_model_desc* d) {
   return IMBA_OK;
 }
 
+// Shapes the bf16 tensor-core kernels cover: the GEMM tiles (d and H dv
+// multiples of 128, the uvqk width a multiple of 256) and the paged
+// attention (head dims 64 / 64, at most 16 head groups of 8).
+bool bf16_shape_supported(const imba_model_desc& d, bool simt_gemm, bool simt_attn) {
+  const int hdv = d.num_heads * d.linear_dim;
+  const int uvqk_n = 2 * d.num_heads * (d.linear_dim + d.attention_dim);
+  const bool gemm_ok = d.model_dim % 128 == 0 && hdv % 128 == 0 && uvqk_n % 256 == 0 && d.attention_dim % 32 == 0 &&
+                       d.linear_dim % 32 == 0;
+  const bool attn_ok = d.attention_dim == 64 && d.linear_dim == 64 && d.num_heads <= 128;
+  return (simt_gemm || gemm_ok) && (simt_attn || attn_ok);
+}
+
 imba_status_t validate_step(const imba_model* m, const imba_step_desc* st, const imba_pool_desc* pool) {
   if (!st || !pool) return IMBA_ERR_ARG;
   if (st->num_rows < 0 || st->num_groups < 0 || st->num_chunks < 0 || st->num_legal < 0 || st->num_extra < 0 ||
@@ -80,6 +93,7 @@ imba_status_t validate_step(const imba_model* m, const imba_step_desc* st, const
     return IMBA_ERR_ARG;
   if (st->num_rows == 0) return IMBA_OK;
   if (!pool->base || pool->num_pages <= 0) return IMBA_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(pool->base) & 255) return IMBA_ERR_ARG;  // TMA views need aligned bases
   if (pool->num_pages > (int64_t)INT32_MAX / IMBA_PAGE_TOKENS) return IMBA_ERR_RANGE;
   const void* req[] = {st->piece_ids, st->side_ids, st->positions, st->row_vis, st->row_extra_off,
                        st->row_dst_slot, st->row_perm};
@@ -124,19 +138,19 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
 
   IMBA_CK(pm.mark(s));
   IMBA_CK(cudaMemsetAsync(w.counters, 0, kNumCounters * sizeof(int), s));
+  // bf16 handles run the tensor-core kernels; a launcher that declines
+  // (returns false) is an error unless a SIMT test hook selected the SIMT
+  // kernel of that component (imba_model_desc.flags).
+  const bool tc_gemm = md.dtype == IMBA_DTYPE_BF16 && !m->simt_gemm;
   if (md.dtype == IMBA_DTYPE_BF16 && !m->simt_board) {
     // tensor-core board encoder -> pooled [R, 192] split bf16; projection + embeddings in the GEMM epilogue
-    if (m->board_kind == 2 && board_tc_applies(md))
-      IMBA_CK(launch_board_tc(md, st, static_cast<bf16*>(w.pooled), s));
-    else if (m->board_kind == 1)
-      IMBA_CK(launch_board_mma(md, st, static_cast<bf16*>(w.pooled), s));
-    else
-      IMBA_CK(launch_board_hybrid(md, st, static_cast<bf16*>(w.pooled), s));
+    IMBA_CK(launch_board_hybrid(md, st, static_cast<bf16*>(w.pooled), s));
     EpiContent ec{w.x, nullptr, md.board_out_b, md.emb_seq, md.emb_turn, md.emb_castle, md.emb_ep, md.emb_halfmove,
                   md.emb_fullmove, md.emb_prev_move, md.emb_pos, st.side_ids, st.positions, d, md.halfmove_vocab,
                   md.fullmove_vocab, md.vocab, md.max_pos, sqrtf((float)d), st.status};
     const bf16* p3 = static_cast<const bf16*>(w.pooled);
     if (!gemm_tc_launch_content(m, R, p3, ec, st.status, s, &e)) {
+      if (tc_gemm) return IMBA_ERR_UNSUPPORTED;
       IMBA_CK(launch_gemm_simt<bf16, bf16, EpiContent>(p3, 3 * IMBA_BOARD_DIM, static_cast<const bf16*>(m->board_proj3),
                                                        3 * IMBA_BOARD_DIM, R, d, 3 * IMBA_BOARD_DIM, ec, s));
     } else if (e != cudaSuccess) {
@@ -151,6 +165,7 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
     IMBA_CK(pm.mark(s));
     EpiUVQK<T> epi{static_cast<T*>(w.u), static_cast<T*>(w.q), poolp, st.row_dst_slot, g, l, st.status};
     if (!gemm_tc_launch_uvqk(m, l, R, static_cast<const T*>(w.xn), epi, s, &e)) {
+      if (tc_gemm) return IMBA_ERR_UNSUPPORTED;
       IMBA_CK(launch_gemm_simt<T, T, EpiUVQK<T>>(static_cast<const T*>(w.xn), d,
                                                 static_cast<const T*>(md.uvqk_w[l]), d, R, m->uvqk_n, d, epi, s));
     } else if (e != cudaSuccess) {
@@ -163,6 +178,7 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
     bf16* gated_bf = std::is_same<T, bf16>::value ? reinterpret_cast<bf16*>(w.gated) : nullptr;
     if (m->simt_attn || !launch_attn_page(aa, md.num_layers, md, pool.num_pages, static_cast<const bf16*>(w.u),
                                           gated_bf, s, &e, &fused)) {
+      if (md.dtype == IMBA_DTYPE_BF16 && !m->simt_attn) return IMBA_ERR_UNSUPPORTED;
       IMBA_CK(launch_attn_simt<T>(aa, s));
     } else if (e != cudaSuccess) {
       return IMBA_ERR_CUDA;
@@ -172,6 +188,7 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
     IMBA_CK(pm.mark(s));
     EpiResidual er{w.x, md.o_b[l], d};
     if (!gemm_tc_launch_out(m, l, R, static_cast<const T*>(w.gated), er, st.status, s, &e)) {
+      if (tc_gemm) return IMBA_ERR_UNSUPPORTED;
       IMBA_CK(launch_gemm_simt<T, T, EpiResidual>(static_cast<const T*>(w.gated), hdv,
                                                   static_cast<const T*>(md.o_w[l]), hdv, R, d, hdv, er, s));
     } else if (e != cudaSuccess) {
@@ -190,6 +207,7 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
   float* logits = st.logits;
   if (st.logits) {
     if (!gemm_tc_launch_policy(m, R, static_cast<const T*>(w.xf3), EpiStore{logits, md.vocab}, st.status, s, &e)) {
+      if (tc_gemm) return IMBA_ERR_UNSUPPORTED;
       IMBA_CK(launch_gemm_simt<float, float, EpiStore>(w.xf32, d, md.policy_w32, d, R, md.vocab, d,
                                                        EpiStore{logits, md.vocab}, s));
     } else if (e != cudaSuccess) {
@@ -204,6 +222,7 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
     const T* xin = bf ? static_cast<const T*>(w.xf3) : reinterpret_cast<const T*>(w.xf32);
     const int lda = bf ? 3 * d : d;
     if (!gemm_tc_launch_value(m, R, xin, lda, eb, st.status, s, &e)) {
+      if (tc_gemm) return IMBA_ERR_UNSUPPORTED;
       IMBA_CK(launch_gemm_simt<T, T, EpiBiasSilu>(xin, lda, static_cast<const T*>(md.value0_w), d, R, hd, d, eb, s));
     } else if (e != cudaSuccess) {
       return IMBA_ERR_CUDA;
@@ -244,15 +263,21 @@ imba_status_t imba_model_create(const imba_model_desc* desc, imba_model** out) {
   *out = nullptr;
   const imba_status_t v = imba::validate_desc(desc);
   if (v != IMBA_OK) return v;
+  // imba_step_noalloc's scratch array is placed on this device now, while the
+  // caller can still allocate, not at the first allocation-free step.
+  const imba_status_t na = imba::noalloc_prepare_device();
+  if (na != IMBA_OK) return na;
   imba_model* m = new (std::nothrow) imba_model();
   if (!m) return IMBA_ERR_OOM;
   m->d = *desc;
   m->uvqk_n = 2 * desc->num_heads * (desc->linear_dim + desc->attention_dim);
-  if (const char* sel = getenv("IMBA_SIMT")) {
-    m->simt_attn = strstr(sel, "attn") != nullptr;
-    m->simt_board = strstr(sel, "board") != nullptr;
+  m->simt_gemm = (desc->flags & IMBA_FLAG_SIMT_GEMM) != 0;
+  m->simt_attn = (desc->flags & IMBA_FLAG_SIMT_ATTN) != 0;
+  m->simt_board = (desc->flags & IMBA_FLAG_SIMT_BOARD) != 0;
+  if (desc->dtype == IMBA_DTYPE_BF16 && !imba::bf16_shape_supported(*desc, m->simt_gemm, m->simt_attn)) {
+    delete m;
+    return IMBA_ERR_UNSUPPORTED;
   }
-  if (const char* sel = getenv("IMBA_BOARD")) m->board_kind = strcmp(sel, "tc") == 0 ? 2 : strcmp(sel, "mma") == 0 ? 1 : 0;
   if (desc->dtype == IMBA_DTYPE_BF16 && !m->simt_board) {
     // Split bf16 copy of the board projection for the content GEMM.
     void* w3 = nullptr;
@@ -304,6 +329,7 @@ static imba_status_t step_impl(const imba_model* model, const imba_step_desc* st
   if (step->num_rows == 0) return IMBA_OK;
   const size_t need = imba::workspace_layout(model, step->num_rows, nullptr, nullptr);
   if (!workspace || workspace_bytes < need) return IMBA_ERR_OOM;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return IMBA_ERR_ARG;  // buffers are carved 256-aligned
   imba::Workspace w = imba::carve_workspace(model, step->num_rows, workspace);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (model->d.dtype == IMBA_DTYPE_BF16) return imba::run_step<imba::bf16>(model, *step, *pool, w, s, pm);

@@ -1,10 +1,10 @@
-// Board encoder for bf16 models, default path: the two pre-LN square-attention
+// Board encoder for bf16 models: the two pre-LN square-attention
 // blocks over the 64 squares of each position, the final LayerNorm and the
 // mean over squares (src/imba_chess/model/hstu_model.py:118-179, :275-278).
 // Output: the pooled 64-vector of every board as the split bf16 operand
-// [hi | lo | hi] (192 values, hi + lo = the fp32 mean to ~2^-16), like the
-// other two encoders (board_mma.cu, board_tc.cu); the 64 -> d projection and
-// the side / position embeddings follow in a GEMM epilogue.
+// [hi | lo | hi] (192 values, hi + lo = the fp32 mean to ~2^-16); the
+// 64 -> d projection and the side / position embeddings follow in a GEMM
+// epilogue.
 //
 // The dense projections go to the 5th-generation tensor cores, the per-board
 // attention stays in registers:
@@ -606,7 +606,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// [d, 64] fp32 board projection -> [d, 192] bf16 [W_hi | W_hi | W_lo], the
+// content GEMM's B operand against the pooled [p_hi | p_lo | p_hi].
+__global__ void split_board_proj_kernel(const float* __restrict__ w, int d, bf16* __restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= d * 64) return;
+  const int row = i >> 6, c = i & 63;
+  const float v = w[i];
+  const bf16 hi = __float2bfloat16_rn(v), lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+  bf16* o = out + (size_t)row * 192;
+  o[c] = hi;
+  o[64 + c] = hi;
+  o[128 + c] = lo;
+}
+
 }  // namespace
+
+cudaError_t build_board_proj_split(const imba_model_desc& md, bf16* out, cudaStream_t s) {
+  const int n = md.model_dim * 64;
+  split_board_proj_kernel<<<(n + 255) / 256, 256, 0, s>>>(md.board_out_w, md.model_dim, out);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_board_hybrid(const imba_model_desc& md, const imba_step_desc& st, bf16* pooled,
                                 cudaStream_t s) {

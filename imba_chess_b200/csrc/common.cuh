@@ -98,11 +98,11 @@ struct imba_model {
   imba_model_desc d;
   int uvqk_n;         // 2 H (d_v + d_qk)
   void* tc = nullptr;  // tensor-core GEMM state (TMA descriptors of the weights), or null
-  // Kernel selection for bf16 models (IMBA_SIMT=gemm,attn,board at handle
-  // creation selects the SIMT kernel of a component, for cross-checking).
+  // Test hooks of bf16 handles (imba_model_desc.flags): the SIMT kernel of a
+  // component instead of its tensor-core kernel, for cross-checks.
+  bool simt_gemm = false;
   bool simt_attn = false;
   bool simt_board = false;
-  int board_kind = 0;  // board encoder: 0 tcgen05 + mma.sync (default), 1 mma.sync (IMBA_BOARD=mma), 2 tcgen05 (IMBA_BOARD=tc)
   // bf16 models with the tensor-core board encoder: [d, 192] bf16 split copy
   // of the board projection (device memory owned by the handle), or null.
   void* board_proj3 = nullptr;

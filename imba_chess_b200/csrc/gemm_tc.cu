@@ -17,8 +17,6 @@
 // Used for the STU projections (uvqk with SiLU + KV append; output projection
 // with bias + residual), the split-precision policy GEMM and the value-head
 // hidden layer (hstu_attention.py:307-325, :415-424; hstu_model.py:745-751).
-#include <cstdlib>
-#include <cstring>
 #include <mutex>
 #include <new>
 
@@ -311,15 +309,15 @@ cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
 imba_status_t gemm_tc_prepare(imba_model* m) {
   const imba_model_desc& d = m->d;
   m->tc = nullptr;
-  if (d.dtype != IMBA_DTYPE_BF16) return IMBA_OK;
-  // IMBA_SIMT containing "gemm" selects the SIMT GEMMs for this handle (cross-checking).
-  const char* sel = getenv("IMBA_SIMT");
-  if (sel && strstr(sel, "gemm")) return IMBA_OK;
+  // fp32 handles, and bf16 handles whose SIMT-GEMM test hook is set, run the
+  // SIMT GEMMs.  Any other bf16 handle must get every tensor map encoded.
+  if (d.dtype != IMBA_DTYPE_BF16 || m->simt_gemm) return IMBA_OK;
   const int hdv = d.num_heads * d.linear_dim;
   const bool shapes_ok = d.model_dim % 64 == 0 && hdv % 64 == 0 && d.attention_dim % 32 == 0 &&
                          d.linear_dim % 32 == 0 && m->uvqk_n % kBNWide == 0 && d.model_dim % kBNNarrow == 0 &&
                          (d.model_dim / 2) % 32 == 0;
-  if (!shapes_ok || !encode_fn()) return IMBA_OK;  // SIMT GEMMs serve this model
+  if (!shapes_ok) return IMBA_ERR_UNSUPPORTED;
+  if (!encode_fn()) return IMBA_ERR_CUDA;  // no cuTensorMapEncodeTiled in this driver
   TCState* t = new (std::nothrow) TCState();
   if (!t) return IMBA_ERR_OOM;
   bool ok = true;
@@ -332,11 +330,13 @@ imba_status_t gemm_tc_prepare(imba_model* m) {
     ok = make_map(&t->value, d.value0_w, d.model_dim / 2, d.model_dim, (uint64_t)d.model_dim * 2, kBNNarrow);
     t->has_value = ok;
   }
-  if (ok && m->board_proj3)
-    t->has_content = make_map(&t->content, m->board_proj3, d.model_dim, 192, 192 * 2, kBNNarrow);
-  if (!ok) {
+  if (ok && m->board_proj3) {
+    ok = make_map(&t->content, m->board_proj3, d.model_dim, 192, 192 * 2, kBNNarrow);
+    t->has_content = ok;
+  }
+  if (!ok) {  // a weight tensor the TMA cannot address (alignment, stride)
     delete t;
-    return IMBA_OK;
+    return IMBA_ERR_ARG;
   }
   m->tc = t;
   return IMBA_OK;

@@ -1,15 +1,17 @@
 // Tensor-core (tcgen05 + TMA) GEMMs of the bf16 step.  Each launcher returns
-// false when it does not handle the model / shape (fp32 models, dimensions the
-// tile shapes do not cover, a TMA descriptor that cannot be encoded); the
-// caller then runs the SIMT GEMM.  When it returns true, *err holds the launch
-// status.
+// false when the handle has no tensor-core state (fp32 handles, or the SIMT
+// GEMM test hook); the caller then runs the SIMT GEMM for an fp32 or hooked
+// handle and reports IMBA_ERR_UNSUPPORTED otherwise.  When it returns true,
+// *err holds the launch status.
 #pragma once
 
 #include "epilogues.cuh"
 
 namespace imba {
 
-// Encodes the weights' TMA descriptors once per model (bf16 models only).
+// Encodes the weights' TMA descriptors once per model (bf16 models only);
+// IMBA_ERR_UNSUPPORTED / IMBA_ERR_ARG when a bf16 handle's weights cannot be
+// served by the tensor-core GEMMs.
 imba_status_t gemm_tc_prepare(imba_model* m);
 void gemm_tc_release(imba_model* m);
 

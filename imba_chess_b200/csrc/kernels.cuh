@@ -20,12 +20,7 @@ struct AttnArgs {
 
 cudaError_t launch_embed(const imba_model_desc& md, const imba_step_desc& st, float* x, cudaStream_t s);
 // Board encoder -> pooled [R, 192] split bf16 ([hi | lo | hi] of the mean):
-// tcgen05 projections + mma.sync attention (board_hybrid.cu, the default),
-// mma.sync only (board_mma.cu, IMBA_BOARD=mma) or tcgen05 only (board_tc.cu,
-// IMBA_BOARD=tc when board_tc_applies).
-bool board_tc_applies(const imba_model_desc& md);
-cudaError_t launch_board_tc(const imba_model_desc& md, const imba_step_desc& st, bf16* pooled, cudaStream_t s);
-cudaError_t launch_board_mma(const imba_model_desc& md, const imba_step_desc& st, bf16* pooled, cudaStream_t s);
+// tcgen05 projections + mma.sync per-head attention (board_hybrid.cu).
 cudaError_t launch_board_hybrid(const imba_model_desc& md, const imba_step_desc& st, bf16* pooled, cudaStream_t s);
 // [d, 64] fp32 board projection -> [d, 192] bf16 [W_hi | W_hi | W_lo].
 cudaError_t build_board_proj_split(const imba_model_desc& md, bf16* out, cudaStream_t s);
@@ -52,5 +47,8 @@ cudaError_t launch_attn_simt(const AttnArgs& a, cudaStream_t s);
 // norm and the u gate, writes `gated` and sets *fused.
 bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& md, int64_t num_pages,
                       const bf16* u, bf16* gated, cudaStream_t s, cudaError_t* err, bool* fused);
+
+// Places imba_step_noalloc's scratch array on the current device (noalloc.cu).
+imba_status_t noalloc_prepare_device();
 
 }  // namespace imba

@@ -10,44 +10,48 @@
 // workspace; this variant uses a scratch array compiled into the library.
 //
 // The scratch is one file-scope device array of IMBA_NOALLOC_SCRATCH_BYTES.
-// Every GPU that loads the library holds it until the process exits.  Its
-// device address is looked up once per device (cudaGetSymbolAddress, with
-// that device current) on the first call made on the device and cached; make
-// that first call before any stream capture.  All calls share the array: two
-// calls that overlap on the GPU (different streams, or different host threads
-// on one device) race on it and must be serialised by the caller.  No part of
-// the scratch needs to start at zero: every scratch byte the step reads is
-// written earlier in the same call, so the previous call's contents are never
-// observed.
-#include <mutex>
-
+// With lazy module loading (the CUDA default) the array is placed on a device
+// when this module is first used there, and stays until the process exits.
+// imba_model_create does that on the handle's device (noalloc_prepare_device
+// below), so the array is resident before any step runs, while the caller can
+// still allocate.  Every imba_step_noalloc call looks the array's device
+// address up again (cudaGetSymbolAddress, cheap once the module is loaded),
+// so no address is cached across a device reset.  All calls share the array:
+// two calls that overlap on the GPU (different streams, or different host
+// threads on one device) race on it and must be serialised by the caller.
+// No part of the scratch needs to start at zero: every scratch byte the step
+// reads is written earlier in the same call (the attention work-queue
+// counters are cleared by the step itself), so the previous call's contents
+// are never observed.
 #include "common.cuh"
 
 namespace {
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[IMBA_NOALLOC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {};
-
 // Device address of the scratch array on the current device.
 imba_status_t scratch_for_current_device(void** out) {
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess) return IMBA_ERR_CUDA;
-  if (dev < 0 || dev >= kMaxDevices) return IMBA_ERR_UNSUPPORTED;
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_addr[dev]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) return IMBA_ERR_CUDA;
-    g_scratch_addr[dev] = p;
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr) {
+    cudaGetLastError();
+    return IMBA_ERR_CUDA;
   }
-  *out = g_scratch_addr[dev];
+  *out = p;
   return IMBA_OK;
 }
 
 }  // namespace
+
+namespace imba {
+
+// Places the scratch array on the current device (loads this module there).
+imba_status_t noalloc_prepare_device() {
+  void* p = nullptr;
+  return scratch_for_current_device(&p);
+}
+
+}  // namespace imba
 
 extern "C" imba_status_t imba_step_noalloc(const imba_model* model, const imba_step_desc* step,
                                            const imba_pool_desc* pool, void* stream) {

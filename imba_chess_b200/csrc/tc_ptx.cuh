@@ -50,17 +50,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* status) {
+// Bounded wait for the phase with the given parity to complete: gives up
+// after limit_ns of global time, recording IMBA_ERR_TIMEOUT.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int32_t* status, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - t0 > kWaitNs) {
+    if (global_ns() - t0 > limit_ns) {
       report(status, IMBA_ERR_TIMEOUT);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* status) {
+  return mbar_wait_for(bar, parity, status, kWaitNs);
 }
 
 // Bounded wait that also gives up as soon as another role has flagged an

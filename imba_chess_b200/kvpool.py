@@ -137,6 +137,15 @@ class KVSequence:
         t = np.repeat(starts, cnt) + np.arange(total, dtype=np.int64) - np.repeat(rbase, cnt)
         return cat[np.repeat(pbase, cnt) + t // PAGE] * PAGE + t % PAGE
 
+    def truncate(self, length: int, num_pages: int) -> None:
+        """Undo reservations: back to ``length`` tokens on the first
+        ``num_pages`` pages (values recorded before the reservations); the
+        pages past them return to the pool."""
+        if num_pages < len(self.pages):
+            self.pool.release_pages(self.pages[num_pages:])
+            del self.pages[num_pages:]
+        self.length = min(self.length, int(length))
+
     def slots(self, start: int, stop: int) -> np.ndarray:
         t = np.arange(start, stop, dtype=np.int64)
         pages = np.asarray(self.pages, dtype=np.int64)

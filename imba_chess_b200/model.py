@@ -70,7 +70,10 @@ class B200HSTUChessModel:
     training = False
 
     def __init__(self, state_dict: Mapping[str, Any], *, dtype: torch.dtype = torch.bfloat16,
-                 device: torch.device | str = "cuda") -> None:
+                 device: torch.device | str = "cuda", simt: tuple[str, ...] = ()) -> None:
+        """``simt`` is a test hook for bf16 models: component names ("gemm",
+        "attn", "board") whose fp32-accumulating SIMT kernels replace the
+        tensor-core ones, so tests can compare the two on identical inputs."""
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("B200HSTUChessModel runs on a CUDA device only (no CPU fallback)")
@@ -96,6 +99,12 @@ class B200HSTUChessModel:
         self.position_embedding = SimpleNamespace(max_seq_len=d.max_pos)
         self.value_head = _ValueHeadMarker() if d.value_head else None
         self._lib = _native.load()
+        flags = 0
+        for name in simt:
+            if name not in _native.SIMT_FLAGS:
+                raise ValueError(f"unknown SIMT component {name!r}: use {sorted(_native.SIMT_FLAGS)}")
+            flags |= _native.SIMT_FLAGS[name]
+        self.weights.desc.flags = flags
         handle = ctypes.c_void_p()
         _native.check(self._lib.imba_model_create(ctypes.byref(self.weights.desc), ctypes.byref(handle)),
                       "imba_model_create")

@@ -342,13 +342,22 @@ class ActorInferenceServer:
             if turn.arena is None:
                 turn.arena = KVSequence(self.pool)
             groups.append(WaveGroup(prefix=turn.seq, prefix_len=turn.prefix_len, arena=turn.arena, chains=chains))
-        plan, own_rows = wave_plan(groups, piece, side, None,
-                                   legal_csr=(np.frombuffer(loff_b, dtype=np.int32),
-                                              np.frombuffer(lids_b, dtype=np.int32)))
-        loff = plan.legal_off
-        self._sync_if_profiling()
-        t1 = time.perf_counter()
-        value_stm, legal_flat, _ = self._run_rows(plan, R)
+        # The reference appends a wave's rows to the arena only after its
+        # forward succeeded (actor_server.py:904-914); a failed wave is rolled
+        # back so later waves mint the same row ids.
+        marks = [(t.arena, t.arena.length, len(t.arena.pages)) for t in turns]
+        try:
+            plan, own_rows = wave_plan(groups, piece, side, None,
+                                       legal_csr=(np.frombuffer(loff_b, dtype=np.int32),
+                                                  np.frombuffer(lids_b, dtype=np.int32)))
+            loff = plan.legal_off
+            self._sync_if_profiling()
+            t1 = time.perf_counter()
+            value_stm, legal_flat, _ = self._run_rows(plan, R)
+        except BaseException:
+            for arena, length, npages in reversed(marks):
+                arena.truncate(length, npages)
+            raise
         t2 = time.perf_counter()
         self.stats["wave_build_s"] += t1 - t0
         self.stats["wave_gpu_s"] += t2 - t1

@@ -276,3 +276,90 @@ def grouped_wave(
         for _ in range(k):
             legal_ids.append(random_legal_ids(rng, int(rng.integers(legal[0], legal[1] + 1)), dims.vocab))
     return GroupedWave(prefixes, concat_tokens(rows), np.concatenate(groups), legal_ids)
+
+
+# ----------------------------------------------------------------------
+# Real chess positions from seeded uniformly-random legal play
+# ----------------------------------------------------------------------
+START_FEN = "rnbqkbnr/pppppppp/8/8/8/8/PPPPPPPP/RNBQKBNR w KQkq - 0 1"
+_SIDE_FIELDS = ("turn_id", "castle_id", "ep_file_id", "halfmove_bucket_id", "fullmove_bucket_id")
+
+
+@dataclass
+class ChessGame:
+    """A game played by uniformly random legal moves from the start position:
+    its token prefix (BOS, then one EVENT token per position from the start
+    position to the current one, ``plies + 2`` tokens), the current FEN and
+    the current position's UCI-sorted legal moves (vocab ids and UCIs)."""
+
+    tokens: dict[str, np.ndarray]
+    fen: str
+    legal_ids: list[int]
+    legal_ucis: list[str]
+
+    @property
+    def plies(self) -> int:
+        return int(self.tokens["piece_ids"].shape[0]) - 2
+
+
+def _position_token(state, prev_move_id: int) -> dict[str, int | list[int]]:
+    return {"piece_ids": list(state.piece_ids), "seq_token_id": EVENT_TOKEN_ID, "prev_move_id": int(prev_move_id),
+            **{k: int(getattr(state, k)) for k in _SIDE_FIELDS}}
+
+
+def chess_game(seed: int, n_plies: int) -> ChessGame:
+    """``n_plies`` uniformly random legal moves from the start position with
+    ``numpy.random.default_rng(seed)`` (fewer when the game ends first),
+    tokenised like the reference's sequence history: BOS with the start id as
+    previous move, then each observed position with the move that reached it
+    (src/imba_chess/eval/position_evaluator.py:25-111).  Uses the worker-side
+    chess extension for move generation and the board-state encoding."""
+    from . import worker_chess as wc
+
+    rng = np.random.default_rng(seed)
+    enc = wc.BoardStateEncoder()
+    vocab = wc.static_move_vocab()
+    fen = START_FEN
+    toks = [{"piece_ids": [0] * 64, "seq_token_id": BOS_TOKEN_ID, "prev_move_id": 1,
+             **{k: 0 for k in _SIDE_FIELDS}}]
+    prev = 1  # the vocabulary's start id
+    ids, ucis = wc.legal_vocab_projection(fen)
+    for _ in range(n_plies):
+        toks.append(_position_token(enc.encode_fen(fen), prev))
+        if not ucis:
+            break
+        u = ucis[int(rng.integers(len(ucis)))]
+        fen = wc.push_uci(fen, u)
+        prev = vocab[u]
+        ids, ucis = wc.legal_vocab_projection(fen)
+    toks.append(_position_token(enc.encode_fen(fen), prev))
+    tokens = {k: np.asarray([t[k] for t in toks], dtype=np.int64) for k in TOKEN_FIELDS}
+    return ChessGame(tokens, fen, list(ids), list(ucis))
+
+
+def chess_grouped_wave(*, n_parents: int, plies: tuple[int, int], seed: int = 1234,
+                       max_children: int | None = None) -> GroupedWave:
+    """A grouped-decode wave over real positions: parent ``g`` is a
+    random-legal-play game (seed ``seed + g``, U[plies] plies, drawn with that
+    seed's generator), and its rows are the depth-0 children reached by each
+    of its legal moves (``max_children`` caps them: the first ones in UCI
+    order), each carrying the child's own UCI-sorted legal move ids."""
+    from . import worker_chess as wc
+
+    enc = wc.BoardStateEncoder()
+    vocab = wc.static_move_vocab()
+    prefixes, rows, groups, legal_ids = [], [], [], []
+    for g in range(n_parents):
+        n_plies = int(np.random.default_rng(seed + g).integers(plies[0], plies[1] + 1))
+        game = chess_game(seed + g, n_plies)
+        prefixes.append(game.tokens)
+        kids = game.legal_ucis if max_children is None else game.legal_ucis[:max_children]
+        toks = []
+        for u in kids:
+            child = wc.push_uci(game.fen, u)
+            toks.append(_position_token(enc.encode_fen(child), vocab[u]))
+            legal_ids.append(np.asarray(wc.legal_vocab_projection(child)[0], dtype=np.int64))
+        if toks:
+            rows.append({k: np.asarray([t[k] for t in toks], dtype=np.int64) for k in TOKEN_FIELDS})
+        groups.append(np.full(len(toks), g, dtype=np.int64))
+    return GroupedWave(prefixes, concat_tokens(rows), np.concatenate(groups), legal_ids)

@@ -55,6 +55,13 @@ typedef int32_t imba_status_t;
 #define IMBA_DTYPE_F32 0        /* fp32 weights, activations and KV pool          */
 #define IMBA_DTYPE_BF16 1       /* bf16 GEMM operands and KV pool, fp32 residual  */
 
+/* imba_model_desc.flags: test hooks that replace one tensor-core component of
+ * a bf16 handle by its fp32-accumulating SIMT kernel, so a test can compare
+ * the two on identical inputs.  Production handles pass 0. */
+#define IMBA_FLAG_SIMT_GEMM 1   /* projections, heads: SIMT GEMMs                 */
+#define IMBA_FLAG_SIMT_ATTN 2   /* attention: SIMT kernel + separate gate pass    */
+#define IMBA_FLAG_SIMT_BOARD 4  /* board encoder + content: fp32 SIMT kernel      */
+
 #define IMBA_MAX_LAYERS 32
 #define IMBA_PAGE_TOKENS 16     /* tokens per KV page                              */
 #define IMBA_CHUNK_ROWS 64      /* max query rows in one attention work item      */
@@ -77,7 +84,7 @@ typedef struct imba_model_desc {
   int32_t fullmove_vocab;
   int32_t has_value_head;
   int32_t dtype;            /* IMBA_DTYPE_*                        */
-  int32_t reserved;
+  int32_t flags;            /* IMBA_FLAG_* (0 for normal use)      */
 
   /* content embedding (hstu_model.py:209-228, :275-335) */
   const float* piece_square;   /* [832, 64]                                */
@@ -189,11 +196,11 @@ IMBA_API int32_t imba_device_arch(void);
 /* Validate a model description and build a handle on the current device.
  * bf16 handles encode their TMA descriptors here and keep one small device
  * copy of the board projection split into bf16 hi / lo parts ([d, 192]
- * bf16, freed by imba_model_destroy).  Environment, read here: IMBA_SIMT
- * naming components (gemm, attn, board) selects their SIMT kernels (for
- * cross-checks); IMBA_BOARD=mma or IMBA_BOARD=tc selects the mma.sync-only
- * or tcgen05-only board encoder instead of the default one (tcgen05
- * projections, mma.sync attention). */
+ * bf16, freed by imba_model_destroy).  A bf16 handle runs only on the
+ * tensor-core kernels (unless desc->flags selects a SIMT test hook): it needs
+ * head dims 64 / 64, d and H x 64 multiples of 128 and 2 H x 128 a multiple
+ * of 256; other shapes return IMBA_ERR_UNSUPPORTED (fp32 handles take any
+ * shape within the limits above). */
 IMBA_API imba_status_t imba_model_create(const imba_model_desc* desc, imba_model** out);
 IMBA_API void imba_model_destroy(imba_model* model);
 
@@ -210,13 +217,16 @@ IMBA_API imba_status_t imba_step(const imba_model* model, const imba_step_desc* 
  * that may not allocate GPU memory at decode time (a runtime whose allocator
  * owns all device memory, or an engine driver with a fixed footprint) and so
  * cannot supply imba_step's workspace.  It runs imba_step on a scratch array
- * of IMBA_NOALLOC_SCRATCH_BYTES compiled into the library (held on every GPU
- * that loads the library until exit) and calls no allocator.  Returns
- * IMBA_ERR_OOM, launching nothing, when imba_step_workspace_bytes(model,
- * step->num_rows) exceeds that size.  The first call on a device looks up the
- * array's device address and must come before any stream capture.  All calls
- * share the array: calls that overlap on the GPU race and must be serialised
- * by the caller. */
+ * of IMBA_NOALLOC_SCRATCH_BYTES compiled into the library and calls no
+ * allocator.  imba_model_create places that array on the handle's device (it
+ * then stays there until the process exits), so the allocation-free calls
+ * that follow need no set-up; the array's address is looked up on every call
+ * (no address outlives a device reset).  Returns IMBA_ERR_OOM, launching
+ * nothing, when imba_step_workspace_bytes(model, step->num_rows) exceeds that
+ * size (about 370 rows at d512 / 8 layers).  All calls share the array and
+ * it keeps the last call's contents (no step reads scratch it did not write
+ * first): calls that overlap on the GPU race and must be serialised by the
+ * caller. */
 #define IMBA_NOALLOC_SCRATCH_BYTES (8u << 20)
 IMBA_API imba_status_t imba_step_noalloc(const imba_model* model, const imba_step_desc* step,
                                          const imba_pool_desc* pool, void* stream);
@@ -234,6 +244,16 @@ IMBA_API imba_status_t imba_step_profiled(const imba_model* model, const imba_st
                                           const imba_pool_desc* pool, void* workspace,
                                           size_t workspace_bytes, void* stream,
                                           void* const* events, int32_t num_events);
+
+/* Failure-path self-test.  Launches one CTA on `stream` that runs the
+ * library's bounded device-side wait (the one every pipelined kernel uses,
+ * 2 s in production) on an mbarrier nothing arrives at, with the given limit
+ * (0 < limit_ns <= 10 s).  The wait runs out, the kernel writes
+ * IMBA_ERR_TIMEOUT to the device status word `status` and returns, leaving
+ * the context usable.  No counterpart in the reference (whose decode path has
+ * no device-side waits); it lets a host test the device-timeout error path
+ * without hanging a GPU. */
+IMBA_API imba_status_t imba_selftest_wait_timeout(int64_t limit_ns, int32_t* status, void* stream);
 
 /* KV page kernels for dense <-> paged conversion (the reference's dense
  * prefix/suffix tensors, hstu_model.py:651-752).  `dense_k` is [n, H, d_qk]

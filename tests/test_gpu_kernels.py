@@ -1,23 +1,19 @@
 """GPU: kernel-level cross-checks on identical inputs.
 
 Each tensor-core kernel of the bf16 model against the SIMT kernel of the same
-component (selected with IMBA_SIMT=<component> when the handle is created),
-on a full grouped-decode step: final hidden state, logits, value logits.
+component (the handle's SIMT test hook, ``B200HSTUChessModel(simt=...)``), on
+a full grouped-decode step: final hidden state, logits, value logits.
 
 * gemm  - tcgen05/TMA GEMMs vs SIMT GEMMs: the same bf16 operands, fp32
           accumulation (the policy GEMM is exact fp32 in SIMT and split bf16 on
           the tensor cores; the uvqk epilogue's SiLU uses the hardware tanh);
-* attn  - mma.sync paged attention (TMA-loaded KV pages, attention-output
-          norm and u gate fused into its epilogue) vs the SIMT attention and
-          the separate gate pass (the tensor-core kernel rounds softmax
-          weights to bf16 for P.V); the second wave's rows carry suffix
+* attn  - mma.sync paged attention (TMA-loaded KV pages) vs the SIMT
+          attention and the separate gate pass (the tensor-core kernel rounds
+          softmax weights to bf16 for P.V); the second wave's rows carry suffix
           chains, so several gathered extra-key tiles per CTA are covered;
-* board - the default board encoder (tcgen05 projections from TMEM in the
-          mma.sync fragment layout, mma.sync attention; bf16 operands) vs the
-          fp32 SIMT encoder;
-* board_mma - the mma.sync-only board encoder (IMBA_BOARD=mma) vs SIMT;
-* board_tc - the tcgen05 board encoder (IMBA_BOARD=tc: TMEM accumulators,
-          two boards per M = 128 tile) vs the SIMT encoder.
+* board - the board encoder (tcgen05 projections from TMEM in the mma.sync
+          fragment layout, mma.sync attention; bf16 operands) vs the fp32
+          SIMT encoder.
 """
 
 from __future__ import annotations
@@ -38,8 +34,7 @@ pytestmark = pytest.mark.gpu
 # tensor-core uvqk epilogue computes SiLU through the hardware tanh (relative
 # error ~2^-11) where the SIMT epilogue uses the exact exponential form, so
 # the gemm bounds cover that as well as accumulation order.
-TOL = {"gemm": (2e-4, 5e-3, 2e-3), "attn": (2e-3, 2e-2, 5e-3), "board": (2e-3, 3e-2, 1e-2),
-       "board_mma": (2e-3, 3e-2, 1e-2), "board_tc": (2e-3, 3e-2, 1e-2)}
+TOL = {"gemm": (2e-4, 5e-3, 2e-3), "attn": (2e-3, 2e-2, 5e-3), "board": (2e-3, 3e-2, 1e-2)}
 
 
 def _run_wave(model, dims, wave, depth2=True):
@@ -74,20 +69,15 @@ def _run_wave(model, dims, wave, depth2=True):
     return out
 
 
-@pytest.mark.parametrize("component", ["gemm", "attn", "board", "board_mma", "board_tc"])
+@pytest.mark.parametrize("component", ["gemm", "attn", "board"])
 @pytest.mark.parametrize("dims,parents", [(synth.D512, 6), (synth.SMALL, 4), (synth.D256, 5), (synth.D1024, 2)],
                          ids=["d512", "d128", "d256", "d1024"])
-def test_tensor_core_kernel_matches_simt(component, dims, parents, monkeypatch):
+def test_tensor_core_kernel_matches_simt(component, dims, parents):
     sd = synth.make_state_dict(dims, 9, profile="reference")
     plies = (20, 140) if component == "attn" else (20, 45)
     wave = synth.grouped_wave(dims, n_parents=parents, plies=plies, siblings=(20, 40), seed=99)
-    if component in ("board_tc", "board_mma"):
-        monkeypatch.setenv("IMBA_BOARD", component[6:])
     model_tc = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
-    monkeypatch.delenv("IMBA_BOARD", raising=False)
-    monkeypatch.setenv("IMBA_SIMT", "board" if component.startswith("board") else component)
-    model_simt = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
-    monkeypatch.delenv("IMBA_SIMT")
+    model_simt = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0", simt=(component,))
     a = _run_wave(model_tc, dims, wave)
     b = _run_wave(model_simt, dims, wave)
     th, tl, tv = TOL[component]
@@ -136,13 +126,7 @@ def test_attention_positions_past_max_pos():
     sd = synth.make_state_dict(dims, 21, profile="sharp")
     wave = synth.grouped_wave(dims, n_parents=3, plies=(100, 230), siblings=(20, 40), seed=23)
     model_tc = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
-    import os
-
-    os.environ["IMBA_SIMT"] = "attn"
-    try:
-        model_simt = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
-    finally:
-        del os.environ["IMBA_SIMT"]
+    model_simt = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0", simt=("attn",))
     a = _run_wave(model_tc, dims, wave)
     b = _run_wave(model_simt, dims, wave)
     th, tl, tv = TOL["attn"]
@@ -217,19 +201,17 @@ def test_legal_gather_matches_full_projection(dtype, max_rows):
 
 
 @pytest.mark.parametrize("dims", [synth.D512, synth.D1024], ids=["d512", "d1024"])
-def test_small_group_steps_match_simt(dims, monkeypatch):
+def test_small_group_steps_match_simt(dims):
     """Steps of one or two rows per group (one token per game): the paged
     attention's work items then hold a single live row block; it must match
-    the SIMT attention (IMBA_SIMT=attn) on the same steps, including the
+    the SIMT attention (the handle's SIMT test hook) on the same steps, including the
     second wave's one-token suffix chains."""
     sd = synth.make_state_dict(dims, 19, profile="reference")
     wave = synth.grouped_wave(dims, n_parents=40 if dims is synth.D512 else 12, plies=(20, 140), siblings=(1, 2),
                               seed=41)
     assert wave.num_rows <= 2 * len(wave.prefix_lens)
     model_tc = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
-    monkeypatch.setenv("IMBA_SIMT", "attn")
-    model_simt = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
-    monkeypatch.delenv("IMBA_SIMT")
+    model_simt = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0", simt=("attn",))
     a = _run_wave(model_tc, dims, wave)
     b = _run_wave(model_simt, dims, wave)
     th, tl, tv = TOL["attn"]

@@ -6,9 +6,15 @@ at load time) cannot hand ``imba_step`` a workspace; they call
 ``imba_step_noalloc``, which runs the same step on a scratch array compiled
 into the library.  This test calls it through the C ABI twice in a row, on two
 different waves (the second one's rows are children of the first one's), and
-checks every output against the regular ``imba_step`` on the same inputs at the
-fp32 tolerance of the parity tests (max abs 1e-4).  It also checks that a step
-too large for the fixed scratch is refused before anything is launched.
+checks every output against the regular ``imba_step`` on the same inputs, for
+an fp32 model (SIMT kernels) and a bf16 model (tensor-core kernels, whose TMA
+tensor maps then point into the library's scratch array).  Both entry points
+run the same kernels, so the outputs must agree to within the fp32 parity
+tolerance (max abs 1e-4; in practice bit for bit).  Before the compared calls
+one allocation-free call runs on a larger, different wave, so the compared
+calls start from another wave's leftover scratch contents.  It also checks
+that a step too large for the fixed scratch is refused before anything is
+launched.
 
 This file is named so that pytest collects it last; it runs alone in a fresh
 process as well as after the other tests.
@@ -51,19 +57,13 @@ def _fill(desc, outs, status):
     desc.status = status.data_ptr()
 
 
-def test_noalloc_step_matches_workspace_step_twice():
-    dims = synth.SMALL
-    sd = synth.make_state_dict(dims, 21, profile="sharp")
-    model = B200HSTUChessModel(sd, dtype=torch.float32, device="cuda:0")
-    lib = _native.load()
-    stream = torch.cuda.current_stream()
-    wave = synth.grouped_wave(dims, n_parents=3, plies=(5, 30), siblings=(4, 9), seed=77)
-    pool = model.new_pool(256)
+def _waves(model, dims, pool, seed):
+    """A prefill of three parents, then wave A (depth-0 siblings) and wave B
+    (one child per wave-A row, whose suffix chain is its wave-A parent)."""
+    wave = synth.grouped_wave(dims, n_parents=3, plies=(5, 30), siblings=(4, 9), seed=seed)
     seqs = [KVSequence(pool) for _ in wave.prefix_lens]
     plan0, _ = root_plan(seqs, wave.prefix_tokens)
     model.run(DeviceStep(plan0, model.device), pool)
-
-    # Wave A: depth-0 siblings; wave B: one child per wave-A row.
     order = np.argsort(wave.group_index, kind="stable")
     counts = np.bincount(wave.group_index, minlength=len(seqs))
     arenas = [KVSequence(pool) for _ in seqs]
@@ -71,13 +71,41 @@ def test_noalloc_step_matches_workspace_step_twice():
     groups_a = [WaveGroup(seqs[g], wave.prefix_lens[g], arenas[g], [[]] * int(counts[g])) for g in range(len(seqs))]
     plan_a, rows_a = wave_plan(groups_a, piece_ids_from_tokens(tok_a), side_ids_from_tokens(tok_a),
                                [wave.legal_ids[i] for i in order])
-    rng = np.random.default_rng(5)
+    rng = np.random.default_rng(seed + 1)
     tok_b = synth.random_tokens(rng, plan_a.num_rows, dims)
     groups_b = [WaveGroup(seqs[g], wave.prefix_lens[g], arenas[g], [[r] for r in rows_a[g]]) for g in range(len(seqs))]
     legal_b = [synth.random_legal_ids(rng, int(rng.integers(1, 30)), dims.vocab) for _ in range(plan_a.num_rows)]
     plan_b, _ = wave_plan(groups_b, piece_ids_from_tokens(tok_b), side_ids_from_tokens(tok_b), legal_b)
+    return plan_a, plan_b
+
+
+@pytest.mark.parametrize("dims,dtype", [(synth.SMALL, torch.float32), (synth.D256, torch.bfloat16)],
+                         ids=["fp32", "bf16"])
+def test_noalloc_step_matches_workspace_step_twice(dims, dtype):
+    sd = synth.make_state_dict(dims, 21, profile="sharp" if dtype == torch.float32 else "reference")
+    model = B200HSTUChessModel(sd, dtype=dtype, device="cuda:0")
+    lib = _native.load()
+    stream = torch.cuda.current_stream()
+    pool = model.new_pool(512)
+    plan_a, plan_b = _waves(model, dims, pool, seed=77)
 
     status = torch.zeros(1, dtype=torch.int32, device=model.device)
+    # A larger, unrelated wave first, so the compared calls below find its
+    # leftover contents in the shared scratch array.
+    big = synth.grouped_wave(dims, n_parents=4, plies=(20, 60), siblings=(20, 30), seed=5)
+    big_seqs = [KVSequence(pool) for _ in big.prefix_lens]
+    plan_big, _ = root_plan(big_seqs, big.prefix_tokens)
+    assert plan_big.num_rows > max(plan_a.num_rows, plan_b.num_rows)
+    ds_big = DeviceStep(plan_big, model.device)
+    out_big = _outputs(model, plan_big.num_rows, 0)
+    del out_big["legal_logits"], out_big["legal_logprob"]
+    _fill(ds_big.desc, out_big, status)
+    ds_big.desc.legal_logits = None
+    ds_big.desc.legal_logprob = None
+    assert int(lib.imba_step_workspace_bytes(model._handle, plan_big.num_rows)) <= _native.NOALLOC_SCRATCH_BYTES
+    assert lib.imba_step_noalloc(model._handle, ctypes.byref(ds_big.desc), ctypes.byref(pool.desc),
+                                 stream.cuda_stream) == _native.IMBA_OK
+
     steps = []
     for plan in (plan_a, plan_b):
         ds = DeviceStep(plan, model.device)
