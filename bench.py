@@ -1,24 +1,30 @@
 #!/usr/bin/env python
 """Benchmark: positions evaluated per second on the grouped-decode wave.
 
-(--workload selects the headline wave below (default), the same wave shape on
-the d1024/16L/16H model with long prefixes, or sequential-halving search
-rounds with suffix chains.)
+Headline workload (one step = one wave): a bf16 HSTU chess model, d_model
+512, 8 layers, 8 heads (head dims 64/64), random-initialised with the
+reference's initialisers; 256 parent positions reached by seeded uniformly
+random legal play of U[20, 200] plies from the start position (parent i uses
+seed 1234 + i), each expanding ALL its legal moves (K = the parent's legal
+move count) as depth-0 sibling rows that share the parent's game prefix in
+the paged KV pool (16-token pages); every sibling carries its own UCI-sorted
+legal move ids.  A step computes every sibling's policy logits at its legal
+ids, their log-softmax, the WDL value and v = p(win) - p(loss), and appends
+the sibling's KV to its turn arena.  Move generation and the board-state
+encoding come from the worker-side chess module; no dataset or checkpoint
+is available, so weights are random and positions are synthetic play.
 
-Workload (one step = one wave): a bf16 HSTU chess model, d_model 512, 8
-layers, 8 heads (head dims 64/64), random-initialised with the reference's
-initialisers; 256 parent positions with game prefixes of U[20, 200] plies
-(n plies = n + 2 tokens), each expanding U[20, 40] sibling candidate moves
-(depth-0 children sharing the parent prefix in the paged KV pool, 16-token
-pages); every sibling carries U[20, 40] legal move ids.  A step computes
-every sibling's policy logits at its legal ids, their log-softmax, the WDL
-value and v = p(win) - p(loss), and appends the sibling's KV to its turn
-arena.  Inputs are seeded synthetic token streams with the reference's
-encoded value ranges (no dataset or checkpoint is available).
+--workload selects other measured workloads (d1024: the same wave shape on
+the d1024/16L/16H model with long synthetic prefixes; halving: sequential-
+halving search rounds with suffix chains; prefill_decode: jagged prefill and
+one-token decode + KV-append steps).  The halving rounds (1,024 games per GPU,
+rounds 32/16/8/4/2) are also measured in every default run and reported under
+the "halving" key of the same line.
 
 Reported:
   value  - positions/s with the wave's inputs resident in HBM (device time,
-           CUDA events on the launching stream, max over ranks).
+           CUDA events on the launching stream, max over ranks): the median
+           of --passes timed passes of exactly --steps steps each.
   e2e    - positions/s through the C-ABI step with host buffers: pinned
            host->device copy of the packed wave, the step, device->host copy
            of its results (v and the legal log-softmax), synchronised every
@@ -28,14 +34,19 @@ Reported:
   roofline - the dominant kernel's algorithmic work per launch over its
            average launch duration, against the measured peaks.  Launch
            durations come from CUDA events around each phase, recorded in a
-           second pass of the same steps right after the timed region (the
+           separate pass of the same steps right after the timed region (the
            events themselves add device time, so the headline value is timed
            without them).
-  cpu_baseline - the CPU oracle (numpy restatement of the reference decode
-           path) on a bounded sample of the same workload on the host cores.
+  cpu_baseline - the reference's own decode path (its ActorInferenceServer,
+           fp32 eager torch on the host cores, installed unmodified in
+           baseline/_ref) on a bounded sample of the same workload.
 
-Multi-GPU (torchrun): each rank runs the same-size workload on its own
-parents (weak scaling, no collective on the data path).
+--impl reference runs that reference path alone (the reference arm), and
+adds the reference on this GPU under its CUDA bf16 autocast as a separate
+field for comparison.
+
+Multi-GPU (torchrun): each rank runs the same-size workload on its own games
+(weak scaling, no collective on the data path).
 """
 
 from __future__ import annotations
@@ -43,6 +54,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import platform
 import statistics
 import subprocess
 import sys
@@ -57,7 +69,7 @@ sys.path.insert(0, ROOT)
 METRIC = "positions evaluated/sec (grouped decode)"
 # Per-workload defaults (per GPU; weak scaling under torchrun).
 WORKLOADS = {
-    "grouped": {"parents": 256, "plies": (20, 200), "siblings": (20, 40), "rounds": None},
+    "grouped": {"parents": 256, "plies": (20, 200), "siblings": None, "rounds": None},
     "d1024": {"parents": 512, "plies": (300, 600), "siblings": (40, 40), "rounds": None},
     "halving": {"parents": 1024, "plies": (40, 250), "siblings": None, "rounds": (32, 16, 8, 4, 2)},
     # games, plies log-uniform in [lo, hi], decode steps built (cycled when more are timed)
@@ -65,33 +77,41 @@ WORKLOADS = {
 }
 UNIT = "positions/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+REF_PATH = os.path.join(ROOT, "baseline", "_ref")
 
 
-def parse_args():
+def parse_args(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--passes", type=int, default=3, help="timed passes of --steps steps; the median is reported")
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=list(WORKLOADS), default="grouped",
-                    help="grouped: the headline grouped-decode wave (d512/8L); d1024: the same wave shape on "
-                         "the d1024/16L/16H model with long prefixes; halving: sequential-halving search rounds "
-                         "with suffix chains (one step = every round of every game); prefill_decode: jagged "
-                         "prefill of every game (timed and reported apart), then one-token decode + KV append "
-                         "steps of every game (one step = one token per game)")
+    ap.add_argument("--workload", choices=list(WORKLOADS), default="grouped")
     ap.add_argument("--parents", type=int, default=None)
     ap.add_argument("--plies", type=int, nargs=2, default=None)
     ap.add_argument("--siblings", type=int, nargs=2, default=None)
     ap.add_argument("--rounds", type=int, nargs="+", default=None, help="halving: arms per round")
+    ap.add_argument("--no-halving", action="store_true", help="skip the extra halving-rounds measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-service", action="store_true")
+    ap.add_argument("--no-reference-cuda", action="store_true", help="reference arm: skip its CUDA bf16 run")
     ap.add_argument("--cpu-sample-parents", type=int, default=4)
-    ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    args = ap.parse_args()
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args(argv)
     for k, v in WORKLOADS[args.workload].items():
         if getattr(args, k) is None:
             setattr(args, k, v)
     return args
+
+
+def workload_args(args, name):
+    """A copy of ``args`` for workload ``name`` with that workload's defaults."""
+    sub = argparse.Namespace(**vars(args))
+    sub.workload = name
+    for k, v in WORKLOADS[name].items():
+        setattr(sub, k, v)
+    return sub
 
 
 def dist_env():
@@ -110,6 +130,17 @@ def load_peaks():
         return dict(PEAKS_FALLBACK), "fallback"
 
 
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor() or "unknown"
+
+
 # ----------------------------------------------------------------------
 # Workload
 # ----------------------------------------------------------------------
@@ -120,10 +151,14 @@ def workload(args, rank, world=1):
     from imba_chess_b200 import synth
     from imba_chess_b200.shard import shard_games
 
-    dims = synth.D1024 if args.workload == "d1024" else synth.D512
     mine = shard_games(args.parents * world, rank, world)
-    parts = [synth.grouped_wave(dims, n_parents=1, plies=tuple(args.plies), siblings=tuple(args.siblings),
-                                seed=1234 + i) for i in mine]
+    if args.workload == "grouped":
+        dims = synth.D512
+        parts = [synth.chess_grouped_wave(n_parents=1, plies=tuple(args.plies), seed=1234 + i) for i in mine]
+    else:
+        dims = synth.D1024
+        parts = [synth.grouped_wave(dims, n_parents=1, plies=tuple(args.plies), siblings=tuple(args.siblings),
+                                    seed=1234 + i) for i in mine]
     wave = synth.GroupedWave(
         prefix_tokens=[p.prefix_tokens[0] for p in parts],
         row_tokens=synth.concat_tokens([p.row_tokens for p in parts]),
@@ -131,6 +166,52 @@ def workload(args, rank, world=1):
         legal_ids=[ids for p in parts for ids in p.legal_ids],
     )
     return dims, wave
+
+
+def workload_config(args):
+    if args.workload == "prefill_decode":
+        return {
+            "workload": "jagged prefill + incremental decode: bf16 HSTU d512/8L/8H (max_pos 1024), "
+                        f"{args.parents} games, prefixes log-uniform in [{args.plies[0]},{args.plies[1]}] plies "
+                        "prefilled in packed batches of <= 32,768 tokens, then one-token decode + KV append "
+                        "steps of every game with its legal log-softmax and v (one step = one token per game)",
+            "games_per_gpu": args.parents,
+            "page_tokens": 16,
+            "l2": "inputs larger than L2 (prefix KV read per step > 126 MB at full size)",
+        }
+    if args.workload == "halving":
+        return {
+            "workload": "sequential-halving search rounds: bf16 HSTU d512/8L/8H (max_pos 513), "
+                        f"{args.parents} games, prefixes U[{args.plies[0]},{args.plies[1]}] plies, rounds of "
+                        f"{'/'.join(str(k) for k in args.rounds)} surviving arms per game, round r evaluates one "
+                        "node per arm at depth r whose suffix is the arm's chain in the turn arena; "
+                        "one step = every round of every game",
+            "games_per_gpu": args.parents,
+            "page_tokens": 16,
+            "l2": "inputs larger than L2 (prefix KV read per round > 126 MB at full size)",
+        }
+    if args.workload == "d1024":
+        return {
+            "workload": "grouped-decode wave: bf16 HSTU d1024/16L/16H (max_pos 1024), head dims 64/64, "
+                        f"{args.parents} parents, synthetic prefixes U[{args.plies[0]},{args.plies[1]}] plies, "
+                        f"U[{args.siblings[0]},{args.siblings[1]}] depth-0 siblings each, 16-token KV pages",
+            "parents_per_gpu": args.parents,
+            "page_tokens": 16,
+            "l2": "inputs larger than L2 (prefix KV read per step > 126 MB at full size)",
+        }
+    return {
+        "workload": "grouped-decode wave: bf16 HSTU d512/8L/8H (max_pos 513), head dims 64/64, "
+                    f"{args.parents} parents from random legal play of U[{args.plies[0]},{args.plies[1]}] plies, "
+                    "every legal move of each parent as a depth-0 sibling (K = its legal move count), "
+                    "16-token KV pages",
+        "parents_per_gpu": args.parents,
+        "page_tokens": 16,
+        "l2": "inputs larger than L2 (prefix KV read per step > 126 MB at full size)",
+    }
+
+
+def full_config(args, rows_all, world):
+    return workload_config(args) | {"rows_per_step": int(rows_all), "parallelism": f"dp{world} (independent games)"}
 
 
 # ----------------------------------------------------------------------
@@ -205,17 +286,115 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------
-# CPU oracle baseline
+# The reference's own decode path (baseline/_ref), CPU fp32 and CUDA bf16
 # ----------------------------------------------------------------------
-def cpu_oracle_rate(dims, wave, n_sample_parents, seconds, steps=None):
-    """Rows/s of the CPU oracle's grouped decode (legal log-priors and v
-    included) on the first ``n_sample_parents`` parents of the wave."""
+SIDE_KEYS = ("turn_id", "castle_id", "ep_file_id", "halfmove_bucket_id", "fullmove_bucket_id")
+
+
+class ReferenceServerRun:
+    """The reference's ``ActorInferenceServer`` (installed unmodified under
+    baseline/_ref, imported through the oracle's import shims) serving the
+    roots and the wave of the given parents: the path ``north_star`` calls the
+    reference's torch path (actor_server.py:519-551 -> forward_decode_grouped,
+    hstu_model.py:651-752).  CPU: fp32 eager on all host threads; CUDA: the
+    server's own bf16 autocast (position_evaluator.py:184-194)."""
+
+    def __init__(self, dims, wave, parents, device: str, dtype_name: str, root_chunk: int = 8):
+        from oracle import ref_shims
+
+        ref_shims.install(REF_PATH)
+        import torch
+        from imba_chess.config import ModelConfig
+        from imba_chess.eval.actor_protocol import RootEvalRequest, WaveRequest, WaveRow
+        from imba_chess.eval.actor_server import ActorInferenceServer
+        from imba_chess.model import HSTUChessModel, build_hstu_chess_config
+
+        from imba_chess_b200 import synth
+
+        self.torch = torch
+        self.device = torch.device(device)
+        if self.device.type == "cpu":
+            torch.set_num_threads(os.cpu_count() or 1)
+        cfg = build_hstu_chess_config(
+            ModelConfig(model_dim=dims.model_dim, linear_hidden_dim=dims.linear_dim,
+                        attention_dim=dims.attention_dim, num_heads=dims.num_heads, num_layers=dims.num_layers,
+                        dropout=0.0, max_position_embeddings=dims.max_pos, halfmove_vocab_size=dims.halfmove_vocab,
+                        fullmove_vocab_size=dims.fullmove_vocab, enable_value_head=dims.value_head),
+            move_vocab_size=dims.vocab)
+        model = HSTUChessModel(cfg).eval()
+        sd = synth.make_state_dict(dims, 2, profile="reference")
+        model.load_state_dict({k: torch.from_numpy(v.copy()) for k, v in sd.items()}, strict=True)
+        model = model.to(self.device)
+        dtype = torch.bfloat16 if dtype_name == "bf16" else torch.float32
+        self.server = ActorInferenceServer(model=model, device=self.device, dtype=dtype)
+        # roots in chunks (the reference merges one service() call's roots into one jagged prefill)
+        for c in range(0, len(parents), root_chunk):
+            roots = [RootEvalRequest(worker_id=g, turn_id=0, legal_vocab_ids=[2],
+                                     batch_arrays=synth.root_batch_arrays(wave.prefix_tokens[g]))
+                     for g in parents[c:c + root_chunk]]
+            self.server.service(roots)
+        rt = wave.row_tokens
+        self.requests = []
+        self.rows = 0
+        for g in parents:
+            rows = []
+            for i in np.nonzero(wave.group_index == g)[0]:
+                bs = {"piece_ids": rt["piece_ids"][i].tolist(), **{k: int(rt[k][i]) for k in SIDE_KEYS}}
+                rows.append(WaveRow(node_id=int(i), parent_id=None, prev_move_vocab_id=int(rt["prev_move_id"][i]),
+                                    board_state=bs, legal_vocab_ids=[int(x) for x in wave.legal_ids[i]]))
+            if rows:
+                self.requests.append(WaveRequest(worker_id=g, turn_id=0, rows=rows))
+                self.rows += len(rows)
+
+    def step(self) -> float:
+        """One wave through service() (inputs from Python objects, outputs
+        back as Python floats); returns its wall time in seconds."""
+        t0 = time.perf_counter()
+        self.server.service(self.requests)
+        return time.perf_counter() - t0
+
+
+def sample_parents(wave, n):
+    """The wave's first ``n`` parents that have sibling rows."""
+    counts = np.bincount(wave.group_index, minlength=len(wave.prefix_tokens))
+    return [int(g) for g in np.nonzero(counts)[0][:n]]
+
+
+def reference_cpu_rate(dims, wave, n_parents, steps=None, seconds=None, warmup=1):
+    """(rows, per-step seconds) of the reference's CPU path on the wave's
+    first ``n_parents`` parents with rows."""
+    run = ReferenceServerRun(dims, wave, sample_parents(wave, n_parents), "cpu", "f32")
+    for _ in range(max(warmup, 1)):
+        run.step()
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        times.append(run.step())
+        if steps is not None and len(times) >= steps:
+            break
+        if steps is None and time.perf_counter() - t_start >= seconds:
+            break
+    return run.rows, times
+
+
+def reference_cuda_rate(dims, wave, steps, warmup=1):
+    """(rows, per-step seconds) of the reference on this GPU (bf16 autocast)
+    over the full wave."""
+    run = ReferenceServerRun(dims, wave, list(range(len(wave.prefix_tokens))), "cuda:0", "bf16")
+    for _ in range(max(warmup, 1)):
+        run.step()
+    return run.rows, [run.step() for _ in range(steps)]
+
+
+def cpu_oracle_rate(dims, wave, n_sample_parents, steps):
+    """Rows/s of the numpy oracle port's grouped decode (legal log-priors and
+    v included) on the first ``n_sample_parents`` parents of the wave."""
     from imba_chess_b200 import synth
     from oracle.hstu_np import OracleModel, gather_legal, log_softmax_f32, value_stm
 
     sd = synth.make_state_dict(dims, 2, profile="reference")
     orc = OracleModel(sd, dims)
-    gsel = list(range(min(n_sample_parents, len(wave.prefix_tokens))))
+    gsel = sample_parents(wave, n_sample_parents)
     lens = [wave.prefix_lens[g] for g in gsel]
     pref = [orc.forward(wave.prefix_tokens[g], [0, lens[i]])["kv_caches"] for i, g in enumerate(gsel)]
     max_p = max(lens)
@@ -226,49 +405,49 @@ def cpu_oracle_rate(dims, wave, n_sample_parents, seconds, steps=None):
         grouped.append((ks, vs))
     rows = np.nonzero(np.isin(wave.group_index, gsel))[0]
     tok = synth.slice_tokens(wave.row_tokens, rows)
-    gi = wave.group_index[rows]
+    gi = np.searchsorted(np.asarray(gsel), wave.group_index[rows])  # group index within the sample
     legal = [wave.legal_ids[i] for i in rows]
-
-    def one():
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
         out = orc.forward_decode_grouped(new_token_batch=tok, positions=np.asarray(lens)[gi], group_index=gi,
                                          prefix_kv_grouped=grouped, prefix_lens_list=lens)
         for x in gather_legal(out["logits"], legal):
             log_softmax_f32(x)
         value_stm(out["value_logits"])
-
-    times = []
-    t_start = time.perf_counter()
-    while True:
-        t0 = time.perf_counter()
-        one()
         times.append(time.perf_counter() - t0)
-        if steps is not None:
-            if len(times) >= steps:
-                break
-        elif time.perf_counter() - t_start >= seconds:
-            break
     return len(rows), times
 
 
+def _torch_version():
+    import torch
+
+    return torch.__version__
+
+
 def run_reference(args):
-    """Reference arm: the CPU oracle port of the reference decode path, all
-    host threads, each step one bounded sample (4 parents) of the wave."""
+    """Reference arm: the reference's own decode path (its ActorInferenceServer
+    on the host cores, fp32 eager, all host threads), each step a bounded
+    sample (the wave's first --cpu-sample-parents parents); rank 0 only."""
     world, rank, _ = dist_env()
     if rank != 0:
         return
-    if args.workload in ("halving", "prefill_decode"):
-        print(json.dumps({"impl": "reference", "unavailable": "the CPU reference arm is timed on the grouped-decode "
+    if args.workload not in ("grouped", "d1024"):
+        print(json.dumps({"impl": "reference", "unavailable": "the reference arm is timed on the grouped-decode "
                                                               "wave workloads only"}), flush=True)
         return
-    dims, wave = workload(args, 0)
-    n_rows, _ = cpu_oracle_rate(dims, wave, args.cpu_sample_parents, 0.0, steps=1)  # warm (imports, caches)
-    for _ in range(max(args.warmup - 1, 0)):
-        cpu_oracle_rate(dims, wave, args.cpu_sample_parents, 0.0, steps=1)
-    n_rows, times = cpu_oracle_rate(dims, wave, args.cpu_sample_parents, 0.0, steps=args.steps)
+    if not os.path.isdir(os.path.join(REF_PATH, "imba_chess")):
+        print(json.dumps({"impl": "reference", "unavailable": "the reference is not installed under baseline/_ref"}),
+              flush=True)
+        return
+    dims, wave = workload(args, 0, world)
+    rows_all = wave.num_rows * world
+    n_rows, times = reference_cpu_rate(dims, wave, args.cpu_sample_parents, steps=args.steps, warmup=args.warmup)
     total = float(sum(times))
     value = n_rows * len(times) / total
     cores = os.cpu_count() or 1
-    sample = f"{args.cpu_sample_parents} parents ({n_rows} sibling rows) of the {args.parents}-parent wave per step"
+    sample = (f"the wave's first {args.cpu_sample_parents} parents with rows ({n_rows} sibling rows) of "
+              f"{args.parents} per step, reference ActorInferenceServer.service(), fp32 eager torch")
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -283,46 +462,28 @@ def run_reference(args):
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": workload_config(args),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "config": full_config(args, rows_all, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "reference", "sample": sample,
+                         "cpu_model": cpu_model(), "torch": _torch_version()},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    import torch
+
+    if not args.no_reference_cuda and torch.cuda.is_available():
+        # For comparison only (not the arm): the reference on this GPU under its
+        # CUDA bf16 autocast, full wave per step.
+        csteps = max(1, min(args.steps, 5))
+        rows, ct = reference_cuda_rate(dims, wave, csteps, warmup=1)
+        line["reference_cuda_bf16"] = {
+            "value": rows * len(ct) / sum(ct), "unit": UNIT, "ms_per_step": 1000.0 * sum(ct) / len(ct),
+            "rows_per_step": rows, "steps": csteps,
+            "what": "reference ActorInferenceServer.service() on cuda:0 with bf16 autocast, eager torch, full wave"}
     print(json.dumps(line), flush=True)
 
 
-def workload_config(args):
-    if args.workload == "prefill_decode":
-        return {
-            "workload": "jagged prefill + incremental decode: bf16 HSTU d512/8L/8H (max_pos 1024), "
-                        f"{args.parents} games, prefixes log-uniform in [{args.plies[0]},{args.plies[1]}] plies "
-                        "prefilled in packed batches of <= 32,768 tokens, then one-token decode + KV append "
-                        "steps of every game with its legal log-softmax and v (one step = one token per game)",
-            "games_per_gpu": args.parents,
-            "page_tokens": 16,
-            "l2": "inputs larger than L2 (prefix KV read per step > 126 MB at full size)",
-        }
-    if args.workload == "halving":
-        return {
-            "workload": "sequential-halving search rounds: bf16 HSTU d512/8L/8H (max_pos 513), "
-                        f"{args.parents} games, prefixes U[{args.plies[0]},{args.plies[1]}] plies, rounds of "
-                        f"{'/'.join(str(k) for k in args.rounds)} surviving arms per game, round r evaluates one "
-                        "node per arm at depth r whose suffix is the arm's chain in the turn arena; "
-                        "one step = every round of every game",
-            "games_per_gpu": args.parents,
-            "page_tokens": 16,
-            "l2": "inputs larger than L2 (prefix KV read per round > 126 MB at full size)",
-        }
-    model = "d1024/16L/16H (max_pos 1024)" if args.workload == "d1024" else "d512/8L/8H (max_pos 513)"
-    return {
-        "workload": f"grouped-decode wave: bf16 HSTU {model}, head dims 64/64, "
-                    f"{args.parents} parents, prefixes U[{args.plies[0]},{args.plies[1]}] plies, "
-                    f"U[{args.siblings[0]},{args.siblings[1]}] depth-0 siblings each, 16-token KV pages",
-        "parents_per_gpu": args.parents,
-        "page_tokens": 16,
-        "l2": "inputs larger than L2 (prefix KV read per step > 126 MB at full size)",
-    }
-
-
+# ----------------------------------------------------------------------
+# B200 arm
+# ----------------------------------------------------------------------
 def prefill(model, pool, seqs, tokens, device, max_tokens=32768):
     """Prefill sequences in packed batches of at most max_tokens tokens (setup, untimed)."""
     import torch
@@ -384,7 +545,7 @@ def build_waves(args, dims, model, device, rank, world):
         _, wave = workload(args, rank, world)
         lens = wave.prefix_lens
         B = wave.num_rows
-        pool = model.new_pool(sum(-(-n // 16) for n in lens) + 4 * (-(-B // 16)) + 64)
+        pool = model.new_pool(sum(-(-n // 16) for n in lens) + 4 * (-(-B // 16)) + 2 * len(lens) + 64)
         seqs = [KVSequence(pool) for _ in lens]
         prefill(model, pool, seqs, wave.prefix_tokens, device)
         order = np.argsort(wave.group_index, kind="stable")
@@ -420,9 +581,6 @@ def build_waves(args, dims, model, device, rank, world):
     return pool, plans, None
 
 
-# ----------------------------------------------------------------------
-# B200 arm
-# ----------------------------------------------------------------------
 PHASES = ("embed", "ln", "uvqk_gemm", "attention", "gate", "out_gemm", "final_ln", "policy_gemm", "value_gemm",
           "value_legal")
 
@@ -500,38 +658,31 @@ def read_traffic():
     return out
 
 
-def run_b200(args):
+def count_launches(dims, plan):
+    """Kernel launches of one bf16 wave step (legal logits only): board
+    encoder, content projection GEMM, L x (input LN, uvqk GEMM, attention with
+    the fused norm / gate (a separate gate pass above 8 heads), output GEMM),
+    final LN, value GEMM, value / legal."""
+    return 2 + (4 if dims.num_heads <= 8 else 5) * dims.num_layers + 3
+
+
+def measure(args, model, dims, device, rank, world, sampler=None):
+    """Everything measured on one workload: the timed passes (device time,
+    max over ranks), the per-phase profile pass, the roofline of the dominant
+    kernel and the end-to-end pass through the C ABI with host buffers."""
+    import ctypes
+
     import torch
     import torch.distributed as dist
 
-    world, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=device, timeout=__import__("datetime").timedelta(seconds=300))
-
-    from imba_chess_b200 import _native, synth
-    from imba_chess_b200.kvpool import KVSequence
-    from imba_chess_b200.model import B200HSTUChessModel
+    from imba_chess_b200 import _native
     from imba_chess_b200.plan import DeviceStep
     from imba_chess_b200.shard import reduce_max, reduce_sum
-    from imba_chess_b200.steps import WaveGroup, root_plan, wave_plan
 
-    if args.workload == "d1024":
-        dims = synth.D1024
-    elif args.workload == "prefill_decode":
-        dims = synth.ModelDims(512, 8, 8, max_pos=1024)
-    else:
-        dims = synth.D512
-    sd = synth.make_state_dict(dims, 2, profile="reference")
-    model = B200HSTUChessModel(sd, dtype=torch.bfloat16, device=device)
     pool, plans, extra = build_waves(args, dims, model, device, rank, world)
-    wave = extra if args.workload in ("grouped", "d1024") else None
     stream = torch.cuda.current_stream(device)
     L = dims.num_layers
     n_ev = int(model._lib.imba_profile_event_count(model._handle))
-
-    import ctypes
 
     class Wave:
         def __init__(self, plan):
@@ -569,7 +720,7 @@ def run_b200(args):
         return [waves[i % len(waves)]] if cycle else waves
 
     R = sum(w.R for w in step_waves(0))  # positions per step on this rank
-    prefill_info = None
+    result = {}
     if args.workload == "prefill_decode":
         # The jagged prefill, timed apart (device time of its packed batches).
         psteps = [DeviceStep(p, device) for p in extra]
@@ -584,8 +735,8 @@ def run_b200(args):
         model.check_status()
         ntok = sum(p.num_rows for p in extra)
         pms = e0.elapsed_time(e1)
-        prefill_info = {"tokens": int(ntok), "batches": len(extra), "ms": round(pms, 3),
-                        "tokens_per_s": ntok / (pms / 1000.0)}
+        result["prefill"] = {"tokens": int(ntok), "batches": len(extra), "ms": round(pms, 3),
+                             "tokens_per_s": ntok / (pms / 1000.0)}
 
     def make_events():
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
@@ -602,22 +753,26 @@ def run_b200(args):
         step_plain(i)
     torch.cuda.synchronize()
     model.check_status()
-    sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.3)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_end = torch.cuda.Event(enable_timing=True)
-    t_start.record(stream)
-    for i in range(args.steps):
-        step_plain(i)
-    t_end.record(stream)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    sampler.stop()
+    if sampler is not None:
+        sampler.start()
+        time.sleep(0.3)
+    pass_ms = []
+    for _ in range(max(args.passes, 1)):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for i in range(args.steps):
+            step_plain(i)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        pass_ms.append(reduce_max(t_start.elapsed_time(t_end), device))
+    if sampler is not None:
+        sampler.stop()
     model.check_status()
     # Per-phase breakdown: a separate pass of the same steps with CUDA events
     # between phases (the events add device time, so this pass is not the
@@ -629,7 +784,7 @@ def run_b200(args):
             w.run_profiled(arr)
     torch.cuda.synchronize()
     model.check_status()
-    elapsed_ms = reduce_max(t_start.elapsed_time(t_end), device)
+    elapsed_ms = statistics.median(pass_ms)
     rows_all = reduce_sum(R, device)  # positions per step over all ranks
     ms_per_step = elapsed_ms / args.steps
     value = rows_all * args.steps / (elapsed_ms / 1000.0)
@@ -678,7 +833,7 @@ def run_b200(args):
         "peak": peaks["bf16_tflops_sustained"] if bound == "tensor" else peaks["hbm_gbs"],
         "unit": dk["unit"],
         "frac": dk["frac"],
-        # the per-row DRAM traffic was captured on the grouped-decode wave
+        # the per-row DRAM traffic was captured on the headline wave
         "traffic": traffic[dom] * R if dom in traffic and args.workload == "grouped" else None,
         "peak_source": f"{peak_src} (MEASURED_PEAKS.json: bf16 sustained / HBM copy)",
         "per_launch_work": amount,
@@ -715,42 +870,103 @@ def run_b200(args):
         "d2h_bytes_per_step": int(sum(w.host_out.numel() * 4 for w in step_waves(0))),
         "p50_wave_latency_ms": round(1000.0 * statistics.median(lat), 3),
     }
+    result.update({
+        "value": value,
+        "ms_per_step": ms_per_step,
+        "passes_ms_per_step": [round(p / args.steps, 4) for p in pass_ms],
+        "rows_all": rows_all,
+        "e2e": e2e,
+        "roofline": roofline,
+        "kernels": kernels,
+        "gpu_launches": int(args.steps * len(step_waves(0)) * count_launches(dims, plans[0])),
+        "wave": extra if args.workload in ("grouped", "d1024") else None,
+    })
+    del waves, pool
+    torch.cuda.synchronize()
+    return result
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        os.environ.setdefault("NCCL_DEBUG", "INFO")  # communicator init lines (ranks) in the log
+        dist.init_process_group("nccl", device_id=device, timeout=__import__("datetime").timedelta(seconds=300))
+
+    from imba_chess_b200 import synth
+    from imba_chess_b200.model import B200HSTUChessModel
+
+    if args.workload == "d1024":
+        dims = synth.D1024
+    elif args.workload == "prefill_decode":
+        dims = synth.ModelDims(512, 8, 8, max_pos=1024)
+    else:
+        dims = synth.D512
+    sd = synth.make_state_dict(dims, 2, profile="reference")
+    model = B200HSTUChessModel(sd, dtype=torch.bfloat16, device=device)
+    sampler = ClockSampler(local)
+    res = measure(args, model, dims, device, rank, world, sampler=sampler)
 
     line = {
         "metric": METRIC,
-        "value": value,
+        "value": res["value"],
         "unit": UNIT,
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": ms_per_step,
+        "ms_per_step": res["ms_per_step"],
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": workload_config(args) | {"rows_per_step": int(rows_all), "parallelism": f"dp{world} (independent games)"},
-        "e2e": e2e,
-        "roofline": roofline,
-        "kernels": kernels,
+        "config": full_config(args, res["rows_all"], world),
+        "e2e": res["e2e"],
+        "roofline": res["roofline"],
+        "kernels": res["kernels"],
         "clocks": sampler.summary(),
-        "gpu_launches": int(args.steps * len(step_waves(0)) * count_launches(dims, plans[0])),
+        "gpu_launches": res["gpu_launches"],
+        "passes_ms_per_step": res["passes_ms_per_step"],
     }
-
-    if prefill_info is not None:
-        line["prefill"] = prefill_info
+    if "prefill" in res:
+        line["prefill"] = res["prefill"]
+    wave = res["wave"]
+    # The sequential-halving search rounds (1,024 games per GPU), measured in
+    # the same run on the same model (every rank takes the same steps).
+    if args.workload == "grouped" and not args.no_halving:
+        hargs = workload_args(args, "halving")
+        hres = measure(hargs, model, dims, device, rank, world)
+        line["halving"] = {
+            "value": hres["value"], "unit": UNIT, "ms_per_step": hres["ms_per_step"],
+            "passes_ms_per_step": hres["passes_ms_per_step"],
+            "config": full_config(hargs, hres["rows_all"], world), "e2e": hres["e2e"],
+            "roofline": {k: hres["roofline"][k] for k in ("kernel", "bound", "achieved", "peak", "unit", "frac",
+                                                            "step_roof_ms", "step_frac")},
+            "gpu_launches": hres["gpu_launches"],
+        }
     if rank == 0 and world == 1 and not args.no_service and wave is not None:
         line["service_api"] = service_api(args, dims, wave, sd, device)
     if rank == 0 and world == 1 and not args.no_cpu_baseline and wave is not None:
-        n_rows, times = cpu_oracle_rate(dims, wave, args.cpu_sample_parents, args.cpu_seconds)
-        line["cpu_baseline"] = {
-            "value": n_rows * len(times) / sum(times),
-            "unit": UNIT,
-            "cores": os.cpu_count() or 1,
-            "kind": "port",
-            "sample": f"{args.cpu_sample_parents} parents ({n_rows} sibling rows) x {len(times)} repetitions, "
-                      "numpy oracle fp32",
-        }
+        cores = os.cpu_count() or 1
+        if os.path.isdir(os.path.join(REF_PATH, "imba_chess")):
+            n_rows, times = reference_cpu_rate(dims, wave, args.cpu_sample_parents, seconds=args.cpu_seconds)
+            line["cpu_baseline"] = {
+                "value": n_rows * len(times) / sum(times), "unit": UNIT, "cores": cores, "kind": "reference",
+                "sample": f"the wave's first {args.cpu_sample_parents} parents ({n_rows} sibling rows) x "
+                          f"{len(times)} waves, reference ActorInferenceServer.service(), fp32 eager torch",
+                "cpu_model": cpu_model(), "torch": _torch_version()}
+        n_rows, times = cpu_oracle_rate(dims, wave, args.cpu_sample_parents, steps=3)
+        port = {"value": n_rows * len(times) / sum(times), "unit": UNIT, "cores": cores, "kind": "port",
+                "sample": f"the wave's first {args.cpu_sample_parents} parents ({n_rows} sibling rows) x "
+                          f"{len(times)} repetitions, numpy oracle fp32"}
+        if "cpu_baseline" in line:
+            line["cpu_baseline_port"] = port
+        else:
+            line["cpu_baseline"] = port
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -758,56 +974,48 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
-def count_launches(dims, plan):
-    """Kernel launches of one bf16 wave step (legal logits only): board
-    encoder, content projection GEMM, L x (input LN, uvqk GEMM, attention with
-    the fused norm / gate (a separate gate pass above 8 heads), output GEMM),
-    final LN, value GEMM, value / legal."""
-    return 2 + (4 if dims.num_heads <= 8 else 5) * dims.num_layers + 3
-
-
 def service_api(args, dims, wave, sd, device):
     """Reference-compatible ActorInferenceServer.service() on the same wave:
     one WaveRequest per parent, Python wire objects in and out."""
     import torch
 
+    from imba_chess_b200 import synth
     from imba_chess_b200.model import B200HSTUChessModel
     from imba_chess_b200.protocol import RootEvalRequest, WaveRequest, WaveRow
     from imba_chess_b200.server import ActorInferenceServer
 
     model = B200HSTUChessModel(sd, dtype=torch.bfloat16, device=device)
     B = wave.num_rows
-    reps = 5
-    pages = sum(-(-n // 16) for n in wave.prefix_lens) + (reps + 2) * (-(-B // 16)) + 2 * len(wave.prefix_lens) + 64
+    reps = 7
+    pages = sum(-(-n // 16) for n in wave.prefix_lens) + (reps + 2) * (-(-B // 16) + len(wave.prefix_lens)) + 64
     server = ActorInferenceServer(model=model, device=device, dtype=torch.bfloat16, kv_pool_pages=pages)
-    roots = []
-    for g, pt in enumerate(wave.prefix_tokens):
-        T = int(pt["piece_ids"].shape[0])
-        ba = {k: v.tolist() for k, v in pt.items()}
-        ba.update(total_tokens=T, seq_offsets=[0, T])
-        roots.append(RootEvalRequest(worker_id=g, turn_id=0, legal_vocab_ids=[2], batch_arrays=ba))
+    roots = [RootEvalRequest(worker_id=g, turn_id=0, legal_vocab_ids=[2], batch_arrays=synth.root_batch_arrays(pt))
+             for g, pt in enumerate(wave.prefix_tokens)]
     server.service(roots)
-    keys = ("turn_id", "castle_id", "ep_file_id", "halfmove_bucket_id", "fullmove_bucket_id")
     reqs = []
     rt = wave.row_tokens
     for g in range(len(wave.prefix_tokens)):
         rows = []
         for i in np.nonzero(wave.group_index == g)[0]:
-            bs = {"piece_ids": rt["piece_ids"][i].tolist(), **{k: int(rt[k][i]) for k in keys}}
+            bs = {"piece_ids": rt["piece_ids"][i].tolist(), **{k: int(rt[k][i]) for k in SIDE_KEYS}}
             rows.append(WaveRow(node_id=int(i), parent_id=None, prev_move_vocab_id=int(rt["prev_move_id"][i]),
                                 board_state=bs, legal_vocab_ids=wave.legal_ids[i].tolist()))
-        reqs.append(WaveRequest(worker_id=g, turn_id=0, rows=rows))
+        if rows:
+            reqs.append(WaveRequest(worker_id=g, turn_id=0, rows=rows))
     server.service(reqs)  # warm-up
+    for k in server.stats:
+        server.stats[k] = 0
     lat = []
     for _ in range(reps):
         t0 = time.perf_counter()
         server.service(reqs)
         lat.append(time.perf_counter() - t0)
     p50 = statistics.median(lat)
+    st = server.stats
     return {"value": B / p50, "unit": UNIT, "p50_wave_latency_ms": round(1000 * p50, 3), "calls": reps,
-            "stats_wave_build_s": round(server.stats["wave_build_s"], 4),
-            "stats_wave_gpu_s": round(server.stats["wave_gpu_s"], 4),
-            "stats_wave_post_s": round(server.stats["wave_post_s"], 4)}
+            "build_ms_per_wave": round(1000 * st["wave_build_s"] / reps, 3),
+            "gpu_ms_per_wave": round(1000 * st["wave_gpu_s"] / reps, 3),
+            "post_ms_per_wave": round(1000 * st["wave_post_s"] / reps, 3)}
 
 
 def main():

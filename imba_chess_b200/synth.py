@@ -362,4 +362,23 @@ def chess_grouped_wave(*, n_parents: int, plies: tuple[int, int], seed: int = 12
         if toks:
             rows.append({k: np.asarray([t[k] for t in toks], dtype=np.int64) for k in TOKEN_FIELDS})
         groups.append(np.full(len(toks), g, dtype=np.int64))
-    return GroupedWave(prefixes, concat_tokens(rows), np.concatenate(groups), legal_ids)
+    row_tokens = concat_tokens(rows) if rows else empty_tokens()
+    return GroupedWave(prefixes, row_tokens, np.concatenate(groups), legal_ids)
+
+
+def empty_tokens() -> dict[str, np.ndarray]:
+    """Zero tokens, with every field's shape and dtype."""
+    return {k: np.zeros((0, 64) if k == "piece_ids" else (0,), dtype=np.int64) for k in TOKEN_FIELDS}
+
+
+def root_batch_arrays(tok: dict[str, np.ndarray], game_id: str = "g") -> dict:
+    """A game prefix as the wire form of a full ``RootEvalRequest``
+    (``batch_arrays``: plain lists, one jagged document), with every field
+    the reference's ``_tensorize_root_batch`` reads
+    (src/imba_chess/eval/actor_server.py:120-133; built like
+    ``_SequenceHistory._build_single_batch``, position_evaluator.py:80-100)."""
+    n = int(tok["piece_ids"].shape[0])
+    ba = {k: np.asarray(tok[k]).tolist() for k in TOKEN_FIELDS}
+    ba.update(game_id=[game_id], num_games=1, total_tokens=n, seq_lens=[n], seq_offsets=[0, n],
+              game_result_white=[0], target_move_id=[-100] * n, played_by_elo=[0] * n)
+    return ba

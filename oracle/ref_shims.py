@@ -1,6 +1,8 @@
-"""Import shims that let the reference imba-chess package load in a container
-without its optional dependencies.  Used only by ``make_golden.py`` (fixture
-generation), never by the product or by the GPU tests.
+"""Import shims that let the reference imba-chess package load without its
+optional dependencies.  TEST INFRASTRUCTURE ONLY: used by
+``tests/golden/make_golden.py`` (fixture generation) and by ``bench.py``'s
+reference arm (the reference's own decode path, timed as the baseline),
+never by the product.
 
 Three stand-ins, each written from the documented semantics of the missing
 package rather than from its source:
@@ -16,7 +18,11 @@ package rather than from its source:
   actor server never call chess code; permissive module stubs whose attributes
   are inert objects satisfy the module-level imports.
 * ``TORCHDYNAMO_DISABLE=1``: the reference wraps ``create_block_mask`` in
-  ``torch.compile``; with dynamo disabled it runs eagerly on CPU.
+  ``torch.compile``; with dynamo disabled it runs eagerly.
+
+``install(reference_path)`` takes the directory that holds the reference's
+``imba_chess`` package (its source tree's ``src`` or a pip ``--target``
+install) and puts it first on ``sys.path``.
 """
 
 from __future__ import annotations
@@ -24,9 +30,6 @@ from __future__ import annotations
 import os
 import sys
 import types
-
-REFERENCE_SRC = "/root/reference/src"
-
 
 class _Inert:
     """Object whose every attribute, call, index and iteration is inert."""
@@ -99,8 +102,11 @@ def _make_attn_gym():
     return pkg, masks
 
 
-def install() -> None:
-    """Install the shims and put the reference sources on ``sys.path``."""
+def install(reference_path: str) -> None:
+    """Install the shims and put ``reference_path`` (the directory holding
+    the reference's ``imba_chess`` package) first on ``sys.path``."""
+    if not os.path.isdir(os.path.join(reference_path, "imba_chess")):
+        raise FileNotFoundError(f"no imba_chess package under {reference_path}")
     os.environ.setdefault("TORCHDYNAMO_DISABLE", "1")
     if "attn_gym" not in sys.modules:
         pkg, masks = _make_attn_gym()
@@ -116,5 +122,5 @@ def install() -> None:
         if full not in sys.modules:
             sys.modules[full] = _StubModule(full)
             setattr(sys.modules["chess"], sub, sys.modules[full])
-    if REFERENCE_SRC not in sys.path:
-        sys.path.insert(0, REFERENCE_SRC)
+    if reference_path not in sys.path:
+        sys.path.insert(0, reference_path)

@@ -34,11 +34,13 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
-sys.path.insert(0, HERE)
 
-import ref_shims  # noqa: E402
+# The reference's source tree (read-only); override with IMBA_REFERENCE_SRC.
+REFERENCE_SRC = os.environ.get("IMBA_REFERENCE_SRC", "/root/reference/src")
 
-ref_shims.install()
+from oracle import ref_shims  # noqa: E402
+
+ref_shims.install(REFERENCE_SRC)
 
 import torch  # noqa: E402
 

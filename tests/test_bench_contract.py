@@ -13,7 +13,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def _run(*extra):
     cmd = [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "1",
-           "--parents", "8", "--cpu-sample-parents", "1", *extra]
+           "--parents", "8", "--cpu-sample-parents", "1", "--no-reference-cuda", *extra]
     out = subprocess.run(cmd, capture_output=True, text=True, timeout=600, cwd=ROOT)
     assert out.returncode == 0, out.stderr[-2000:]
     lines = [l for l in out.stdout.splitlines() if l.startswith("{")]
@@ -22,15 +22,22 @@ def _run(*extra):
 
 
 def test_reference_arm_line():
+    """The reference arm runs the reference's own ActorInferenceServer from
+    its unmodified install under baseline/_ref (or reports it unavailable)."""
     d = _run()
+    assert d["impl"] == "reference"
+    if not os.path.isdir(os.path.join(ROOT, "baseline", "_ref", "imba_chess")):
+        assert "unavailable" in d
+        return
     for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
               "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
         assert k in d, k
-    assert d["impl"] == "reference"
     assert d["value"] > 0 and d["unit"] == "positions/s"
-    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
+    cb = d["cpu_baseline"]
+    assert cb["kind"] == "reference" and cb["cores"] >= 1 and cb["cpu_model"] and cb["torch"]
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
-    assert "workload" in d["config"]
+    # the same config dict as the B200 arm's line
+    assert {"workload", "rows_per_step", "parallelism"} <= set(d["config"])
 
 
 def test_reference_arm_unavailable_for_search_workloads():

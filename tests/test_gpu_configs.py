@@ -148,9 +148,17 @@ def _assert_bf16(stats):
 # config 1: fp32 d256 / 4 layers / 4 heads, 64 games, prefill + one decode token
 # ----------------------------------------------------------------------
 def _cfg1_games():
+    """64 games of U[10, 120] random legal plies that are still in progress
+    (a game that ended in mate or stalemate has no decode token to add; the
+    next seed takes its place)."""
     rng = np.random.default_rng(1234)
-    plies = rng.integers(10, 121, size=64)
-    return [synth.chess_game(1234 + g, int(n)) for g, n in enumerate(plies)]
+    games, seed = [], 1234
+    while len(games) < 64:
+        g = synth.chess_game(seed, int(rng.integers(10, 121)))
+        seed += 1
+        if g.legal_ucis:
+            games.append(g)
+    return games
 
 
 def test_config1_prefill_then_decode_fp32_model_api():
