@@ -5,21 +5,27 @@
 // Persistent: one CTA per SM (per head group when H > 8) pulls work items
 // from a per-layer atomic counter.  An item is <= 32 query rows of one
 // sequence group (a chunk; a 64-row chunk is two items) and HC heads (all of
-// them when H <= 8).  Warp roles:
+// them when H <= 8).  Warp roles, every hand-off an mbarrier:
 //   * the producer warp (index 2 HC) claims the next chunk, resolves its
 //     rows' metadata (row ids, visible prefix, query positions, extra-key
-//     offsets and the first extra tile's owners) into one of two item
-//     buffers, then streams the group's visible KV pages: per 16-token page
-//     two TMA tiled loads (K rows of the HC heads, then their V rows:
-//     [HC x 16, 64] bf16 with the 128-byte swizzle) into a ring of stages
-//     with one "full" (transaction bytes) and one "empty" (one arrive per
-//     consumer warp) mbarrier per stage.  It runs ahead into the next item
-//     while the consumers finish the current one, so the metadata and page
-//     latency of an item overlaps the previous item's math.
+//     offsets and the first extra key's slot) into one of two item buffers,
+//     copies the item's query tile (cp.async, one lane per row, arrival
+//     tracked on q_full) into one of two swizzled query buffers, then
+//     streams the group's visible KV pages: per 16-token page two TMA tiled
+//     loads (K rows of the HC heads, then their V rows: [HC x 16, 64] bf16
+//     with the 128-byte swizzle) into a ring of stages with one "full"
+//     (transaction bytes) and one "empty" (one arrive per consumer warp)
+//     mbarrier per stage.  It runs ahead into the next item while the
+//     consumers finish the current one, so an item's metadata, queries and
+//     first pages arrive under the previous item's math.
 //   * consumer warps 0 .. 2 HC - 1: warp w owns local head w / 2 and query
-//     rows 16 (w % 2) .. +15 of the item.  The item's queries are staged
-//     once in a swizzled shared tile (cp.async) and read per page with
-//     ldmatrix, which keeps a warp's registers to its softmax state and O.
+//     rows 16 (w % 2) .. +15 of the item, reading its queries per page from
+//     the query buffer with ldmatrix (registers hold only the softmax state
+//     and O).
+//   * with every head in the CTA, kEpiWarps norm / gate warps: LayerNorm of
+//     each row's H dv outputs and the u gate, from the O tile the consumers
+//     leave in shared memory, so the consumers go straight on to the next
+//     item.
 // Every page is read from HBM once per item and serves every sibling row and
 // every head.  Per page a consumer warp computes S = Q K^T (mma.sync
 // m16n8k16, fp32 accumulate), scales it, adds the relative-position bias
@@ -30,11 +36,11 @@
 // per row afterwards: the four lanes that share a row split the 64-dim dot
 // product (a quad reduction), update the row's online softmax and add p v to
 // their O columns, reading K / V straight from the pool.
-// Epilogue: O / l; when the CTA holds every head, O is staged in shared
-// memory and after one barrier each warp takes whole rows: LayerNorm over the
-// row's H dv outputs (no affine, eps 1e-6, warp reductions) times u, stored
-// in bf16 for the output projection; otherwise fp32 O is stored and the gate
-// runs as its own pass.
+// Epilogue: O / l, rounded to bf16 (the reference's bf16 attention output
+// is bf16 too) into the O tile; the norm warps take whole rows: LayerNorm
+// over the row's H dv outputs (no affine, eps 1e-6, warp reductions) times
+// u, stored in bf16 for the output projection.  With more than 8 heads a CTA
+// holds a head group: fp32 O is stored and the gate runs as its own pass.
 // Every wait is bounded; a timeout sets the status word and ends the CTA.
 // Semantics: src/imba_chess/model/hstu_attention.py :64-76, :81-132,
 // :134-148, :327-413 (attention), :185-190 (norm and gate).
@@ -54,7 +60,8 @@ constexpr int kPageBytes = IMBA_PAGE_TOKENS * 128;            // 16 tokens x 64 
 constexpr size_t kSmemMax = 227 * 1024;                       // dynamic shared memory per CTA
 constexpr int kMaxStages = 8;
 constexpr int kMetaBytes = 8192;
-constexpr int kMaxThreads = (2 * kMaxHC + 1) * 32;
+constexpr int kEpiWarps = 3;                                 // norm / gate warps of the fused epilogue
+constexpr int kMaxThreads = (2 * kMaxHC + 1 + kEpiWarps) * 32;
 
 // Item buffer (int32 words): header, then per-row arrays.
 constexpr int kItN = 0;        // rows in the item (-1: no more items)
@@ -77,10 +84,10 @@ struct PageParams {
   bf16* gated;    // [R, H dv]: fused norm + gate output (nullptr: store fp32 O to a.out)
 };
 
-// Row stride (floats) of the staged O tile: 4 floats of padding keep the
-// per-lane float2 writes of eight different rows in different banks.
-__host__ __device__ constexpr int otile_ld(int hdv) { return hdv + 4; }
-__host__ __device__ constexpr int otile_bytes(int hdv) { return kHalfRows * otile_ld(hdv) * 4; }
+// Row stride (bf16) of the staged O tile: 8 values of padding keep the
+// per-lane 4-byte writes of eight different rows in different banks.
+__host__ __device__ constexpr int otile_ld(int hdv) { return hdv + 8; }
+__host__ __device__ constexpr int otile_bytes(int hdv) { return (kHalfRows * otile_ld(hdv) * 2 + 15) / 16 * 16; }
 
 __device__ __forceinline__ int bias_index(int kpos, int qpos, int max_pos) {
   int idx = kpos - qpos + (max_pos - 1);
@@ -319,29 +326,38 @@ __device__ __forceinline__ void extra_key(float& m, float& l, float (&o)[8][4], 
   }
 }
 
+// Bounded wait on one of the kernel's mbarriers; false (abort flag set, or
+// the wait ran out and recorded IMBA_ERR_TIMEOUT) tells the caller to leave.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int32_t* status, volatile int* abort) {
+  return tc::mbar_wait_or_abort(bar, parity, status, abort);
+}
+
 template <bool kSmemBias>
 __global__ void __launch_bounds__(kMaxThreads, 1)
     attn_page_kernel(const __grid_constant__ CUtensorMap kvmap, const PageParams prm) {
   const AttnArgs& a = prm.a;
   const imba_step_desc& st = a.st;
   const int HC = prm.hc, S = prm.stages;
+  const bool fused = prm.gated != nullptr;
   const int ncw = 2 * HC, nct = ncw * 32;  // consumer warps (head, row block) / threads
+  const int nepi = fused ? kEpiWarps : 0;  // norm / gate warps
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int H = a.g.H;
   constexpr int D = 64;
   const int hdv = H * D;
   const int h0 = blockIdx.z * HC;
   const int stage_bytes = 2 * HC * kPageBytes;
+  const int q_bytes = HC * kHalfRows * 128;  // one item's query tile
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = base;                                    // S stages: [K: HC x 2 KB][V: HC x 2 KB]
-  uint8_t* qtile = ring + S * stage_bytes;                 // [HC][32 rows][128 B] queries, 128-byte swizzle
+  uint8_t* qtile = ring + S * stage_bytes;                 // [2][HC][32 rows][128 B] queries, 128-byte swizzle
   const int bias_w = 2 * a.max_pos - 1;                    // ps_w row length
-  // Fused epilogue: the item's O [32 rows][H dv + 4] fp32, staged.
-  float* otile = reinterpret_cast<float*>(qtile + HC * kHalfRows * 128);
-  const int otile_size = prm.gated ? otile_bytes(hdv) : 0;
-  __half* bias_s = reinterpret_cast<__half*>(qtile + HC * kHalfRows * 128 + otile_size);  // [HC][bias_w] (kSmemBias)
+  // Fused epilogue: the item's O [32 rows][H dv + 8] bf16, staged for the norm warps.
+  bf16* otile = reinterpret_cast<bf16*>(qtile + 2 * q_bytes);
+  const int otile_size = fused ? otile_bytes(hdv) : 0;
+  __half* bias_s = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(otile) + otile_size);  // [HC][bias_w]
   const int bias_bytes = kSmemBias ? (HC * bias_w * 2 + 15) / 16 * 16 : 0;
   int* items = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bias_s) + bias_bytes);  // [2][kItemInts]
   int* misc = items + 2 * kItemInts;                       // [0] abort flag, [1] pad
@@ -349,6 +365,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
   uint64_t* empty = full + kMaxStages;
   uint64_t* item_full = empty + kMaxStages;
   uint64_t* item_empty = item_full + 2;
+  uint64_t* q_full = item_empty + 2;
+  uint64_t* o_full = q_full + 2;
+  uint64_t* o_empty = o_full + 1;
   volatile int* abort_flag = misc;
 
   if (tid == 0) {
@@ -358,8 +377,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&item_full[b], 1);
-      tc::mbar_init(&item_empty[b], ncw);
+      tc::mbar_init(&item_empty[b], ncw + nepi);  // consumers and norm warps release an item buffer
+      tc::mbar_init(&q_full[b], 32);              // one cp.async-tracked arrival per producer lane
     }
+    tc::mbar_init(o_full, ncw);
+    tc::mbar_init(o_empty, nepi > 0 ? nepi : 1);
     misc[0] = 0;
     tc::fence_mbar_init();
   }
@@ -368,11 +390,13 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
   if (warp == ncw) {
     // ---------------- producer ----------------
     const int64_t num_pages = a.g.num_slots / IMBA_PAGE_TOKENS;
+    const bf16* Q = static_cast<const bf16*>(a.q);
     int* ctr = a.counters + blockIdx.z;
     int next_c = 0;
     if (lane == 0) next_c = atomicAdd(ctr, 1);
     int c = 0, half = 0, nhalves = 0, off0 = 0, n_chunk = 0, pg0 = 0, cap = 0;
     int it = 0, pc = 0;
+    bool waited = false;  // griddepcontrol.wait done (queries and pages may come from the previous kernel)
     while (true) {
       if (++half >= nhalves) {  // claim the next non-empty chunk
         half = 0;
@@ -410,9 +434,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       }
       const int ib = it & 1;
       int* item = items + ib * kItemInts;
-      if (it >= 2) {  // the consumers release a buffer after the item's epilogue
+      if (it >= 2) {  // consumers and norm warps release a buffer (item metadata and queries)
         int ok = 1;
-        if (lane == 0) ok = tc::mbar_wait_or_abort(&item_empty[ib], ((it >> 1) - 1) & 1, st.status, abort_flag);
+        if (lane == 0) ok = wait_bar(&item_empty[ib], ((it >> 1) - 1) & 1, st.status, abort_flag);
         if (!__shfl_sync(0xffffffffu, ok, 0)) return;
       }
       if (c >= st.num_chunks) {
@@ -420,6 +444,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
           item[kItN] = -1;
           tc::mbar_arrive(&item_full[ib]);
         }
+        asm volatile("cp.async.wait_all;\n" ::: "memory");
         return;
       }
       // Rows of this item, one lane per row.
@@ -474,8 +499,30 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       }
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&item_full[ib]);
-      // The pages may hold KV written by the preceding projection kernel.
-      pdl_wait();
+      // Queries and pages may have been written by the preceding kernels.
+      if (!waited) {
+        pdl_wait();
+        waited = true;
+      }
+      // This item's query tile: lane = row; rows past n are zero.  The tile's
+      // arrival is tracked on q_full[ib] (one arrival per lane once its copies land).
+      {
+        const uint32_t qt = tc::smem_u32(qtile) + ib * q_bytes;
+        for (int hh = 0; hh < HC; ++hh) {
+          const uint32_t dst = qt + hh * (kHalfRows * 128);
+#pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8) {
+            const uint32_t d8 = dst + blk_off(lane, c8);
+            // rows past n are zero-filled by the copy itself (source size 0)
+            const bf16* src = Q + (lane < n ? (size_t)r * (H * D) + (h0 + hh) * D + 8 * c8 : 0);
+            const uint32_t nbytes = lane < n ? 16u : 0u;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d8), "l"(src), "r"(nbytes)
+                         : "memory");
+          }
+        }
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(tc::smem_u32(&q_full[ib]))
+                     : "memory");
+      }
       // Stream the visible pages through the ring.
       for (int b0 = 0; b0 < npg; b0 += 32) {
         int pg = 0;
@@ -492,7 +539,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
           int ok = 1;
           if (lane == 0) {
             const int s = pc % S;
-            if (pc >= S) ok = tc::mbar_wait_or_abort(&empty[s], ((pc / S) - 1) & 1, st.status, abort_flag);
+            if (pc >= S) ok = wait_bar(&empty[s], ((pc / S) - 1) & 1, st.status, abort_flag);
             if (ok) {
               uint8_t* dst = ring + s * stage_bytes;
               const int rowK = ((page * prm.num_layers + a.layer) * 2 * H + h0) * IMBA_PAGE_TOKENS;
@@ -502,11 +549,97 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
               tc::tma_load_2d(dst + HC * kPageBytes, &kvmap, &full[s], 0, rowV);
             }
           }
-          if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+          if (!__shfl_sync(0xffffffffu, ok, 0)) {
+            asm volatile("cp.async.wait_all;\n" ::: "memory");
+            return;
+          }
           ++pc;
         }
       }
       ++it;
+    }
+  }
+
+  if (warp > ncw) {
+    // ---------------- norm / gate warps (fused epilogue) ----------------
+    // LayerNorm over each row's H dv attention outputs (no affine, eps 1e-6)
+    // times u, stored in bf16 for the output projection; lane l owns columns
+    // 128 k + 4 l .. +3 (k < 4) of a row; warp e takes rows e, e + nepi, ...
+    const int ew = warp - ncw - 1;
+    const int ld = otile_ld(hdv);
+    auto col_ok = [&](int k) { return 128 * k + 4 * lane < hdv; };
+    pdl_wait();  // u comes from the preceding projection kernel
+    for (int it = 0;; ++it) {
+      const int ib = it & 1;
+      const int* item = items + ib * kItemInts;
+      if (!wait_bar(&item_full[ib], (it >> 1) & 1, st.status, abort_flag)) return;
+      const int n = item[kItN];
+      if (n < 0) return;
+      // u of this warp's first row, loaded before O is ready
+      uint2 un[4];
+      {
+        const int gr = ew < n ? item[kItRows + ew] : -1;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          un[k] = (gr >= 0 && col_ok(k)) ? __ldg(reinterpret_cast<const uint2*>(prm.u + (size_t)gr * hdv + 128 * k +
+                                                                                   4 * lane))
+                                         : make_uint2(0u, 0u);
+      }
+      if (!wait_bar(o_full, it & 1, st.status, abort_flag)) return;
+      for (int rr = ew; rr < n; rr += nepi) {
+        const int gr = item[kItRows + rr];
+        uint2 ur[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) ur[k] = un[k];
+        const int rn = rr + nepi;  // next row of this warp: its u load overlaps this row
+        const int grn = rn < n ? item[kItRows + rn] : -1;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          un[k] = (grn >= 0 && col_ok(k)) ? __ldg(reinterpret_cast<const uint2*>(prm.u + (size_t)grn * hdv +
+                                                                                    128 * k + 4 * lane))
+                                          : make_uint2(0u, 0u);
+        float v[4][4];
+        float sum = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (col_ok(k)) {
+            const uint2 w = *reinterpret_cast<const uint2*>(otile + rr * ld + 128 * k + 4 * lane);
+            const float2 a01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
+            const float2 a23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+            v[k][0] = a01.x;
+            v[k][1] = a01.y;
+            v[k][2] = a23.x;
+            v[k][3] = a23.y;
+          } else {
+            v[k][0] = v[k][1] = v[k][2] = v[k][3] = 0.f;
+          }
+          sum += (v[k][0] + v[k][1]) + (v[k][2] + v[k][3]);
+        }
+        const float mu = warp_sum(sum) / (float)hdv;
+        float sq = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (col_ok(k))
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sq += (v[k][e] - mu) * (v[k][e] - mu);
+        }
+        const float rsd = 1.0f / sqrtf(warp_sum(sq) / (float)hdv + 1e-6f);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (!col_ok(k)) continue;
+          const float2 u01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ur[k].x));
+          const float2 u23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ur[k].y));
+          uint2 o;
+          o.x = pack_bf16(u01.x * ((v[k][0] - mu) * rsd), u01.y * ((v[k][1] - mu) * rsd));
+          o.y = pack_bf16(u23.x * ((v[k][2] - mu) * rsd), u23.y * ((v[k][3] - mu) * rsd));
+          *reinterpret_cast<uint2*>(prm.gated + (size_t)gr * hdv + 128 * k + 4 * lane) = o;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        tc::mbar_arrive(o_empty);          // the O tile may be overwritten
+        tc::mbar_arrive(&item_empty[ib]);  // done with the item's metadata
+      }
     }
   }
 
@@ -527,11 +660,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       for (int k = 0; k < 8; ++k)
         if (base + k < total) bias_s[base + k] = __float2half_rn(v[k] * kLog2e);
     }
-    // visible to every consumer warp after the first item's barrier
+    bar_consumers(nct);  // the table is complete before any warp reads it
   }
   // The bias table (weights) and the producer's first item (host-written step
-  // metadata) overlap the previous kernel; queries, u, the rows' own K / V
-  // and the outputs are ordered after it.
+  // metadata) overlap the previous kernel; the rows' own K / V and the
+  // outputs are ordered after it.
   pdl_wait();
   pdl_trigger();
   using Bias = typename std::conditional<kSmemBias, BiasShared, BiasGlobal>::type;
@@ -539,16 +672,13 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
   if constexpr (kSmemBias) psw.p = bias_s + (size_t)hl * bias_w;
   else psw.p = a.ps_w + (size_t)h * bias_w;
   const bf16* Pool = static_cast<const bf16*>(a.pool);
-  const bf16* Q = static_cast<const bf16*>(a.q);
   const uint32_t ring_base = tc::smem_u32(ring), qtb = tc::smem_u32(qtile);
-  const uint32_t qb = qtb + hl * (kHalfRows * 128) + rb * (16 * 128);  // this warp's 16 query rows
 
   int pc = 0;
   for (int it = 0;; ++it) {
     const int ib = it & 1;
     const int* item = items + ib * kItemInts;
-    const bool ok_item =
-        __all_sync(0xffffffffu, tc::mbar_wait_or_abort(&item_full[ib], (it >> 1) & 1, st.status, abort_flag));
+    const bool ok_item = __all_sync(0xffffffffu, wait_bar(&item_full[ib], (it >> 1) & 1, st.status, abort_flag));
     if (bar_consumers_or(nct, !ok_item)) {
       *abort_flag = 1;
       return;
@@ -556,19 +686,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     const int n = item[kItN];
     if (n < 0) return;
     const int npg = item[kItNpg];
-    // Query tile of the item: row r, head hh, 16-byte chunk c8 (rows past n are zero).
-    for (int idx = tid; idx < kHalfRows * HC * 8; idx += nct) {
-      const int c8 = idx & 7, rest = idx >> 3;
-      const int hh = rest % HC, row = rest / HC;
-      const uint32_t dst = qtb + hh * (kHalfRows * 128) + blk_off(row, c8);
-      if (row < n) {
-        const bf16* src = Q + (size_t)item[kItRows + row] * (H * D) + (h0 + hh) * D + 8 * c8;
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
-      } else {
-        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};\n" ::"r"(dst), "r"(0u) : "memory");
-      }
-    }
-    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    const uint32_t qb = qtb + ib * q_bytes + hl * (kHalfRows * 128) + rb * (16 * 128);  // this warp's 16 rows
     // Bring the K / V lines of each row's first extra key (usually the row
     // itself, written by the preceding projection) into L1 while the pages
     // stream: lane t of a quad takes (row rl0 | rl1) x (K | V).
@@ -598,18 +716,17 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     int wvis = max(vis0, vis1);  // pages past every row of this warp are skipped
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) wvis = max(wvis, __shfl_xor_sync(0xffffffffu, wvis, o));
-    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
-    bar_consumers(nct);  // the query tile is complete
+    // the item's query tile (copied by the producer)
+    bool aborted = !__all_sync(0xffffffffu, wait_bar(&q_full[ib], (it >> 1) & 1, st.status, abort_flag));
     RowState rs;
 #pragma unroll
     for (int j = 0; j < 8; ++j) rs.o[j][0] = rs.o[j][1] = rs.o[j][2] = rs.o[j][3] = 0.f;
     rs.m0 = rs.m1 = -INFINITY;
     rs.l0 = rs.l1 = 0.f;
 
-    bool aborted = false;
-    for (int p = 0; p < npg; ++p, ++pc) {
+    for (int p = 0; p < npg && !aborted; ++p, ++pc) {
       const int s = pc % S;
-      const bool ok = __all_sync(0xffffffffu, tc::mbar_wait_or_abort(&full[s], (pc / S) & 1, st.status, abort_flag));
+      const bool ok = __all_sync(0xffffffffu, wait_bar(&full[s], (pc / S) & 1, st.status, abort_flag));
       if (!ok) {
         aborted = true;
         break;
@@ -631,7 +748,6 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     // decision to stop is uniform and no warp waits at a later barrier.
     if (bar_consumers_or(nct, aborted)) {
       *abort_flag = 1;
-      asm volatile("cp.async.wait_all;\n" ::: "memory");
       return;  // the status word already holds the timeout
     }
     // Extra keys, per row: the suffix chain and the row itself.
@@ -686,8 +802,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       rs.o[j][2] *= i1;
       rs.o[j][3] *= i1;
     }
-    const int r0 = rl0 < n ? item[kItRows + rl0] : -1, r1 = rl1 < n ? item[kItRows + rl1] : -1;
-    if (prm.gated == nullptr) {
+    if (!fused) {
+      const int r0 = rl0 < n ? item[kItRows + rl0] : -1, r1 = rl1 < n ? item[kItRows + rl1] : -1;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int col = h * D + 8 * j + 2 * t;
@@ -695,72 +811,24 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         if (r1 >= 0) *reinterpret_cast<float2*>(a.out + (size_t)r1 * hdv + col) = make_float2(rs.o[j][2], rs.o[j][3]);
       }
     } else {
-      // LayerNorm over the row's H dv outputs, then the gate by u: O goes to
-      // the shared O tile, and after one barrier each warp normalises whole
-      // rows (2 of the 32) with warp reductions; u and the gated output move
-      // as coalesced 8-byte pieces.  The u loads are issued first.
-      // Lane l owns columns 128 k + 4 l .. +3 (k < 4) of a row; warp w
-      // normalises rows w, w + 2 HC, ... (two rows when HC = 8).
-      const int ld = otile_ld(hdv);
-      auto col_ok = [&](int k) { return 128 * k + 4 * lane < hdv; };
-      uint2 uw[2][4];  // u of this warp's first two rows, loaded before the barrier
+      // O (rounded to bf16, as the reference's bf16 attention output is) to the
+      // staged tile once the norm warps have read the previous item's.  A
+      // failed wait has set the abort flag: the warp skips the tile and
+      // leaves through the next item's uniform abort vote.
+      if (it == 0 || __all_sync(0xffffffffu, wait_bar(o_empty, (it - 1) & 1, st.status, abort_flag))) {
+        const int ld = otile_ld(hdv);
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int rr = warp + i * ncw;
-        const int gr = rr < n ? item[kItRows + rr] : -1;
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          uw[i][k] = (gr >= 0 && col_ok(k))
-                         ? __ldg(reinterpret_cast<const uint2*>(prm.u + (size_t)gr * hdv + 128 * k + 4 * lane))
-                         : make_uint2(0u, 0u);
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int col = hl * D + 8 * j + 2 * t;
-        *reinterpret_cast<float2*>(otile + rl0 * ld + col) = make_float2(rs.o[j][0], rs.o[j][1]);
-        *reinterpret_cast<float2*>(otile + rl1 * ld + col) = make_float2(rs.o[j][2], rs.o[j][3]);
-      }
-      bar_consumers(nct);
-      for (int i = 0, rr = warp; rr < n; ++i, rr += ncw) {
-        const int gr = item[kItRows + rr];
-        uint2 ur[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          ur[k] = i < 2 ? (i ? uw[1][k] : uw[0][k])
-                        : (col_ok(k) ? __ldg(reinterpret_cast<const uint2*>(prm.u + (size_t)gr * hdv + 128 * k +
-                                                                            4 * lane))
-                                     : make_uint2(0u, 0u));
-        float4 v[4];
-        float sum = 0.f;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          v[k] = col_ok(k) ? *reinterpret_cast<const float4*>(otile + rr * ld + 128 * k + 4 * lane)
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
-          sum += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+        for (int j = 0; j < 8; ++j) {
+          const int col = hl * D + 8 * j + 2 * t;
+          *reinterpret_cast<uint32_t*>(otile + rl0 * ld + col) = pack_bf16(rs.o[j][0], rs.o[j][1]);
+          *reinterpret_cast<uint32_t*>(otile + rl1 * ld + col) = pack_bf16(rs.o[j][2], rs.o[j][3]);
         }
-        const float mu = warp_sum(sum) / (float)hdv;
-        float sq = 0.f;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          if (col_ok(k))
-            sq += (v[k].x - mu) * (v[k].x - mu) + (v[k].y - mu) * (v[k].y - mu) + (v[k].z - mu) * (v[k].z - mu) +
-                  (v[k].w - mu) * (v[k].w - mu);
-        }
-        const float rsd = 1.0f / sqrtf(warp_sum(sq) / (float)hdv + 1e-6f);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          if (!col_ok(k)) continue;
-          const float2 u01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ur[k].x));
-          const float2 u23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ur[k].y));
-          uint2 o;
-          o.x = pack_bf16(u01.x * ((v[k].x - mu) * rsd), u01.y * ((v[k].y - mu) * rsd));
-          o.y = pack_bf16(u23.x * ((v[k].z - mu) * rsd), u23.y * ((v[k].w - mu) * rsd));
-          *reinterpret_cast<uint2*>(prm.gated + (size_t)gr * hdv + 128 * k + 4 * lane) = o;
-        }
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(o_full);
       }
     }
     __syncwarp();
-    if (lane == 0) tc::mbar_arrive(&item_empty[ib]);  // this warp is done with the item buffer
+    if (lane == 0) tc::mbar_arrive(&item_empty[ib]);  // this warp is done with the item buffer and queries
   }
 }
 
@@ -820,7 +888,7 @@ bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& 
   // table, item buffers and barriers.  The bias table is
   // kept in shared memory when at least 3 ring stages still fit.
   const size_t stage_bytes = 2 * (size_t)hc * kPageBytes;
-  const size_t fixed = 1024 + (size_t)hc * kHalfRows * 128 + (fuse ? (size_t)otile_bytes(H * 64) : 0) + kMetaBytes;
+  const size_t fixed = 1024 + 2 * (size_t)hc * kHalfRows * 128 + (fuse ? (size_t)otile_bytes(H * 64) : 0) + kMetaBytes;
   const size_t bias_bytes = ((size_t)hc * (2 * md.max_pos - 1) * 2 + 15) / 16 * 16;
   const bool smem_bias = fixed + bias_bytes + 3 * stage_bytes <= kSmemMax;
   size_t stages = (kSmemMax - fixed - (smem_bias ? bias_bytes : 0)) / stage_bytes;
@@ -839,7 +907,7 @@ bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& 
   PageParams prm{a, num_layers, hc, (int)stages, u, fuse ? gated : nullptr};
   const int ctas = a.st.num_chunks < sms ? a.st.num_chunks : sms;
   dim3 grid(ctas, 1, H / hc);
-  *err = launch_pdl(kern, grid, dim3((2 * hc + 1) * 32), smem, s, map, prm);
+  *err = launch_pdl(kern, grid, dim3((2 * hc + 1 + (fuse ? kEpiWarps : 0)) * 32), smem, s, map, prm);
   *fused = fuse && *err == cudaSuccess;
   return true;
 }
