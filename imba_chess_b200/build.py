@@ -100,7 +100,7 @@ def _build_ext(src: str, ext: str, force: bool) -> str:
     cxx = os.environ.get("CXX") or shutil.which("g++") or "g++"
     inc = sysconfig.get_paths()["include"]
     tmp = ext + ".tmp"
-    cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden", "-I", inc, src, "-o", tmp]
+    cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden", "-pthread", "-I", inc, src, "-o", tmp]
     proc = subprocess.run(cmd, capture_output=True, text=True)
     if proc.returncode != 0:
         raise RuntimeError(f"host extension build failed ({src}):\n{proc.stdout}\n{proc.stderr}")

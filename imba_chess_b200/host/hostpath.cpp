@@ -14,16 +14,28 @@
 //   R*64 bytes, out_side: writable int32 buffer [R, 7] (column 0 is left to
 //   the caller).  legal_off is int32 [R+1], legal_ids int32, node / parent
 //   ids int64 (parent INT64_MIN for None).  Raises ValueError for piece ids outside
-//   0..12 or boards without 64 squares, TypeError for non-integers.
+//   0..12 or boards without 64 squares, TypeError for non-integers.  The
+//   attributes are read on the calling thread; the elements of the integer
+//   lists (64 piece ids and the legal ids of every row) are converted by a
+//   few worker threads that only read the int objects' memory, while the
+//   calling thread holds the GIL and waits for them.
+//
+// wave_chains(dicts, counts, parent_ids) -> (depths, chain rows) and
+// record_chains(dicts, counts, node_ids, parent_ids, own_start): the turn
+// node-chain bookkeeping of a wave (see the functions below).
 //
 // wave_responses(counts, values, legal, offsets) -> list of row lists
 //   counts: rows per request; values: float32 [R]; legal: float32 [NL];
-//   offsets: int32 [R+1].  Returns, per request, [(value, [legal...]), ...].
+//   offsets: int32 [R+1].  Returns, per request, [(value, [legal...]), ...];
+//   the rows are not tracked by the cyclic garbage collector (they hold
+//   only floats).
 #define PY_SSIZE_T_CLEAN
 #include <Python.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstring>
+#include <thread>
 #include <vector>
 
 namespace {
@@ -105,27 +117,85 @@ struct Buf {
   }
 };
 
+// An exact int that fits one digit, read without any API call (safe from
+// worker threads while the calling thread holds the GIL and waits).
+inline bool compact_int(PyObject* o, long long* out) {
+#if PY_VERSION_HEX >= 0x030C0000
+  if (PyLong_CheckExact(o) && PyUnstable_Long_IsCompact(reinterpret_cast<PyLongObject*>(o))) {
+    *out = (long long)PyUnstable_Long_CompactValue(reinterpret_cast<PyLongObject*>(o));
+    return true;
+  }
+#endif
+  (void)o;
+  (void)out;
+  return false;
+}
+
+inline int32_t clamp32(long long v) {
+  return v > INT32_MAX ? INT32_MAX : (v < INT32_MIN ? INT32_MIN : (int32_t)v);
+}
+
+// Piece ids and legal ids of one row, from the borrowed item arrays of its
+// lists; false when an element needs the general conversion (or is out of
+// range), which the calling thread then redoes with the Python API.
+bool convert_row_fast(PyObject* const* pieces, PyObject* const* legal, Py_ssize_t nlegal, uint8_t* prow,
+                      int32_t* lrow) {
+  for (int k = 0; k < 64; ++k) {
+    long long v;
+    if (!compact_int(pieces[k], &v) || v < 0 || v > 12) return false;
+    prow[k] = (uint8_t)v;
+  }
+  for (Py_ssize_t k = 0; k < nlegal; ++k) {
+    long long v;
+    if (!compact_int(legal[k], &v)) return false;
+    lrow[k] = clamp32(v);
+  }
+  return true;
+}
+
+// The same with the general conversions and the error messages.
+bool convert_row_slow(PyObject* const* pieces, PyObject* const* legal, Py_ssize_t nlegal, uint8_t* prow,
+                      int32_t* lrow) {
+  for (int k = 0; k < 64; ++k) {
+    long long v;
+    if (!as_long(pieces[k], &v)) return false;
+    if (v < 0 || v > 12) {
+      PyErr_SetString(PyExc_ValueError, "piece_ids values must be in [0, 12]");
+      return false;
+    }
+    prow[k] = (uint8_t)v;
+  }
+  for (Py_ssize_t k = 0; k < nlegal; ++k) {
+    long long v;
+    if (!as_long(legal[k], &v)) return false;
+    lrow[k] = clamp32(v);
+  }
+  return true;
+}
+
 PyObject* pack_wave_rows(PyObject*, PyObject* args) {
   PyObject *requests, *out_piece, *out_side;
   if (!PyArg_ParseTuple(args, "OOO", &requests, &out_piece, &out_side)) return nullptr;
   Ref reqs(PySequence_Fast(requests, "requests must be a sequence"));
   if (!reqs) return nullptr;
   const Py_ssize_t G = PySequence_Fast_GET_SIZE(reqs.get());
-  // Rows of every request (kept alive while packing).
-  std::vector<PyObject*> row_lists;
-  row_lists.reserve(G);
+  // Every sequence object read below is kept alive until the end.
+  std::vector<PyObject*> keep;
   struct Cleanup {
     std::vector<PyObject*>& v;
     ~Cleanup() {
       for (PyObject* o : v) Py_XDECREF(o);
     }
-  } cleanup{row_lists};
+  } cleanup{keep};
+  std::vector<PyObject*> row_lists;
+  row_lists.reserve(G);
   Py_ssize_t R = 0;
   for (Py_ssize_t g = 0; g < G; ++g) {
     Ref rows(PyObject_GetAttr(PySequence_Fast_GET_ITEM(reqs.get(), g), s_rows));
     if (!rows) return nullptr;
     PyObject* fast = PySequence_Fast(rows.get(), "rows must be a sequence");
     if (!fast) return nullptr;
+    keep.push_back(fast);
     row_lists.push_back(fast);
     R += PySequence_Fast_GET_SIZE(fast);
   }
@@ -141,10 +211,13 @@ PyObject* pack_wave_rows(PyObject*, PyObject* args) {
   uint8_t* pc = static_cast<uint8_t*>(piece.view.buf);
   int32_t* sd = static_cast<int32_t*>(side.view.buf);
   std::vector<int32_t> loff((size_t)R + 1, 0);
-  std::vector<int32_t> lids;
   std::vector<int64_t> node((size_t)R), parent((size_t)R);
-  lids.reserve((size_t)R * 40);
+  std::vector<PyObject* const*> pitems((size_t)R), litems((size_t)R);
+  keep.reserve(keep.size() + 2 * (size_t)R);
+  // Pass 1 (this thread): attributes, side fields, ids and the item arrays
+  // of every row's two integer lists.
   Py_ssize_t r = 0;
+  long long total_legal = 0;
   for (PyObject* rows : row_lists) {
     const Py_ssize_t n = PySequence_Fast_GET_SIZE(rows);
     for (Py_ssize_t i = 0; i < n; ++i, ++r) {
@@ -169,52 +242,69 @@ PyObject* pack_wave_rows(PyObject*, PyObject* args) {
       {
         Ref o(PyObject_GetAttr(row, s_prev_move));
         if (!o || !as_long(o.get(), &v)) return nullptr;
-        srow[6] = v > INT32_MAX ? INT32_MAX : (v < INT32_MIN ? INT32_MIN : (int32_t)v);
+        srow[6] = clamp32(v);
       }
       Ref bs(PyObject_GetAttr(row, s_board_state));
       if (!bs) return nullptr;
       for (int f = 0; f < 5; ++f) {
         Ref o(get_item(bs.get(), s_fields[f]));
         if (!o || !as_long(o.get(), &v)) return nullptr;
-        srow[1 + f] = v > INT32_MAX ? INT32_MAX : (v < INT32_MIN ? INT32_MIN : (int32_t)v);
+        srow[1 + f] = clamp32(v);
       }
       {
         Ref pl(get_item(bs.get(), s_piece_ids));
         if (!pl) return nullptr;
-        Ref fast(PySequence_Fast(pl.get(), "piece_ids must be a sequence"));
+        PyObject* fast = PySequence_Fast(pl.get(), "piece_ids must be a sequence");
         if (!fast) return nullptr;
-        if (PySequence_Fast_GET_SIZE(fast.get()) != 64) {
+        keep.push_back(fast);
+        if (PySequence_Fast_GET_SIZE(fast) != 64) {
           PyErr_SetString(PyExc_ValueError, "every board_state must carry 64 piece_ids");
           return nullptr;
         }
-        uint8_t* prow = pc + (size_t)r * 64;
-        for (int k = 0; k < 64; ++k) {
-          if (!as_long(PySequence_Fast_GET_ITEM(fast.get(), k), &v)) return nullptr;
-          if (v < 0 || v > 12) {
-            PyErr_SetString(PyExc_ValueError, "piece_ids values must be in [0, 12]");
-            return nullptr;
-          }
-          prow[k] = (uint8_t)v;
-        }
+        pitems[r] = PySequence_Fast_ITEMS(fast);
       }
       {
         Ref ll(PyObject_GetAttr(row, s_legal));
         if (!ll) return nullptr;
-        Ref fast(PySequence_Fast(ll.get(), "legal_vocab_ids must be a sequence"));
+        PyObject* fast = PySequence_Fast(ll.get(), "legal_vocab_ids must be a sequence");
         if (!fast) return nullptr;
-        const Py_ssize_t m = PySequence_Fast_GET_SIZE(fast.get());
-        for (Py_ssize_t k = 0; k < m; ++k) {
-          if (!as_long(PySequence_Fast_GET_ITEM(fast.get(), k), &v)) return nullptr;
-          lids.push_back(v > INT32_MAX ? INT32_MAX : (v < INT32_MIN ? INT32_MIN : (int32_t)v));
-        }
-        if ((long long)lids.size() > INT32_MAX) {
+        keep.push_back(fast);
+        total_legal += PySequence_Fast_GET_SIZE(fast);
+        if (total_legal > INT32_MAX) {
           PyErr_SetString(PyExc_ValueError, "too many legal ids in one wave");
           return nullptr;
         }
-        loff[r + 1] = (int32_t)lids.size();
+        litems[r] = PySequence_Fast_ITEMS(fast);
+        loff[r + 1] = (int32_t)total_legal;
       }
     }
   }
+  // Pass 2 (worker threads, no Python API): the integer lists' elements.
+  std::vector<int32_t> lids((size_t)total_legal);
+  std::vector<uint8_t> slow((size_t)R, 0);
+  auto work = [&](Py_ssize_t lo, Py_ssize_t hi) {
+    for (Py_ssize_t q = lo; q < hi; ++q)
+      if (!convert_row_fast(pitems[q], litems[q], loff[q + 1] - loff[q], pc + (size_t)q * 64, lids.data() + loff[q]))
+        slow[q] = 1;
+  };
+  const unsigned hw = std::thread::hardware_concurrency();
+  const Py_ssize_t nthreads = std::min<Py_ssize_t>(std::max<Py_ssize_t>(1, R / 512), hw > 1 ? (Py_ssize_t)hw : 1);
+  const Py_ssize_t T = std::min<Py_ssize_t>(nthreads, 8);
+  if (T <= 1) {
+    work(0, R);
+  } else {
+    std::vector<std::thread> pool;
+    pool.reserve((size_t)T - 1);
+    const Py_ssize_t per = (R + T - 1) / T;
+    for (Py_ssize_t t = 1; t < T; ++t) pool.emplace_back(work, t * per, std::min(R, (t + 1) * per));
+    work(0, std::min(R, per));
+    for (auto& th : pool) th.join();
+  }
+  // Pass 3 (this thread): rows with other integer types, or errors.
+  for (Py_ssize_t q = 0; q < R; ++q)
+    if (slow[q] &&
+        !convert_row_slow(pitems[q], litems[q], loff[q + 1] - loff[q], pc + (size_t)q * 64, lids.data() + loff[q]))
+      return nullptr;
   return Py_BuildValue("(ny#y#y#y#)", R, reinterpret_cast<const char*>(loff.data()),
                        (Py_ssize_t)(loff.size() * 4), reinterpret_cast<const char*>(lids.data()),
                        (Py_ssize_t)(lids.size() * 4), reinterpret_cast<const char*>(node.data()),
@@ -287,15 +377,184 @@ PyObject* wave_responses(PyObject*, PyObject* args) {
       Py_DECREF(v);
       Py_DECREF(ll);
       if (!tup) return nullptr;
+      // A row is a float and a list of floats: it can never be part of a
+      // reference cycle, so it stays out of the cyclic collector's lists
+      // (whose next pass would otherwise scan every row of the wave).
+      PyObject_GC_UnTrack(ll);
+      PyObject_GC_UnTrack(tup);
       PyList_SET_ITEM(lst, i, tup);
     }
   }
   return Py_NewRef(out.get());
 }
 
+// Reads an int64 buffer argument.
+bool int64_view(PyObject* o, Buf* b, const int64_t** data, Py_ssize_t* n) {
+  if (PyObject_GetBuffer(o, &b->view, PyBUF_C_CONTIGUOUS) != 0) return false;
+  b->ok = true;
+  if (b->view.len % 8) {
+    PyErr_SetString(PyExc_ValueError, "expected an int64 buffer");
+    return false;
+  }
+  *data = static_cast<const int64_t*>(b->view.buf);
+  *n = b->view.len / 8;
+  return true;
+}
+
+// Per-request row counts as a vector (and their sum).
+bool read_counts(PyObject* counts, std::vector<Py_ssize_t>* out, Py_ssize_t* total) {
+  Ref cf(PySequence_Fast(counts, "counts must be a sequence"));
+  if (!cf) return false;
+  const Py_ssize_t G = PySequence_Fast_GET_SIZE(cf.get());
+  out->resize(G);
+  *total = 0;
+  for (Py_ssize_t g = 0; g < G; ++g) {
+    long long n;
+    if (!as_long(PySequence_Fast_GET_ITEM(cf.get(), g), &n)) return false;
+    if (n < 0) {
+      PyErr_SetString(PyExc_ValueError, "negative row count");
+      return false;
+    }
+    (*out)[g] = (Py_ssize_t)n;
+    *total += (Py_ssize_t)n;
+  }
+  return true;
+}
+
+// The parent chain (arena rows, root -> parent) of one row: a borrowed list
+// from the turn's node_chains, or nullptr for a child of the root.  KeyError
+// for a parent the turn does not know (actor_server.py:839-850 indexes
+// node_chains[parent_id] the same way).
+bool parent_chain(PyObject* dict, int64_t parent, PyObject** chain) {
+  *chain = nullptr;
+  if (parent == INT64_MIN) return true;
+  Ref key(PyLong_FromLongLong(parent));
+  if (!key) return false;
+  PyObject* c = PyDict_GetItemWithError(dict, key.get());
+  if (!c) {
+    if (!PyErr_Occurred()) PyErr_SetObject(PyExc_KeyError, key.get());
+    return false;
+  }
+  if (!PyList_Check(c)) {
+    PyErr_SetString(PyExc_TypeError, "node chains must be lists of arena rows");
+    return false;
+  }
+  *chain = c;
+  return true;
+}
+
+// wave_chains(dicts, counts, parent_ids) -> (depths bytes, chain rows bytes)
+//   dicts: per request, its turn's node_chains (node id -> list of arena
+//   rows); counts: rows per request; parent_ids: int64 per row (INT64_MIN:
+//   a child of the root).  depths: int64 per row (the parent chain's
+//   length); chain rows: int64, every row's parent chain, concatenated.
+PyObject* wave_chains(PyObject*, PyObject* args) {
+  PyObject *dicts, *counts, *parents;
+  if (!PyArg_ParseTuple(args, "OOO", &dicts, &counts, &parents)) return nullptr;
+  Ref df(PySequence_Fast(dicts, "dicts must be a sequence"));
+  if (!df) return nullptr;
+  std::vector<Py_ssize_t> cnt;
+  Py_ssize_t R = 0;
+  if (!read_counts(counts, &cnt, &R)) return nullptr;
+  Buf pb;
+  const int64_t* par;
+  Py_ssize_t np_;
+  if (!int64_view(parents, &pb, &par, &np_)) return nullptr;
+  if (np_ != R || PySequence_Fast_GET_SIZE(df.get()) != (Py_ssize_t)cnt.size()) {
+    PyErr_SetString(PyExc_ValueError, "counts, dicts and parent ids disagree");
+    return nullptr;
+  }
+  std::vector<int64_t> depth((size_t)R), flat;
+  flat.reserve((size_t)R * 2);
+  Py_ssize_t r = 0;
+  for (size_t g = 0; g < cnt.size(); ++g) {
+    PyObject* d = PySequence_Fast_GET_ITEM(df.get(), (Py_ssize_t)g);
+    if (!PyDict_Check(d)) {
+      PyErr_SetString(PyExc_TypeError, "node chains must be dicts");
+      return nullptr;
+    }
+    for (Py_ssize_t i = 0; i < cnt[g]; ++i, ++r) {
+      PyObject* c;
+      if (!parent_chain(d, par[r], &c)) return nullptr;
+      const Py_ssize_t n = c ? PyList_GET_SIZE(c) : 0;
+      depth[r] = n;
+      for (Py_ssize_t k = 0; k < n; ++k) {
+        long long v;
+        if (!as_long(PyList_GET_ITEM(c, k), &v)) return nullptr;
+        flat.push_back(v);
+      }
+    }
+  }
+  return Py_BuildValue("(y#y#)", reinterpret_cast<const char*>(depth.data()), (Py_ssize_t)(depth.size() * 8),
+                       reinterpret_cast<const char*>(flat.data()), (Py_ssize_t)(flat.size() * 8));
+}
+
+// record_chains(dicts, counts, node_ids, parent_ids, own_start)
+//   After a wave: node_chains[node] = node_chains[parent] + [own row] for
+//   every row, own row = own_start[request] + its index within the request
+//   (actor_server.py:904-914; the rows the wave minted, in wave order).
+PyObject* record_chains(PyObject*, PyObject* args) {
+  PyObject *dicts, *counts, *nodes, *parents, *starts;
+  if (!PyArg_ParseTuple(args, "OOOOO", &dicts, &counts, &nodes, &parents, &starts)) return nullptr;
+  Ref df(PySequence_Fast(dicts, "dicts must be a sequence"));
+  if (!df) return nullptr;
+  std::vector<Py_ssize_t> cnt;
+  Py_ssize_t R = 0;
+  if (!read_counts(counts, &cnt, &R)) return nullptr;
+  Buf nb, pb, sb;
+  const int64_t *nod, *par, *st;
+  Py_ssize_t nn, np_, ns;
+  if (!int64_view(nodes, &nb, &nod, &nn) || !int64_view(parents, &pb, &par, &np_) ||
+      !int64_view(starts, &sb, &st, &ns))
+    return nullptr;
+  if (nn != R || np_ != R || ns != (Py_ssize_t)cnt.size() ||
+      PySequence_Fast_GET_SIZE(df.get()) != (Py_ssize_t)cnt.size()) {
+    PyErr_SetString(PyExc_ValueError, "counts, dicts, node / parent ids and starts disagree");
+    return nullptr;
+  }
+  Py_ssize_t r = 0;
+  for (size_t g = 0; g < cnt.size(); ++g) {
+    PyObject* d = PySequence_Fast_GET_ITEM(df.get(), (Py_ssize_t)g);
+    if (!PyDict_Check(d)) {
+      PyErr_SetString(PyExc_TypeError, "node chains must be dicts");
+      return nullptr;
+    }
+    // Parents first: a row whose parent is recorded by this same wave sees
+    // the chain the parent had before the wave, as the reference does.
+    std::vector<PyObject*> chains((size_t)cnt[g]);
+    for (Py_ssize_t i = 0; i < cnt[g]; ++i) {
+      if (!parent_chain(d, par[r + i], &chains[(size_t)i])) return nullptr;
+    }
+    std::vector<Ref> fresh((size_t)cnt[g]);
+    for (Py_ssize_t i = 0; i < cnt[g]; ++i) {
+      PyObject* c = chains[(size_t)i];
+      const Py_ssize_t n = c ? PyList_GET_SIZE(c) : 0;
+      PyObject* lst = PyList_New(n + 1);
+      if (!lst) return nullptr;
+      fresh[(size_t)i].p = lst;
+      for (Py_ssize_t k = 0; k < n; ++k) {
+        PyObject* v = PyList_GET_ITEM(c, k);
+        Py_INCREF(v);
+        PyList_SET_ITEM(lst, k, v);
+      }
+      PyObject* own = PyLong_FromLongLong(st[g] + i);
+      if (!own) return nullptr;
+      PyList_SET_ITEM(lst, n, own);
+      PyObject_GC_UnTrack(lst);  // a list of ints: no cycles, nothing for the collector to scan
+    }
+    for (Py_ssize_t i = 0; i < cnt[g]; ++i, ++r) {
+      Ref key(PyLong_FromLongLong(nod[r]));
+      if (!key || PyDict_SetItem(d, key.get(), fresh[(size_t)i].get()) != 0) return nullptr;
+    }
+  }
+  Py_RETURN_NONE;
+}
+
 PyMethodDef kMethods[] = {
     {"pack_wave_rows", pack_wave_rows, METH_VARARGS, "Pack the rows of wave requests into flat arrays."},
     {"wave_responses", wave_responses, METH_VARARGS, "Per-request response rows from a step's results."},
+    {"wave_chains", wave_chains, METH_VARARGS, "Depths and parent-chain arena rows of a wave's rows."},
+    {"record_chains", record_chains, METH_VARARGS, "Record the node chains of a wave's rows."},
     {nullptr, nullptr, 0, nullptr},
 };
 

@@ -142,10 +142,10 @@ class StepPlan:
         }
         return {k: np.ascontiguousarray(v, dtype=np.int32).reshape(-1) for k, v in out.items()}
 
-    def pack(self) -> tuple[np.ndarray, dict[str, tuple[int, int]]]:
-        """One int32 buffer: piece bytes (padded to 16 B), then each section
-        padded to a multiple of 4 elements.  Returns (buffer, {name: (offset
-        in int32 elements, length)})."""
+    def layout(self) -> tuple[int, dict[str, tuple[int, int]], dict[str, np.ndarray]]:
+        """(int32 words, {name: (offset in int32 elements, length)}, arrays)
+        of the packed buffer: piece bytes (padded to 16 B), then each section
+        padded to a multiple of 4 elements."""
         arrs = self.arrays()
         R = self.num_rows
         piece_words = -(-(R * 64) // 16) * 4
@@ -155,11 +155,24 @@ class StepPlan:
             n = int(arrs[name].shape[0])
             layout[name] = (off, n)
             off += -(-max(n, 1) // 4) * 4
-        buf = np.zeros(off, dtype=np.int32)
+        return off, layout, arrs
+
+    def pack_into(self, buf: np.ndarray, words: int, layout, arrs) -> None:
+        """Write the packed plan into ``buf`` (int32, at least ``words`` long)."""
+        R = self.num_rows
+        buf[:words] = 0
         buf.view(np.uint8)[: R * 64] = self.piece_ids.reshape(-1)
         for name in _SECTIONS:
             o, n = layout[name]
             buf[o : o + n] = arrs[name]
+
+    def pack(self) -> tuple[np.ndarray, dict[str, tuple[int, int]]]:
+        """One int32 buffer holding every integer input of the step (see
+        ``layout``).  Returns (buffer, {name: (offset in int32 elements,
+        length)})."""
+        words, layout, arrs = self.layout()
+        buf = np.zeros(words, dtype=np.int32)
+        self.pack_into(buf, words, layout, arrs)
         return buf, layout
 
     def counts(self) -> dict[str, int]:
@@ -172,6 +185,45 @@ class StepPlan:
             "num_extra": int(self.extra_slot.shape[0]),
             "num_group_pages": int(self.group_pages.shape[0]),
         }
+
+
+class StepBuffers:
+    """Pinned host and device buffers reused by consecutive steps on one
+    device: the packed plan (written on the host, copied once per step) and
+    the step's float32 results.  One step may be in flight at a time: the
+    caller synchronises before staging the next one."""
+
+    def __init__(self, device: torch.device) -> None:
+        self.device = device
+        self._host: torch.Tensor | None = None
+        self._dev: torch.Tensor | None = None
+        self._out_host: torch.Tensor | None = None
+        self._out_dev: torch.Tensor | None = None
+
+    @staticmethod
+    def _grow(n: int) -> int:
+        return max(1024, int(n * 1.25))
+
+    def stage(self, plan: "StepPlan", stream: torch.cuda.Stream | None = None) -> "DeviceStep":
+        """Pack ``plan`` into the pinned buffer and enqueue its copy to the
+        device on ``stream`` (default: the current stream)."""
+        words, layout, arrs = plan.layout()
+        if self._host is None or self._host.numel() < words:
+            self._host = torch.empty(self._grow(words), dtype=torch.int32, pin_memory=True)
+            self._dev = torch.empty(self._host.numel(), dtype=torch.int32, device=self.device)
+        plan.pack_into(self._host.numpy(), words, layout, arrs)
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        with torch.cuda.stream(s):
+            self._dev[:words].copy_(self._host[:words], non_blocking=True)
+        return DeviceStep.over(plan, self._dev, layout, words)
+
+    def outputs(self, n: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """(device float32 [n], pinned host float32 [n]) result buffers."""
+        if self._out_host is None or self._out_host.numel() < n:
+            size = self._grow(n)
+            self._out_host = torch.empty(size, dtype=torch.float32, pin_memory=True)
+            self._out_dev = torch.empty(size, dtype=torch.float32, device=self.device)
+        return self._out_dev[:n], self._out_host[:n]
 
 
 class DeviceStep:
@@ -198,6 +250,25 @@ class DeviceStep:
         if not self.has_legal:
             self.desc.legal_off = None
             self.desc.legal_ids = None
+
+    @classmethod
+    def over(cls, plan: "StepPlan", dev: torch.Tensor, layout, words: int) -> "DeviceStep":
+        """A step whose packed plan already sits at the start of ``dev``."""
+        self = cls.__new__(cls)
+        self.host = None
+        self.buf = dev[:words]
+        self.layout = layout
+        self.has_legal = plan.legal_off is not None
+        self.desc = _native.StepDesc()
+        for k, v in plan.counts().items():
+            setattr(self.desc, k, v)
+        base = dev.data_ptr()
+        for name, (off, _n) in layout.items():
+            setattr(self.desc, name, base + 4 * off)
+        if not self.has_legal:
+            self.desc.legal_off = None
+            self.desc.legal_ids = None
+        return self
 
     @property
     def h2d_bytes(self) -> int:

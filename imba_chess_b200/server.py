@@ -35,8 +35,8 @@ import torch
 from . import _hostpath, _native
 from .kvpool import PAGE, KVPool, KVSequence
 from .model import B200HSTUChessModel
-from .plan import DeviceStep, StepPlan
-from .steps import WaveGroup, root_plan, wave_plan
+from .plan import StepBuffers, StepPlan
+from .steps import root_plan, wave_plan_flat
 from .protocol import RootEvalResponse, WaveResponse, is_root_request, is_wave_request
 from .synth import EVENT_TOKEN_ID, TOKEN_FIELDS
 
@@ -91,6 +91,8 @@ class ActorInferenceServer:
         self._device = model.device
         self._dtype = dtype
         self.profile_sync = bool(profile_sync)
+        # waves of at least this many rows run as two overlapped steps
+        self.split_rows = 2048
         self.stats: dict[str, float] = {
             "root_build_s": 0.0, "root_gpu_s": 0.0, "root_post_s": 0.0,
             "wave_build_s": 0.0, "wave_gpu_s": 0.0, "wave_post_s": 0.0,
@@ -111,6 +113,10 @@ class ActorInferenceServer:
         self._turns: dict[tuple[int, int], _TurnState] = {}
         self._games: dict[int, _GameState] = {}
         self._status = torch.zeros(1, dtype=torch.int32, device=self._device)
+        # pinned / device step buffers reused by every call (two: a large wave
+        # runs as two steps in flight at once)
+        self._buffers = StepBuffers(self._device)
+        self._buffers2 = StepBuffers(self._device)
 
     def _page_bytes(self) -> int:
         d = self._model.dims
@@ -162,24 +168,39 @@ class ActorInferenceServer:
             old.release()
         self._turns[key] = _TurnState(seq=game.seq.retain(), prefix_len=game.prefix_len)
 
-    def _run_rows(self, plan: StepPlan, n_legal_rows: int):
-        """Run one step and bring back (value_stm [R], legal_logits flat)."""
+    def _launch(self, plan: StepPlan, buffers: StepBuffers):
+        """Enqueue one step (its packed plan copied in, its value and legal
+        logits and the status word copied out) on the current stream; returns
+        a handle for ``_collect``."""
         R = plan.num_rows
-        dstep = DeviceStep(plan, self._device, pinned=True)
         nl = 0 if plan.legal_ids is None else int(plan.legal_ids.shape[0])
-        out = torch.empty(R + nl + 1, dtype=torch.float32, device=self._device)
+        stream = torch.cuda.current_stream(self._device)
+        dstep = buffers.stage(plan, stream)
+        out, host = buffers.outputs(R + nl + 1)
         self._status.zero_()
         self._model.run(dstep, self.pool, value_stm=out[:R], legal_logits=out[R : R + nl],
-                        status=self._status)
-        out[R + nl :].copy_(self._status.view(torch.float32))
-        host = torch.empty(R + nl + 1, dtype=torch.float32, pin_memory=True)
+                        status=self._status, stream=stream)
+        out[R + nl :].copy_(self._status.view(torch.float32))  # before the next step clears it
         host.copy_(out, non_blocking=True)
-        torch.cuda.current_stream(self._device).synchronize()
-        status = int(host[R + nl :].view(torch.int32).item())
+        done = torch.cuda.Event()
+        done.record(stream)
+        return done, host, R, nl
+
+    @staticmethod
+    def _collect(handle):
+        """Wait for a launched step; (value_stm [R], legal_logits flat)."""
+        done, host, R, nl = handle
+        done.synchronize()
+        arr = host.numpy()
+        status = int(arr[R + nl :].view(np.int32)[0])
         if status != _native.IMBA_OK:
             raise _native.ImbaError(status, "device-side check")
-        arr = host.numpy()
-        return arr[:R].copy(), arr[R : R + nl].copy(), dstep
+        return arr[:R].copy(), arr[R : R + nl].copy()
+
+    def _run_rows(self, plan: StepPlan, n_legal_rows: int):
+        """Run one step and bring back (value_stm [R], legal_logits flat)."""
+        v, ll = self._collect(self._launch(plan, self._buffers))
+        return v, ll, None
 
     def _service_roots(self, requests: list) -> list:
         if not requests:
@@ -309,7 +330,6 @@ class ActorInferenceServer:
                 gc.enable()
 
     def _service_waves_impl(self, requests: list) -> list:
-        t0 = time.perf_counter()
         turns: list[_TurnState] = []
         for req in requests:
             key = (int(req.worker_id), int(req.turn_id))
@@ -320,59 +340,81 @@ class ActorInferenceServer:
                     "missing/out-of-order RootEvalRequest, or release_turn() already freed this turn."
                 )
             turns.append(turn)
-        # Rows in request order, packed by the C++ host path (ids, boards,
-        # legal CSR, node / parent ids) in one pass over the wire objects.
         counts = [len(req.rows) for req in requests]
         R = sum(counts)
-        piece = np.empty((R, 64), dtype=np.uint8)
-        side = np.empty((R, 7), dtype=np.int32)
-        _, loff_b, lids_b, node_b, parent_b = _hostpath.pack_wave_rows(requests, piece, side)
-        side[:, 0] = EVENT_TOKEN_ID
-        node_ids = np.frombuffer(node_b, dtype=np.int64).tolist()
-        parent_ids = np.frombuffer(parent_b, dtype=np.int64).tolist()
-        chains_per_req: list[list[list[int]]] = []
-        r0 = 0
-        for turn, n in zip(turns, counts):
-            nc = turn.node_chains
-            chains_per_req.append([nc[p] if p != _NO_PARENT else [] for p in parent_ids[r0 : r0 + n]])
-            r0 += n
-        # Arena rows (logical ids exactly as _KVArena.append mints them) and slots.
-        groups = []
-        for turn, chains in zip(turns, chains_per_req):
+        # A large wave runs as two steps over consecutive request ranges (rows
+        # keep their order, so arena rows are minted exactly as for one step):
+        # the second part is packed and planned while the GPU runs the first,
+        # and the first part's responses are built while the GPU runs the second.
+        if R >= self.split_rows and len(requests) >= 2:
+            csum = np.cumsum(counts)
+            cut = int(np.searchsorted(csum, R / 2)) + 1
+            cut = min(max(cut, 1), len(requests) - 1)
+            parts = [(0, cut), (cut, len(requests))]
+        else:
+            parts = [(0, len(requests))]
+        for turn in turns:
             if turn.arena is None:
                 turn.arena = KVSequence(self.pool)
-            groups.append(WaveGroup(prefix=turn.seq, prefix_len=turn.prefix_len, arena=turn.arena, chains=chains))
         # The reference appends a wave's rows to the arena only after its
         # forward succeeded (actor_server.py:904-914); a failed wave is rolled
         # back so later waves mint the same row ids.
         marks = [(t.arena, t.arena.length, len(t.arena.pages)) for t in turns]
+        launched = []
+        t_build = t_gpu = 0.0
         try:
-            plan, own_rows = wave_plan(groups, piece, side, None,
-                                       legal_csr=(np.frombuffer(loff_b, dtype=np.int32),
-                                                  np.frombuffer(lids_b, dtype=np.int32)))
-            loff = plan.legal_off
+            for (a, b), bufs in zip(parts, (self._buffers, self._buffers2)):
+                t0 = time.perf_counter()
+                launched.append((a, b) + self._plan_part(requests[a:b], turns[a:b], counts[a:b], bufs))
+                t_build += time.perf_counter() - t0
             self._sync_if_profiling()
-            t1 = time.perf_counter()
-            value_stm, legal_flat, _ = self._run_rows(plan, R)
+            responses: list = []
+            t_post = 0.0
+            for a, b, handle, loff, starts, node_b, parent_b in launched:
+                t1 = time.perf_counter()
+                value_stm, legal_flat = self._collect(handle)
+                t2 = time.perf_counter()
+                t_gpu += t2 - t1
+                rows_out = _hostpath.wave_responses(counts[a:b], value_stm, legal_flat, loff)
+                responses.extend(WaveResponse(rows=rows_g) for rows_g in rows_out)
+                t_post += time.perf_counter() - t2
         except BaseException:
+            for h in launched:  # nothing of this wave may still be running when the arenas shrink
+                h[2][0].synchronize()
             for arena, length, npages in reversed(marks):
                 arena.truncate(length, npages)
             raise
-        t2 = time.perf_counter()
-        self.stats["wave_build_s"] += t1 - t0
-        self.stats["wave_gpu_s"] += t2 - t1
+        t3 = time.perf_counter()
+        # node_chains[child] = chain(parent) + [own arena row], in wave order
+        for a, b, handle, loff, starts, node_b, parent_b in launched:
+            _hostpath.record_chains([t.node_chains for t in turns[a:b]], counts[a:b], node_b, parent_b,
+                                    starts.tobytes())
+        self._sync_if_profiling()
+        self.stats["wave_build_s"] += t_build
+        self.stats["wave_gpu_s"] += t_gpu
+        self.stats["wave_post_s"] += t_post + time.perf_counter() - t3
         self.stats["wave_calls"] += 1
         self.stats["wave_reqs"] += len(requests)
         self.stats["wave_rows"] += R
-        rows_out = _hostpath.wave_responses(counts, value_stm, legal_flat, loff)
-        responses = []
-        r0 = 0
-        for turn, chains, own, n, rows_g in zip(turns, chains_per_req, own_rows, counts, rows_out):
-            nc = turn.node_chains
-            for nid, ch, own_row in zip(node_ids[r0 : r0 + n], chains, own):
-                nc[nid] = ch + [own_row]
-            responses.append(WaveResponse(rows=rows_g))
-            r0 += n
-        self._sync_if_profiling()
-        self.stats["wave_post_s"] += time.perf_counter() - t2
         return responses
+
+    def _plan_part(self, requests: list, turns: list, counts: list, buffers: StepBuffers):
+        """Pack, plan and launch one consecutive range of a wave's requests;
+        returns (step handle, legal offsets, first arena row per request,
+        node ids, parent ids)."""
+        R = sum(counts)
+        piece = np.empty((R, 64), dtype=np.uint8)
+        side = np.empty((R, 7), dtype=np.int32)
+        # Rows in request order, packed by the C++ host path (ids, boards,
+        # legal CSR, node / parent ids) in one pass over the wire objects.
+        _, loff_b, lids_b, node_b, parent_b = _hostpath.pack_wave_rows(requests, piece, side)
+        side[:, 0] = EVENT_TOKEN_ID
+        # Parent chains (arena rows of each row's turn) looked up before the
+        # wave, as the reference builds its suffix index (actor_server.py:839-850).
+        depth_b, chain_b = _hostpath.wave_chains([t.node_chains for t in turns], counts, parent_b)
+        plan, starts = wave_plan_flat(
+            [t.seq for t in turns], [t.prefix_len for t in turns], [t.arena for t in turns], counts,
+            np.frombuffer(depth_b, dtype=np.int64), np.frombuffer(chain_b, dtype=np.int64), piece, side,
+            (np.frombuffer(loff_b, dtype=np.int32), np.frombuffer(lids_b, dtype=np.int32)))
+        handle = self._launch(plan, buffers)
+        return handle, plan.legal_off, starts, node_b, parent_b

@@ -104,27 +104,44 @@ def wave_plan(groups: list[WaveGroup], piece: np.ndarray, side: np.ndarray, lega
     Legal ids come as per-row lists or, already packed, as ``legal_csr`` =
     (int32 offsets [R+1], int32 ids).  Returns the plan and, per group, the
     arena rows minted for its rows."""
-    G = len(groups)
-    counts = np.fromiter((len(g.chains) for g in groups), dtype=np.int64, count=G)
+    counts = np.fromiter((len(g.chains) for g in groups), dtype=np.int64, count=len(groups))
+    all_chains = [c for g in groups for c in g.chains]
+    depths = np.fromiter(map(len, all_chains), dtype=np.int64, count=len(all_chains))
+    flat = np.fromiter(chain.from_iterable(all_chains), dtype=np.int64, count=int(depths.sum()))
+    plan, starts = wave_plan_flat([g.prefix for g in groups], [g.prefix_len for g in groups],
+                                  [g.arena for g in groups], counts, depths, flat, piece, side,
+                                  legal_csr if legal_csr is not None else ids_csr(legal_ids))
+    own_rows = [list(range(int(s), int(s) + int(n))) for s, n in zip(starts, counts)]
+    return plan, own_rows
+
+
+def wave_plan_flat(prefixes: list[KVSequence], prefix_lens, arenas: list[KVSequence], counts: np.ndarray,
+                   depths: np.ndarray, chain_rows: np.ndarray, piece: np.ndarray, side: np.ndarray,
+                   legal_csr: tuple[np.ndarray, np.ndarray]) -> tuple[StepPlan, np.ndarray]:
+    """``wave_plan`` on flat arrays: group g has ``counts[g]`` rows; row r's
+    parent chain (arena row ids of its group's arena, root -> parent) is
+    ``chain_rows[sum(depths[:r]) : sum(depths[:r + 1])]``.  Reserves one
+    arena row per decode row, numbered consecutively per arena in wave order
+    like ``_KVArena.append`` (actor_server.py:246-255; an arena listed twice
+    continues where its previous group stopped).  Returns the plan and, per
+    group, the arena row id of its first new row."""
+    G = len(prefixes)
+    counts = np.asarray(counts, dtype=np.int64).reshape(G)
     R = int(counts.sum())
-    starts = [g.arena.length for g in groups]
-    dst = KVSequence.reserve_many([g.arena for g in groups], counts)
-    # A group's own rows: the arena rows just reserved (an arena listed twice
-    # continues where its previous group stopped).
-    own_rows: list[list[int]] = []
+    starts = np.empty(G, dtype=np.int64)
     seen: dict[int, int] = {}
-    for g, start, n in zip(groups, starts, counts.tolist()):
-        start = seen.get(id(g.arena), start)
-        own_rows.append(list(range(start, start + n)))
-        seen[id(g.arena)] = start + n
-    npre = [min(-(-g.prefix_len // PAGE), len(g.prefix.pages)) for g in groups]  # as page_array slices
-    pages_cat = np.fromiter(chain.from_iterable(g.prefix.pages[:k] for g, k in zip(groups, npre)), dtype=np.int64,
+    for i, (a, n) in enumerate(zip(arenas, counts.tolist())):
+        s0 = seen.get(id(a), a.length)
+        starts[i] = s0
+        seen[id(a)] = s0 + n
+    dst = KVSequence.reserve_many(arenas, counts)
+    plen = np.asarray(prefix_lens, dtype=np.int64).reshape(G)
+    npre = [min(-(-int(n) // PAGE), len(p.pages)) for p, n in zip(prefixes, plen)]  # as page_array slices
+    pages_cat = np.fromiter(chain.from_iterable(p.pages[:k] for p, k in zip(prefixes, npre)), dtype=np.int64,
                             count=sum(npre))
     row_group = np.repeat(np.arange(G), counts)
-    plen = np.fromiter((g.prefix_len for g in groups), dtype=np.int64, count=G)
-    all_chains = [c for g in groups for c in g.chains]
-    depths = np.fromiter(map(len, all_chains), dtype=np.int64, count=R)
     prow = plen[row_group]
+    depths = np.asarray(depths, dtype=np.int64).reshape(R)
     positions = prow + depths
     # Extras of row r: its chain (positions P + j), then itself (position P + depth).
     per_row = depths + 1
@@ -136,19 +153,25 @@ def wave_plan(groups: list[WaveGroup], piece: np.ndarray, side: np.ndarray, lega
     own_idx = eoff[1:] - 1
     extra_slot[own_idx] = dst
     extra_pos[own_idx] = positions
-    if int(depths.sum()):
+    if E > R:
         is_chain = np.ones(E, dtype=bool)
         is_chain[own_idx] = False
-        chain_slots = []
-        for g in groups:
-            flat = np.fromiter(chain.from_iterable(g.chains), dtype=np.int64)
-            chain_slots.append(g.arena.slots_of(flat) if flat.size else np.zeros(0, np.int64))
-        extra_slot[is_chain] = np.concatenate(chain_slots)
+        # arena row -> slot through each row's arena page list (after the reservation)
+        apages = [a.pages for a in arenas]
+        anp = np.fromiter(map(len, apages), dtype=np.int64, count=G)
+        abase = np.zeros(G, dtype=np.int64)
+        np.cumsum(anp[:-1], out=abase[1:])
+        acat = np.fromiter(chain.from_iterable(apages), dtype=np.int64, count=int(anp.sum()))
+        rows = np.asarray(chain_rows, dtype=np.int64)
+        grp = np.repeat(row_group, depths)
+        if rows.size and (rows.min() < 0 or (rows // PAGE >= anp[grp]).any()):
+            raise KeyError("a parent chain names an arena row its turn does not hold")
+        extra_slot[is_chain] = acat[abase[grp] + rows // PAGE] * PAGE + rows % PAGE
         j = np.arange(E) - np.repeat(eoff[:-1], per_row)  # index within the row's extras
         extra_pos[is_chain] = (np.repeat(prow, per_row) + j)[is_chain]
     gpo = np.zeros(G + 1, dtype=np.int64)
     np.cumsum(npre, out=gpo[1:])
-    loff, lids = legal_csr if legal_csr is not None else ids_csr(legal_ids)
+    loff, lids = legal_csr
     plan = StepPlan(
         piece_ids=piece,
         side_ids=side,
@@ -164,4 +187,4 @@ def wave_plan(groups: list[WaveGroup], piece: np.ndarray, side: np.ndarray, lega
         legal_off=loff,
         legal_ids=lids,
     )
-    return plan, own_rows
+    return plan, starts

@@ -136,21 +136,21 @@ def test_server_maps_device_range_error_to_exception():
                     legal_vocab_ids=[3, 7, 11]) for i in range(6)])]
 
     clean = server.service(wave(0))
-    orig = server_mod.wave_plan
+    orig = server_mod.wave_plan_flat
 
     def corrupt(*a, **k):
-        plan, own = orig(*a, **k)
+        plan, starts = orig(*a, **k)
         plan.row_vis = plan.row_vis.copy()
         plan.row_vis[0] += 64  # past the prefix's pages
-        return plan, own
+        return plan, starts
 
-    server_mod.wave_plan = corrupt
+    server_mod.wave_plan_flat = corrupt
     try:
         with pytest.raises(_native.ImbaError) as ei:
             server.service(wave(100))
         assert ei.value.code == _native.IMBA_ERR_RANGE
     finally:
-        server_mod.wave_plan = orig
+        server_mod.wave_plan_flat = orig
     again = server.service(wave(200))
     for (v0, l0), (v1, l1) in zip(clean[0].rows, again[0].rows):
         assert v0 == v1 and l0 == l1
