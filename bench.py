@@ -74,6 +74,8 @@ WORKLOADS = {
     "halving": {"parents": 1024, "plies": (40, 250), "siblings": None, "rounds": (32, 16, 8, 4, 2)},
     # games, plies log-uniform in [lo, hi], decode steps built (cycled when more are timed)
     "prefill_decode": {"parents": 1024, "plies": (1, 300), "siblings": None, "rounds": (50,)},
+    # the headline wave through the dense model API and through the paged executors
+    "model_api": {"parents": 256, "plies": (20, 200), "siblings": None, "rounds": None},
 }
 UNIT = "positions/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -152,7 +154,7 @@ def workload(args, rank, world=1):
     from imba_chess_b200.shard import shard_games
 
     mine = shard_games(args.parents * world, rank, world)
-    if args.workload == "grouped":
+    if args.workload in ("grouped", "model_api"):
         dims = synth.D512
         parts = [synth.chess_grouped_wave(n_parents=1, plies=tuple(args.plies), seed=1234 + i) for i in mine]
     else:
@@ -189,6 +191,18 @@ def workload_config(args):
             "games_per_gpu": args.parents,
             "page_tokens": 16,
             "l2": "inputs larger than L2 (prefix KV read per round > 126 MB at full size)",
+        }
+    if args.workload == "model_api":
+        return {
+            "workload": "grouped-decode wave through the reference-compatible APIs: bf16 HSTU d512/8L/8H "
+                        f"(max_pos 513), {args.parents} parents from random legal play of "
+                        f"U[{args.plies[0]},{args.plies[1]}] plies, every legal move as a depth-0 sibling; "
+                        "value: B200HSTUChessModel.forward_decode_grouped on the reference's padded [G,H,maxP,d] "
+                        "prefix stack (device tensors, full 1,970-way logits and new per-layer KV returned, "
+                        "synchronised per call); paged: the rollout executor on pool-resident prefixes",
+            "parents_per_gpu": args.parents,
+            "page_tokens": 16,
+            "l2": "inputs larger than L2 (prefix stack per call > 126 MB)",
         }
     if args.workload == "d1024":
         return {
@@ -886,6 +900,84 @@ def measure(args, model, dims, device, rank, world, sampler=None):
     return result
 
 
+def run_model_api(args, model, dims, device, rank, world):
+    """The headline wave through the dense reference-compatible model API
+    (``forward_decode_grouped`` with the padded prefix stack the reference's
+    merge builds, merged_executors.py:187-196) and through the paged rollout
+    executors (imba_chess_b200.executors); each call synchronised."""
+    import torch
+
+    from imba_chess_b200 import synth
+    from imba_chess_b200.executors import PagedDecodeRequest, make_decode_wave_executor, make_root_eval_executor
+
+    _, wave = workload(args, rank, world)
+    lens = wave.prefix_lens
+    G, B, L = len(lens), wave.num_rows, dims.num_layers
+    tok = synth.concat_tokens(wave.prefix_tokens)
+    offsets = np.concatenate([[0], np.cumsum(lens)])
+    batch = {k: torch.from_numpy(v) for k, v in tok.items()}
+    batch["seq_offsets"] = torch.from_numpy(offsets)
+    batch["total_tokens"] = int(offsets[-1])
+    kv = model.forward(batch, return_loss=False, return_kv=True)["kv_caches"]
+    max_p = max(lens)
+    stack = []
+    for k, v in kv:  # the reference's per-wave merge: pad every prefix to maxP and stack
+        ks = torch.zeros((G, dims.num_heads, max_p, dims.attention_dim), dtype=k.dtype, device=device)
+        vs = torch.zeros((G, dims.num_heads, max_p, dims.linear_dim), dtype=v.dtype, device=device)
+        for g in range(G):
+            a, b = int(offsets[g]), int(offsets[g + 1])
+            ks[g, :, : b - a] = k[:, a:b]
+            vs[g, :, : b - a] = v[:, a:b]
+        stack.append((ks, vs))
+    del kv
+    rt = wave.row_tokens
+    new = {k: torch.from_numpy(v).to(device) for k, v in rt.items()}
+    gi = torch.from_numpy(wave.group_index).to(device)
+    pos = torch.from_numpy(np.asarray(lens)[wave.group_index]).to(device)
+    lens_t = torch.tensor(lens, device=device)
+
+    def call():
+        return model.forward_decode_grouped(new_token_batch=new, positions=pos, group_index=gi,
+                                            prefix_kv_grouped=stack, prefix_lens=lens_t, prefix_lens_list=lens)
+
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    lat = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        call()
+        torch.cuda.synchronize()
+        lat.append(time.perf_counter() - t0)
+    dense_ms = 1000.0 * statistics.median(lat)
+    # paged: roots into the pool once, then the decode wave per call
+    pool = model.new_pool(sum(-(-n // 16) for n in lens) + (args.warmup + args.steps + 2) * (-(-B // 16) + G) + 64)
+    root = make_root_eval_executor(model=model, pool=pool)
+    games = [r["game"] for r in root([dict(pt) for pt in wave.prefix_tokens])]
+    decode = make_decode_wave_executor(model=model, pool=pool)
+    reqs = []
+    for g in range(G):
+        idx = np.nonzero(wave.group_index == g)[0]
+        reqs.append(PagedDecodeRequest(game=games[g], tokens=synth.slice_tokens(rt, idx),
+                                       parent_rows=[[] for _ in idx],
+                                       legal_ids=[wave.legal_ids[i].tolist() for i in idx]))
+    for _ in range(args.warmup):
+        decode(reqs)
+    plat = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        decode(reqs)
+        plat.append(time.perf_counter() - t0)
+    paged_ms = 1000.0 * statistics.median(plat)
+    return {
+        "metric": METRIC, "value": B / (dense_ms / 1000.0), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dense_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": full_config(args, B, world),
+        "timing": "wall clock per call (p50), each call synchronised",
+        "paged_executor": {"value": B / (paged_ms / 1000.0), "unit": UNIT, "ms_per_step": paged_ms},
+    }
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -908,6 +1000,14 @@ def run_b200(args):
         dims = synth.D512
     sd = synth.make_state_dict(dims, 2, profile="reference")
     model = B200HSTUChessModel(sd, dtype=torch.bfloat16, device=device)
+    if args.workload == "model_api":
+        line = run_model_api(args, model, dims, device, rank, world)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     sampler = ClockSampler(local)
     res = measure(args, model, dims, device, rank, world, sampler=sampler)
 

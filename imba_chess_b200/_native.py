@@ -60,6 +60,7 @@ EXPORTED_SYMBOLS = (
     "imba_kv_scatter",
     "imba_kv_gather",
     "imba_selftest_wait_timeout",
+    "imba_kv_scatter_indexed",
 )
 
 _P = ctypes.c_void_p
@@ -201,6 +202,10 @@ def load() -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = [_P, ctypes.POINTER(PoolDesc), _I32, _I32, _P, _P, _P, _P, _P]
             fn.restype = _I32
+        lib.imba_kv_scatter_indexed.argtypes = [_P, ctypes.POINTER(PoolDesc), _I32, _I32, _P, _P, _P, _P, _P,
+                                                ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64), _P,
+                                                _P]
+        lib.imba_kv_scatter_indexed.restype = _I32
         lib.imba_selftest_wait_timeout.argtypes = [ctypes.c_int64, _P, _P]
         lib.imba_selftest_wait_timeout.restype = _I32
         _lib = lib

@@ -378,6 +378,33 @@ imba_status_t imba_kv_scatter(const imba_model* model, const imba_pool_desc* poo
                  stream);
 }
 
+imba_status_t imba_kv_scatter_indexed(const imba_model* model, const imba_pool_desc* pool, int32_t layer, int32_t n,
+                                      const int32_t* slots, const int32_t* src_a, const int32_t* src_b,
+                                      const void* src_k, const void* src_v, const int64_t* strides_k,
+                                      const int64_t* strides_v, int32_t* status, void* stream) {
+  if (!model || !pool || !pool->base || pool->num_pages <= 0) return IMBA_ERR_ARG;
+  if (layer < 0 || layer >= model->d.num_layers || n < 0) return IMBA_ERR_RANGE;
+  if (n == 0) return IMBA_OK;
+  if (!slots || !src_a || !src_b || !src_k || !src_v || !strides_k || !strides_v) return IMBA_ERR_ARG;
+  imba::KVStrides st;
+  for (int i = 0; i < 4; ++i) {
+    st.k[i] = strides_k[i];
+    st.v[i] = strides_v[i];
+  }
+  const imba::PoolGeom g = model->geom(pool->num_pages);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (model->d.dtype == IMBA_DTYPE_BF16)
+    e = imba::launch_kv_scatter_indexed<imba::bf16>(g, static_cast<imba::bf16*>(pool->base), layer, n, slots, src_a,
+                                                    src_b, static_cast<const imba::bf16*>(src_k),
+                                                    static_cast<const imba::bf16*>(src_v), st, status, s);
+  else
+    e = imba::launch_kv_scatter_indexed<float>(g, static_cast<float*>(pool->base), layer, n, slots, src_a, src_b,
+                                               static_cast<const float*>(src_k), static_cast<const float*>(src_v), st,
+                                               status, s);
+  return e == cudaSuccess ? IMBA_OK : IMBA_ERR_CUDA;
+}
+
 imba_status_t imba_kv_gather(const imba_model* model, const imba_pool_desc* pool, int32_t layer, int32_t n,
                              const int32_t* slots, void* dense_k, void* dense_v, int32_t* status, void* stream) {
   return kv_copy(model, pool, layer, n, slots, dense_k, dense_v, 0, status, stream);

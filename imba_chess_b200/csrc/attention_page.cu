@@ -277,23 +277,32 @@ __device__ __forceinline__ void step16(RowState& rs, uint32_t qb, uint32_t kb, u
   }
 }
 
-// Fold one extra key (pool slot, position) into one row's online softmax.
+// One extra key's K and V as this lane's slice: K dims 16 t .. 16 t + 15
+// (two 16-byte loads) and V columns 8 j + 2 t, +1 (j < 8).
+struct ExtraKV {
+  uint4 k[2];
+  uint32_t v[8];
+};
+
+__device__ __forceinline__ void extra_load(ExtraKV& x, bool active, const bf16* kp, const bf16* vp, int t) {
+  x.k[0] = x.k[1] = make_uint4(0, 0, 0, 0);
+  if (active) {
+    x.k[0] = __ldg(reinterpret_cast<const uint4*>(kp + 16 * t));
+    x.k[1] = __ldg(reinterpret_cast<const uint4*>(kp + 16 * t + 8));
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) x.v[j] = active ? __ldg(reinterpret_cast<const uint32_t*>(vp + 8 * j + 2 * t)) : 0u;
+}
+
+// Fold one extra key (loaded by extra_load) into one row's online softmax.
 // The row's four lanes (t = 0..3) each take 16 of the 64 dims of q . k and
 // reduce across the quad; ol / oh: this lane's O columns 8 j + 2 t, +1 of the
 // row.  active is uniform across the quad.
 template <class Bias>
-__device__ __forceinline__ void extra_key(float& m, float& l, float (&o)[8][4], int ci, bool active, uint32_t qrow,
-                                          int qrow_sw, const bf16* kp, const bf16* vp, int kpos, int qpos,
-                                          const Bias& psw, float scale2, int max_pos, int t) {
+__device__ __forceinline__ void extra_apply(float& m, float& l, float (&o)[8][4], int ci, bool active, uint32_t qrow,
+                                            int qrow_sw, const ExtraKV& x, int kpos, int qpos, const Bias& psw,
+                                            float scale2, int max_pos, int t) {
   float part = 0.f;
-  uint4 kv[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-  if (active) {
-    kv[0] = __ldg(reinterpret_cast<const uint4*>(kp + 16 * t));
-    kv[1] = __ldg(reinterpret_cast<const uint4*>(kp + 16 * t + 8));
-  }
-  uint32_t vv[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) vv[j] = active ? __ldg(reinterpret_cast<const uint32_t*>(vp + 8 * j + 2 * t)) : 0u;
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
     uint4 qv;
@@ -301,7 +310,7 @@ __device__ __forceinline__ void extra_key(float& m, float& l, float (&o)[8][4], 
                  : "=r"(qv.x), "=r"(qv.y), "=r"(qv.z), "=r"(qv.w)
                  : "r"(qrow + (uint32_t)(((2 * t + c) ^ qrow_sw) << 4)));
     const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
-    const uint32_t kw[4] = {kv[c].x, kv[c].y, kv[c].z, kv[c].w};
+    const uint32_t kw[4] = {x.k[c].x, x.k[c].y, x.k[c].z, x.k[c].w};
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const float2 qf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qw[w]));
@@ -320,7 +329,7 @@ __device__ __forceinline__ void extra_key(float& m, float& l, float (&o)[8][4], 
   l = fmaf(l, c, t == 0 ? p : 0.f);  // the quad's partial sums: one lane counts the key
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const float2 vf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vv[j]));
+    const float2 vf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&x.v[j]));
     o[j][2 * ci] = fmaf(o[j][2 * ci], c, p * vf.x);
     o[j][2 * ci + 1] = fmaf(o[j][2 * ci + 1], c, p * vf.y);
   }
@@ -759,32 +768,46 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       for (int o = 4; o < 32; o <<= 1) emax = max(emax, __shfl_xor_sync(0xffffffffu, emax, o));
       const uint32_t qr0 = qb + g * 128, qr1 = qb + (g + 8) * 128;  // rows rl0, rl1 of the query tile
       for (int e = 0; e < emax; ++e) {
+        int kpos[2] = {0, 0}, slot[2] = {-1, -1};
 #pragma unroll
         for (int ci = 0; ci < 2; ++ci) {
           const int cnt = ci ? c1 : c0;
-          int slot = -1, kpos = 0;
           if (e == 0) {  // resolved (and range-checked) by the producer
             const int rl = ci ? rl1 : rl0;
             if (cnt > 0) {
-              slot = item[kItX0slot + rl];
-              kpos = item[kItX0pos + rl];
+              slot[ci] = item[kItX0slot + rl];
+              kpos[ci] = item[kItX0pos + rl];
             }
           } else if (e < cnt) {
             const int xi = (ci ? o1 : o0) + e;
-            slot = st.extra_slot[xi];
-            kpos = st.extra_pos[xi];
-            if (slot < 0 || slot >= a.g.num_slots) {
+            slot[ci] = st.extra_slot[xi];
+            kpos[ci] = st.extra_pos[xi];
+            if (slot[ci] < 0 || slot[ci] >= a.g.num_slots) {
               report(st.status, IMBA_ERR_RANGE);
-              slot = -1;
+              slot[ci] = -1;
             }
           }
-          const bool act = slot >= 0;
-          const bf16* kp = Pool + (act ? a.g.k_off(slot, a.layer, h) : 0);
-          const bf16* vp = Pool + (act ? a.g.v_off(slot, a.layer, h) : 0);
+        }
+        // Both rows' K / V lines move towards L1 together (lane t of a quad:
+        // row rl0 | rl1 by t & 1, K | V by t & 2), so the second row's loads
+        // below do not wait a second memory round trip.
+        {
+          const int sl = slot[t & 1];
+          if (sl >= 0) {
+            const bf16* ln = Pool + ((t & 2) ? a.g.v_off(sl, a.layer, h) : a.g.k_off(sl, a.layer, h));
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(ln));
+          }
+        }
+#pragma unroll
+        for (int ci = 0; ci < 2; ++ci) {
+          const bool act = slot[ci] >= 0;
+          ExtraKV x;
+          extra_load(x, act, Pool + (act ? a.g.k_off(slot[ci], a.layer, h) : 0),
+                     Pool + (act ? a.g.v_off(slot[ci], a.layer, h) : 0), t);
           if (ci == 0)
-            extra_key(rs.m0, rs.l0, rs.o, 0, act, qr0, g & 7, kp, vp, kpos, qp0, psw, scale2, a.max_pos, t);
+            extra_apply(rs.m0, rs.l0, rs.o, 0, act, qr0, g & 7, x, kpos[0], qp0, psw, scale2, a.max_pos, t);
           else
-            extra_key(rs.m1, rs.l1, rs.o, 1, act, qr1, (g + 8) & 7, kp, vp, kpos, qp1, psw, scale2, a.max_pos, t);
+            extra_apply(rs.m1, rs.l1, rs.o, 1, act, qr1, (g + 8) & 7, x, kpos[1], qp1, psw, scale2, a.max_pos, t);
         }
       }
     }

@@ -91,6 +91,12 @@ struct PoolGeom {
   }
 };
 
+// Element strides [a, b, head, dim] of a dense K or V source (imba_kv_scatter_indexed).
+struct KVStrides {
+  int64_t k[4];
+  int64_t v[4];
+};
+
 }  // namespace imba
 
 // The opaque handle behind imba_model*.

@@ -37,6 +37,10 @@ cudaError_t launch_value_legal(const imba_model_desc& md, const imba_step_desc& 
 template <typename T>
 cudaError_t launch_kv_copy(const PoolGeom& g, T* pool, int layer, int n, const int32_t* slots, T* dk, T* dv,
                            int to_pool, int32_t* status, cudaStream_t s);
+template <typename T>
+cudaError_t launch_kv_scatter_indexed(const PoolGeom& g, T* pool, int layer, int n, const int32_t* slots,
+                                      const int32_t* ia, const int32_t* ib, const T* sk, const T* sv,
+                                      const KVStrides& st, int32_t* status, cudaStream_t s);
 template <typename TA, typename TW, class Epi>
 cudaError_t launch_gemm_simt(const TA* A, int lda, const TW* W, int ldw, int M, int N, int K, Epi epi,
                              cudaStream_t s);

@@ -410,6 +410,34 @@ __global__ void kv_copy_kernel(PoolGeom g, T* pool, int layer, int n, const int3
   }
 }
 
+// Dense strided K / V rows -> pool slots: row r's element (h, e) comes from
+// src[a[r] * s[0] + b[r] * s[1] + h * s[2] + e * s[3]] (elements).  One CTA
+// per row.
+template <typename T>
+__global__ void kv_scatter_indexed_kernel(PoolGeom g, T* pool, int layer, int n, const int32_t* __restrict__ slots,
+                                          const int32_t* __restrict__ ia, const int32_t* __restrict__ ib,
+                                          const T* __restrict__ sk, const T* __restrict__ sv, KVStrides st,
+                                          int32_t* status) {
+  const int r = blockIdx.x;
+  if (r >= n) return;
+  const int64_t slot = slots[r];
+  if (slot < 0 || slot >= g.num_slots) {
+    if (threadIdx.x == 0) report(status, IMBA_ERR_RANGE);
+    return;
+  }
+  const int64_t a = ia[r], b = ib[r];
+  const int nk = g.H * g.dqk, nv = g.H * g.dv;
+  for (int i = threadIdx.x; i < nk + nv; i += blockDim.x) {
+    if (i < nk) {
+      const int h = i / g.dqk, e = i % g.dqk;
+      pool[g.k_off(slot, layer, h) + e] = sk[a * st.k[0] + b * st.k[1] + h * st.k[2] + e * st.k[3]];
+    } else {
+      const int j = i - nk, h = j / g.dv, e = j % g.dv;
+      pool[g.v_off(slot, layer, h) + e] = sv[a * st.v[0] + b * st.v[1] + h * st.v[2] + e * st.v[3]];
+    }
+  }
+}
+
 inline int warp_blocks(int rows) { return (rows + 7) / 8; }  // 8 warps per 256-thread block
 
 }  // namespace
@@ -458,6 +486,20 @@ cudaError_t launch_kv_copy(const PoolGeom& g, T* pool, int layer, int n, const i
 }
 template cudaError_t launch_kv_copy<float>(const PoolGeom&, float*, int, int, const int32_t*, float*, float*, int,
                                            int32_t*, cudaStream_t);
+
+template <typename T>
+cudaError_t launch_kv_scatter_indexed(const PoolGeom& g, T* pool, int layer, int n, const int32_t* slots,
+                                      const int32_t* ia, const int32_t* ib, const T* sk, const T* sv,
+                                      const KVStrides& st, int32_t* status, cudaStream_t s) {
+  kv_scatter_indexed_kernel<T><<<n, 128, 0, s>>>(g, pool, layer, n, slots, ia, ib, sk, sv, st, status);
+  return cudaGetLastError();
+}
+template cudaError_t launch_kv_scatter_indexed<float>(const PoolGeom&, float*, int, int, const int32_t*,
+                                                      const int32_t*, const int32_t*, const float*, const float*,
+                                                      const KVStrides&, int32_t*, cudaStream_t);
+template cudaError_t launch_kv_scatter_indexed<bf16>(const PoolGeom&, bf16*, int, int, const int32_t*, const int32_t*,
+                                                     const int32_t*, const bf16*, const bf16*, const KVStrides&,
+                                                     int32_t*, cudaStream_t);
 template cudaError_t launch_kv_copy<bf16>(const PoolGeom&, bf16*, int, int, const int32_t*, bf16*, bf16*, int,
                                           int32_t*, cudaStream_t);
 

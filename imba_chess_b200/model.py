@@ -31,7 +31,7 @@ import torch
 
 from . import _native
 from .kvpool import PAGE, KVPool
-from .plan import DeviceStep, StepPlan, piece_ids_from_tokens, side_ids_from_tokens
+from .plan import DeviceStep, StepBuffers, StepPlan, piece_ids_from_tokens, side_ids_from_tokens
 from .weights import PackedWeights
 
 _TOKEN_KEYS = (
@@ -223,7 +223,7 @@ class B200HSTUChessModel:
         doc_pages = -(-lengths // PAGE)
         page_off = np.concatenate([[0], np.cumsum(doc_pages)]).astype(np.int64)
         total_pages = max(int(page_off[-1]), 1)
-        pool = self.new_pool(total_pages)
+        pool = self._scratch_pool(total_pages)
         row_doc = np.repeat(np.arange(ndocs), lengths)
         local = np.arange(S) - np.repeat(offsets[:-1], lengths)
         slots = (page_off[row_doc] + local // PAGE) * PAGE + local % PAGE
@@ -324,7 +324,7 @@ class B200HSTUChessModel:
         extra_tokens = n_valid + B
         region0 = int(gpage_off[-1])
         total_pages = max(region0 + -(-extra_tokens // PAGE), 1)
-        pool = self.new_pool(total_pages)
+        pool = self._scratch_pool(total_pages)
         # extras: row r's valid suffix entries (in order), then its own slot
         per_row = smask.sum(axis=1).astype(np.int64) + 1
         extra_off = np.concatenate([[0], np.cumsum(per_row)]).astype(np.int64)
@@ -349,33 +349,31 @@ class B200HSTUChessModel:
             group_page_off=gpage_off.astype(np.int32),
             group_pages=np.arange(region0, dtype=np.int32),
         )
-        # Stage the dense prefix / suffix KV into the scratch pool.
+        # Stage the caller's dense prefix stack and suffix tensors straight
+        # into the scratch pool (one strided scatter per layer and tensor; the
+        # index arrays go to the device in one copy).
         g_tok = np.concatenate([np.arange(n) for n in lens_arr]) if G else np.zeros(0, np.int64)
         g_of = np.repeat(np.arange(G), lens_arr)
         prefix_slots = (gpage_off[g_of] + g_tok // PAGE) * PAGE + g_tok % PAGE
-        prefix_slots_t = torch.from_numpy(prefix_slots.astype(np.int32)).to(self.device)
-        suffix_slots_t = torch.from_numpy((region0 * PAGE + suffix_dst).astype(np.int32)).to(self.device)
-        g_of_t = torch.from_numpy(g_of).to(self.device)
-        g_tok_t = torch.from_numpy(g_tok).to(self.device)
-        rr_t = torch.from_numpy(rr).to(self.device)
-        cc_t = torch.from_numpy(cc).to(self.device)
+        suffix_slots = region0 * PAGE + suffix_dst
+        np_, ns_ = int(prefix_slots.size), int(suffix_slots.size) if has_suffix else 0
+        idx = np.concatenate([prefix_slots, g_of, g_tok, suffix_slots[:ns_], rr[:ns_], cc[:ns_],
+                              plan.row_dst_slot]).astype(np.int32)
+        idx_d = torch.from_numpy(idx).to(self.device, non_blocking=True)
+        o = 0
+        p_slots, p_a, p_b = idx_d[o:o + np_], idx_d[o + np_:o + 2 * np_], idx_d[o + 2 * np_:o + 3 * np_]
+        o += 3 * np_
+        s_slots, s_a, s_b = idx_d[o:o + ns_], idx_d[o + ns_:o + 2 * ns_], idx_d[o + 2 * ns_:o + 3 * ns_]
+        o += 3 * ns_
+        own_t = idx_d[o:o + B]
         for l in range(L):
-            pk, pv = prefix_kv_grouped[l]
-            if prefix_slots.size:
-                pk = pk.to(self.device)
-                pv = pv.to(self.device)
-                kd = pk[g_of_t, :, g_tok_t, :].to(self.dtype).contiguous()  # [N, H, d]
-                vd = pv[g_of_t, :, g_tok_t, :].to(self.dtype).contiguous()
-                self.kv_scatter(pool, l, prefix_slots_t, kd, vd)
-            if has_suffix and n_valid:
+            if np_:
+                pk, pv = prefix_kv_grouped[l]
+                self._scatter_dense(pool, l, np_, p_slots, p_a, p_b, pk, pv)
+            if ns_:
                 sk, sv = suffix_kv[l]
-                sk = sk.to(self.device)
-                sv = sv.to(self.device)
-                kd = sk[rr_t, :, cc_t, :].to(self.dtype).contiguous()
-                vd = sv[rr_t, :, cc_t, :].to(self.dtype).contiguous()
-                self.kv_scatter(pool, l, suffix_slots_t, kd, vd)
+                self._scatter_dense(pool, l, ns_, s_slots, s_a, s_b, sk, sv)
         out = self._run_dense(plan, pool)
-        own_t = torch.from_numpy(plan.row_dst_slot).to(self.device)
         new_kv = []
         for l in range(L):
             k, v = self.kv_gather(pool, l, own_t)
@@ -386,11 +384,39 @@ class B200HSTUChessModel:
         self.check_status()
         return result
 
+    def _scratch_pool(self, num_pages: int) -> KVPool:
+        """The dense-API entry points' scratch pool, reused across calls and
+        grown (by a quarter more than asked) when a call needs more pages."""
+        pool = getattr(self, "_scratch", None)
+        if pool is None or pool.num_pages < num_pages:
+            pool = self._scratch = self.new_pool(max(num_pages, int(num_pages * 1.25), 64))
+        return pool
+
+    def _scatter_dense(self, pool: KVPool, layer: int, n: int, slots, ia, ib, k: torch.Tensor,
+                       v: torch.Tensor) -> None:
+        """Rows (ia[r], :, ib[r], :) of dense [A, H, B, d] K / V tensors into
+        ``slots`` of ``pool`` (imba_kv_scatter_indexed)."""
+        if k.device != self.device or k.dtype != self.dtype:
+            k = k.to(device=self.device, dtype=self.dtype)
+        if v.device != self.device or v.dtype != self.dtype:
+            v = v.to(device=self.device, dtype=self.dtype)
+        # [A, H, B, d] tensors: strides in the order (a, b, head, dim)
+        sk = (ctypes.c_int64 * 4)(k.stride(0), k.stride(2), k.stride(1), k.stride(3))
+        sv = (ctypes.c_int64 * 4)(v.stride(0), v.stride(2), v.stride(1), v.stride(3))
+        s = torch.cuda.current_stream(self.device)
+        with torch.cuda.device(self.device):
+            code = self._lib.imba_kv_scatter_indexed(self._handle, ctypes.byref(pool.desc), layer, n,
+                                                     slots.data_ptr(), ia.data_ptr(), ib.data_ptr(), k.data_ptr(),
+                                                     v.data_ptr(), sk, sv, self._status.data_ptr(), s.cuda_stream)
+        _native.check(code, "imba_kv_scatter_indexed")
+
     def _run_dense(self, plan: StepPlan, pool: KVPool) -> dict[str, torch.Tensor]:
         R = plan.num_rows
         logits = torch.empty((R, self.dims.vocab), dtype=torch.float32, device=self.device)
         value_logits = torch.empty((R, 3), dtype=torch.float32, device=self.device)
         if R:
-            dstep = DeviceStep(plan, self.device)
+            if getattr(self, "_buffers", None) is None:
+                self._buffers = StepBuffers(self.device)
+            dstep = self._buffers.stage(plan)  # reused pinned buffers: every dense call ends synchronised
             self.run(dstep, pool, logits=logits, value_logits=value_logits)
         return {"logits": logits, "value_logits": value_logits}

@@ -245,6 +245,21 @@ IMBA_API imba_status_t imba_step_profiled(const imba_model* model, const imba_st
                                           size_t workspace_bytes, void* stream,
                                           void* const* events, int32_t num_events);
 
+/* Dense strided K / V rows of one layer into pool slots, in the model dtype,
+ * without an intermediate copy: row r (< n) goes to slot slots[r]; its
+ * element (head h, dim e) is read from
+ *   src_k[src_a[r] * strides_k[0] + src_b[r] * strides_k[1] + h * strides_k[2] + e * strides_k[3]]
+ * (strides in elements; src_v likewise).  With (src_a, src_b) = (group,
+ * token) this stages the reference's padded [G, H, maxP, d] prefix stack
+ * (hstu_model.py:651-752, merged_executors.py:187-196), with (row, column)
+ * its [B, H, s, d] suffix tensors.  Slots outside the pool are skipped and
+ * reported in the status word (IMBA_ERR_RANGE). */
+IMBA_API imba_status_t imba_kv_scatter_indexed(const imba_model* model, const imba_pool_desc* pool, int32_t layer,
+                                               int32_t n, const int32_t* slots, const int32_t* src_a,
+                                               const int32_t* src_b, const void* src_k, const void* src_v,
+                                               const int64_t* strides_k, const int64_t* strides_v, int32_t* status,
+                                               void* stream);
+
 /* Failure-path self-test.  Launches one CTA on `stream` that runs the
  * library's bounded device-side wait (the one every pipelined kernel uses,
  * 2 s in production) on an mbarrier nothing arrives at, with the given limit
