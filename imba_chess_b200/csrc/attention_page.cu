@@ -60,8 +60,8 @@ constexpr int kPageBytes = IMBA_PAGE_TOKENS * 128;            // 16 tokens x 64 
 constexpr size_t kSmemMax = 227 * 1024;                       // dynamic shared memory per CTA
 constexpr int kMaxStages = 8;
 constexpr int kMetaBytes = 8192;
-constexpr int kEpiWarps = 3;                                 // norm / gate warps of the fused epilogue
-constexpr int kMaxThreads = (2 * kMaxHC + 1 + kEpiWarps) * 32;
+constexpr int kEpiWarps = 2;                                 // norm / gate warps of the fused epilogue
+constexpr int kMaxThreads = (2 * kMaxHC + 2 + kEpiWarps) * 32;
 
 // Item buffer (int32 words): header, then per-row arrays.
 constexpr int kItN = 0;        // rows in the item (-1: no more items)
@@ -73,7 +73,10 @@ constexpr int kItXoff = 104;   // [32] first extra of the row
 constexpr int kItXcnt = 136;   // [32] extras of the row
 constexpr int kItX0slot = 168; // [32] pool slot of the row's first extra (-1: none)
 constexpr int kItX0pos = 200;  // [32] its position
-constexpr int kItemInts = 232;
+constexpr int kItPg0 = 2;      // first entry of the group's page list
+constexpr int kItPages = 232;  // [kItMaxPages] the item's first page ids
+constexpr int kItMaxPages = 64;
+constexpr int kItemInts = kItPages + kItMaxPages;
 
 struct PageParams {
   AttnArgs a;
@@ -396,17 +399,15 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
   }
   __syncthreads();
 
-  if (warp == ncw) {
-    // ---------------- producer ----------------
-    const int64_t num_pages = a.g.num_slots / IMBA_PAGE_TOKENS;
+  if (warp == ncw + 1) {
+    // ---------------- resolver: claims items, fills item buffers and query tiles ----------------
     const bf16* Q = static_cast<const bf16*>(a.q);
     int* ctr = a.counters + blockIdx.z;
     int next_c = 0;
     if (lane == 0) next_c = atomicAdd(ctr, 1);
     int c = 0, half = 0, nhalves = 0, off0 = 0, n_chunk = 0, pg0 = 0, cap = 0;
-    int it = 0, pc = 0;
-    bool waited = false;  // griddepcontrol.wait done (queries and pages may come from the previous kernel)
-    while (true) {
+    bool waited = false;  // griddepcontrol.wait done (queries may come from the previous kernel)
+    for (int it = 0;; ++it) {
       if (++half >= nhalves) {  // claim the next non-empty chunk
         half = 0;
         nhalves = 0;
@@ -446,7 +447,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       if (it >= 2) {  // consumers and norm warps release a buffer (item metadata and queries)
         int ok = 1;
         if (lane == 0) ok = wait_bar(&item_empty[ib], ((it >> 1) - 1) & 1, st.status, abort_flag);
-        if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+        if (!__shfl_sync(0xffffffffu, ok, 0)) {
+          asm volatile("cp.async.wait_all;\n" ::: "memory");
+          return;
+        }
       }
       if (c >= st.num_chunks) {
         if (lane == 0) {
@@ -502,13 +506,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         item[kItX0slot + lane] = slot0;
         item[kItX0pos + lane] = pos0;
       }
+      // the first kItMaxPages page ids (the streaming warp loads any others itself)
+      for (int p = lane; p < npg && p < kItMaxPages; p += 32) item[kItPages + p] = st.group_pages[pg0 + p];
       if (lane == 0) {
         item[kItN] = n;
         item[kItNpg] = npg;
+        item[kItPg0] = pg0;
       }
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&item_full[ib]);
-      // Queries and pages may have been written by the preceding kernels.
+      // Queries may have been written by the preceding kernels.
       if (!waited) {
         pdl_wait();
         waited = true;
@@ -532,11 +539,27 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(tc::smem_u32(&q_full[ib]))
                      : "memory");
       }
-      // Stream the visible pages through the ring.
+    }
+  }
+
+  if (warp == ncw) {
+    // ---------------- page streamer: each item's visible KV pages through the ring ----------------
+    const int64_t num_pages = a.g.num_slots / IMBA_PAGE_TOKENS;
+    int pc = 0;
+    pdl_wait();  // the pages may hold KV written by the preceding projection kernel
+    for (int it = 0;; ++it) {
+      const int ib = it & 1;
+      const int* item = items + ib * kItemInts;
+      int ok = 1;
+      if (lane == 0) ok = wait_bar(&item_full[ib], (it >> 1) & 1, st.status, abort_flag);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+      const int n = item[kItN];
+      if (n < 0) return;
+      const int npg = item[kItNpg], pg0 = item[kItPg0];
       for (int b0 = 0; b0 < npg; b0 += 32) {
         int pg = 0;
         if (b0 + lane < npg) {
-          pg = st.group_pages[pg0 + b0 + lane];
+          pg = b0 + lane < kItMaxPages ? item[kItPages + b0 + lane] : st.group_pages[pg0 + b0 + lane];
           if (pg < 0 || pg >= num_pages) {
             report(st.status, IMBA_ERR_RANGE);
             pg = 0;
@@ -545,11 +568,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         const int cnt2 = npg - b0 < 32 ? npg - b0 : 32;
         for (int k = 0; k < cnt2; ++k) {
           const int page = __shfl_sync(0xffffffffu, pg, k);
-          int ok = 1;
+          int ok2 = 1;
           if (lane == 0) {
             const int s = pc % S;
-            if (pc >= S) ok = wait_bar(&empty[s], ((pc / S) - 1) & 1, st.status, abort_flag);
-            if (ok) {
+            if (pc >= S) ok2 = wait_bar(&empty[s], ((pc / S) - 1) & 1, st.status, abort_flag);
+            if (ok2) {
               uint8_t* dst = ring + s * stage_bytes;
               const int rowK = ((page * prm.num_layers + a.layer) * 2 * H + h0) * IMBA_PAGE_TOKENS;
               const int rowV = rowK + H * IMBA_PAGE_TOKENS;
@@ -558,23 +581,19 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
               tc::tma_load_2d(dst + HC * kPageBytes, &kvmap, &full[s], 0, rowV);
             }
           }
-          if (!__shfl_sync(0xffffffffu, ok, 0)) {
-            asm volatile("cp.async.wait_all;\n" ::: "memory");
-            return;
-          }
+          if (!__shfl_sync(0xffffffffu, ok2, 0)) return;
           ++pc;
         }
       }
-      ++it;
     }
   }
 
-  if (warp > ncw) {
+  if (warp > ncw + 1) {
     // ---------------- norm / gate warps (fused epilogue) ----------------
     // LayerNorm over each row's H dv attention outputs (no affine, eps 1e-6)
     // times u, stored in bf16 for the output projection; lane l owns columns
     // 128 k + 4 l .. +3 (k < 4) of a row; warp e takes rows e, e + nepi, ...
-    const int ew = warp - ncw - 1;
+    const int ew = warp - ncw - 2;
     const int ld = otile_ld(hdv);
     auto col_ok = [&](int k) { return 128 * k + 4 * lane < hdv; };
     pdl_wait();  // u comes from the preceding projection kernel
@@ -930,7 +949,7 @@ bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& 
   PageParams prm{a, num_layers, hc, (int)stages, u, fuse ? gated : nullptr};
   const int ctas = a.st.num_chunks < sms ? a.st.num_chunks : sms;
   dim3 grid(ctas, 1, H / hc);
-  *err = launch_pdl(kern, grid, dim3((2 * hc + 1 + (fuse ? kEpiWarps : 0)) * 32), smem, s, map, prm);
+  *err = launch_pdl(kern, grid, dim3((2 * hc + 2 + (fuse ? kEpiWarps : 0)) * 32), smem, s, map, prm);
   *fused = fuse && *err == cudaSuccess;
   return true;
 }
