@@ -5,27 +5,21 @@
 // Persistent: one CTA per SM (per head group when H > 8) pulls work items
 // from a per-layer atomic counter.  An item is <= 32 query rows of one
 // sequence group (a chunk; a 64-row chunk is two items) and HC heads (all of
-// them when H <= 8).  Warp roles, every hand-off an mbarrier:
+// them when H <= 8).  Warp roles:
 //   * the producer warp (index 2 HC) claims the next chunk, resolves its
 //     rows' metadata (row ids, visible prefix, query positions, extra-key
-//     offsets and the first extra key's slot) into one of two item buffers,
-//     copies the item's query tile (cp.async, one lane per row, arrival
-//     tracked on q_full) into one of two swizzled query buffers, then
-//     streams the group's visible KV pages: per 16-token page two TMA tiled
-//     loads (K rows of the HC heads, then their V rows: [HC x 16, 64] bf16
-//     with the 128-byte swizzle) into a ring of stages with one "full"
-//     (transaction bytes) and one "empty" (one arrive per consumer warp)
-//     mbarrier per stage.  It runs ahead into the next item while the
-//     consumers finish the current one, so an item's metadata, queries and
-//     first pages arrive under the previous item's math.
+//     offsets and the first extra tile's owners) into one of two item
+//     buffers, then streams the group's visible KV pages: per 16-token page
+//     two TMA tiled loads (K rows of the HC heads, then their V rows:
+//     [HC x 16, 64] bf16 with the 128-byte swizzle) into a ring of stages
+//     with one "full" (transaction bytes) and one "empty" (one arrive per
+//     consumer warp) mbarrier per stage.  It runs ahead into the next item
+//     while the consumers finish the current one, so the metadata and page
+//     latency of an item overlaps the previous item's math.
 //   * consumer warps 0 .. 2 HC - 1: warp w owns local head w / 2 and query
-//     rows 16 (w % 2) .. +15 of the item, reading its queries per page from
-//     the query buffer with ldmatrix (registers hold only the softmax state
-//     and O).
-//   * with every head in the CTA, kEpiWarps norm / gate warps: LayerNorm of
-//     each row's H dv outputs and the u gate, from the O tile the consumers
-//     leave in shared memory, so the consumers go straight on to the next
-//     item.
+//     rows 16 (w % 2) .. +15 of the item.  The item's queries are staged
+//     once in a swizzled shared tile (cp.async) and read per page with
+//     ldmatrix, which keeps a warp's registers to its softmax state and O.
 // Every page is read from HBM once per item and serves every sibling row and
 // every head.  Per page a consumer warp computes S = Q K^T (mma.sync
 // m16n8k16, fp32 accumulate), scales it, adds the relative-position bias
@@ -36,11 +30,11 @@
 // per row afterwards: the four lanes that share a row split the 64-dim dot
 // product (a quad reduction), update the row's online softmax and add p v to
 // their O columns, reading K / V straight from the pool.
-// Epilogue: O / l, rounded to bf16 (the reference's bf16 attention output
-// is bf16 too) into the O tile; the norm warps take whole rows: LayerNorm
-// over the row's H dv outputs (no affine, eps 1e-6, warp reductions) times
-// u, stored in bf16 for the output projection.  With more than 8 heads a CTA
-// holds a head group: fp32 O is stored and the gate runs as its own pass.
+// Epilogue: O / l; when the CTA holds every head, O is staged in shared
+// memory and after one barrier each warp takes whole rows: LayerNorm over the
+// row's H dv outputs (no affine, eps 1e-6, warp reductions) times u, stored
+// in bf16 for the output projection; otherwise fp32 O is stored and the gate
+// runs as its own pass.
 // Every wait is bounded; a timeout sets the status word and ends the CTA.
 // Semantics: src/imba_chess/model/hstu_attention.py :64-76, :81-132,
 // :134-148, :327-413 (attention), :185-190 (norm and gate).
@@ -60,8 +54,7 @@ constexpr int kPageBytes = IMBA_PAGE_TOKENS * 128;            // 16 tokens x 64 
 constexpr size_t kSmemMax = 227 * 1024;                       // dynamic shared memory per CTA
 constexpr int kMaxStages = 8;
 constexpr int kMetaBytes = 8192;
-constexpr int kEpiWarps = 2;                                 // norm / gate warps of the fused epilogue
-constexpr int kMaxThreads = (2 * kMaxHC + 2 + kEpiWarps) * 32;
+constexpr int kMaxThreads = (2 * kMaxHC + 1) * 32;
 
 // Item buffer (int32 words): header, then per-row arrays.
 constexpr int kItN = 0;        // rows in the item (-1: no more items)
@@ -73,10 +66,7 @@ constexpr int kItXoff = 104;   // [32] first extra of the row
 constexpr int kItXcnt = 136;   // [32] extras of the row
 constexpr int kItX0slot = 168; // [32] pool slot of the row's first extra (-1: none)
 constexpr int kItX0pos = 200;  // [32] its position
-constexpr int kItPg0 = 2;      // first entry of the group's page list
-constexpr int kItPages = 232;  // [kItMaxPages] the item's first page ids
-constexpr int kItMaxPages = 64;
-constexpr int kItemInts = kItPages + kItMaxPages;
+constexpr int kItemInts = 232;
 
 struct PageParams {
   AttnArgs a;
@@ -87,10 +77,10 @@ struct PageParams {
   bf16* gated;    // [R, H dv]: fused norm + gate output (nullptr: store fp32 O to a.out)
 };
 
-// Row stride (bf16) of the staged O tile: 8 values of padding keep the
-// per-lane 4-byte writes of eight different rows in different banks.
-__host__ __device__ constexpr int otile_ld(int hdv) { return hdv + 8; }
-__host__ __device__ constexpr int otile_bytes(int hdv) { return (kHalfRows * otile_ld(hdv) * 2 + 15) / 16 * 16; }
+// Row stride (floats) of the staged O tile: 4 floats of padding keep the
+// per-lane float2 writes of eight different rows in different banks.
+__host__ __device__ constexpr int otile_ld(int hdv) { return hdv + 4; }
+__host__ __device__ constexpr int otile_bytes(int hdv) { return kHalfRows * otile_ld(hdv) * 4; }
 
 __device__ __forceinline__ int bias_index(int kpos, int qpos, int max_pos) {
   int idx = kpos - qpos + (max_pos - 1);
@@ -280,32 +270,23 @@ __device__ __forceinline__ void step16(RowState& rs, uint32_t qb, uint32_t kb, u
   }
 }
 
-// One extra key's K and V as this lane's slice: K dims 16 t .. 16 t + 15
-// (two 16-byte loads) and V columns 8 j + 2 t, +1 (j < 8).
-struct ExtraKV {
-  uint4 k[2];
-  uint32_t v[8];
-};
-
-__device__ __forceinline__ void extra_load(ExtraKV& x, bool active, const bf16* kp, const bf16* vp, int t) {
-  x.k[0] = x.k[1] = make_uint4(0, 0, 0, 0);
-  if (active) {
-    x.k[0] = __ldg(reinterpret_cast<const uint4*>(kp + 16 * t));
-    x.k[1] = __ldg(reinterpret_cast<const uint4*>(kp + 16 * t + 8));
-  }
-#pragma unroll
-  for (int j = 0; j < 8; ++j) x.v[j] = active ? __ldg(reinterpret_cast<const uint32_t*>(vp + 8 * j + 2 * t)) : 0u;
-}
-
-// Fold one extra key (loaded by extra_load) into one row's online softmax.
+// Fold one extra key (pool slot, position) into one row's online softmax.
 // The row's four lanes (t = 0..3) each take 16 of the 64 dims of q . k and
 // reduce across the quad; ol / oh: this lane's O columns 8 j + 2 t, +1 of the
 // row.  active is uniform across the quad.
 template <class Bias>
-__device__ __forceinline__ void extra_apply(float& m, float& l, float (&o)[8][4], int ci, bool active, uint32_t qrow,
-                                            int qrow_sw, const ExtraKV& x, int kpos, int qpos, const Bias& psw,
-                                            float scale2, int max_pos, int t) {
+__device__ __forceinline__ void extra_key(float& m, float& l, float (&o)[8][4], int ci, bool active, uint32_t qrow,
+                                          int qrow_sw, const bf16* kp, const bf16* vp, int kpos, int qpos,
+                                          const Bias& psw, float scale2, int max_pos, int t) {
   float part = 0.f;
+  uint4 kv[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+  if (active) {
+    kv[0] = __ldg(reinterpret_cast<const uint4*>(kp + 16 * t));
+    kv[1] = __ldg(reinterpret_cast<const uint4*>(kp + 16 * t + 8));
+  }
+  uint32_t vv[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) vv[j] = active ? __ldg(reinterpret_cast<const uint32_t*>(vp + 8 * j + 2 * t)) : 0u;
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
     uint4 qv;
@@ -313,7 +294,7 @@ __device__ __forceinline__ void extra_apply(float& m, float& l, float (&o)[8][4]
                  : "=r"(qv.x), "=r"(qv.y), "=r"(qv.z), "=r"(qv.w)
                  : "r"(qrow + (uint32_t)(((2 * t + c) ^ qrow_sw) << 4)));
     const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
-    const uint32_t kw[4] = {x.k[c].x, x.k[c].y, x.k[c].z, x.k[c].w};
+    const uint32_t kw[4] = {kv[c].x, kv[c].y, kv[c].z, kv[c].w};
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const float2 qf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qw[w]));
@@ -332,16 +313,10 @@ __device__ __forceinline__ void extra_apply(float& m, float& l, float (&o)[8][4]
   l = fmaf(l, c, t == 0 ? p : 0.f);  // the quad's partial sums: one lane counts the key
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const float2 vf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&x.v[j]));
+    const float2 vf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vv[j]));
     o[j][2 * ci] = fmaf(o[j][2 * ci], c, p * vf.x);
     o[j][2 * ci + 1] = fmaf(o[j][2 * ci + 1], c, p * vf.y);
   }
-}
-
-// Bounded wait on one of the kernel's mbarriers; false (abort flag set, or
-// the wait ran out and recorded IMBA_ERR_TIMEOUT) tells the caller to leave.
-__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int32_t* status, volatile int* abort) {
-  return tc::mbar_wait_or_abort(bar, parity, status, abort);
 }
 
 template <bool kSmemBias>
@@ -350,26 +325,23 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
   const AttnArgs& a = prm.a;
   const imba_step_desc& st = a.st;
   const int HC = prm.hc, S = prm.stages;
-  const bool fused = prm.gated != nullptr;
   const int ncw = 2 * HC, nct = ncw * 32;  // consumer warps (head, row block) / threads
-  const int nepi = fused ? kEpiWarps : 0;  // norm / gate warps
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int H = a.g.H;
   constexpr int D = 64;
   const int hdv = H * D;
   const int h0 = blockIdx.z * HC;
   const int stage_bytes = 2 * HC * kPageBytes;
-  const int q_bytes = HC * kHalfRows * 128;  // one item's query tile
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = base;                                    // S stages: [K: HC x 2 KB][V: HC x 2 KB]
-  uint8_t* qtile = ring + S * stage_bytes;                 // [2][HC][32 rows][128 B] queries, 128-byte swizzle
+  uint8_t* qtile = ring + S * stage_bytes;                 // [HC][32 rows][128 B] queries, 128-byte swizzle
   const int bias_w = 2 * a.max_pos - 1;                    // ps_w row length
-  // Fused epilogue: the item's O [32 rows][H dv + 8] bf16, staged for the norm warps.
-  bf16* otile = reinterpret_cast<bf16*>(qtile + 2 * q_bytes);
-  const int otile_size = fused ? otile_bytes(hdv) : 0;
-  __half* bias_s = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(otile) + otile_size);  // [HC][bias_w]
+  // Fused epilogue: the item's O [32 rows][H dv + 4] fp32, staged.
+  float* otile = reinterpret_cast<float*>(qtile + HC * kHalfRows * 128);
+  const int otile_size = prm.gated ? otile_bytes(hdv) : 0;
+  __half* bias_s = reinterpret_cast<__half*>(qtile + HC * kHalfRows * 128 + otile_size);  // [HC][bias_w] (kSmemBias)
   const int bias_bytes = kSmemBias ? (HC * bias_w * 2 + 15) / 16 * 16 : 0;
   int* items = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bias_s) + bias_bytes);  // [2][kItemInts]
   int* misc = items + 2 * kItemInts;                       // [0] abort flag, [1] pad
@@ -377,9 +349,6 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
   uint64_t* empty = full + kMaxStages;
   uint64_t* item_full = empty + kMaxStages;
   uint64_t* item_empty = item_full + 2;
-  uint64_t* q_full = item_empty + 2;
-  uint64_t* o_full = q_full + 2;
-  uint64_t* o_empty = o_full + 1;
   volatile int* abort_flag = misc;
 
   if (tid == 0) {
@@ -389,25 +358,22 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&item_full[b], 1);
-      tc::mbar_init(&item_empty[b], ncw + nepi);  // consumers and norm warps release an item buffer
-      tc::mbar_init(&q_full[b], 32);              // one cp.async-tracked arrival per producer lane
+      tc::mbar_init(&item_empty[b], ncw);
     }
-    tc::mbar_init(o_full, ncw);
-    tc::mbar_init(o_empty, nepi > 0 ? nepi : 1);
     misc[0] = 0;
     tc::fence_mbar_init();
   }
   __syncthreads();
 
-  if (warp == ncw + 1) {
-    // ---------------- resolver: claims items, fills item buffers and query tiles ----------------
-    const bf16* Q = static_cast<const bf16*>(a.q);
+  if (warp == ncw) {
+    // ---------------- producer ----------------
+    const int64_t num_pages = a.g.num_slots / IMBA_PAGE_TOKENS;
     int* ctr = a.counters + blockIdx.z;
     int next_c = 0;
     if (lane == 0) next_c = atomicAdd(ctr, 1);
     int c = 0, half = 0, nhalves = 0, off0 = 0, n_chunk = 0, pg0 = 0, cap = 0;
-    bool waited = false;  // griddepcontrol.wait done (queries may come from the previous kernel)
-    for (int it = 0;; ++it) {
+    int it = 0, pc = 0;
+    while (true) {
       if (++half >= nhalves) {  // claim the next non-empty chunk
         half = 0;
         nhalves = 0;
@@ -444,20 +410,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       }
       const int ib = it & 1;
       int* item = items + ib * kItemInts;
-      if (it >= 2) {  // consumers and norm warps release a buffer (item metadata and queries)
+      if (it >= 2) {  // the consumers release a buffer after the item's epilogue
         int ok = 1;
-        if (lane == 0) ok = wait_bar(&item_empty[ib], ((it >> 1) - 1) & 1, st.status, abort_flag);
-        if (!__shfl_sync(0xffffffffu, ok, 0)) {
-          asm volatile("cp.async.wait_all;\n" ::: "memory");
-          return;
-        }
+        if (lane == 0) ok = tc::mbar_wait_or_abort(&item_empty[ib], ((it >> 1) - 1) & 1, st.status, abort_flag);
+        if (!__shfl_sync(0xffffffffu, ok, 0)) return;
       }
       if (c >= st.num_chunks) {
         if (lane == 0) {
           item[kItN] = -1;
           tc::mbar_arrive(&item_full[ib]);
         }
-        asm volatile("cp.async.wait_all;\n" ::: "memory");
         return;
       }
       // Rows of this item, one lane per row.
@@ -506,60 +468,19 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         item[kItX0slot + lane] = slot0;
         item[kItX0pos + lane] = pos0;
       }
-      // the first kItMaxPages page ids (the streaming warp loads any others itself)
-      for (int p = lane; p < npg && p < kItMaxPages; p += 32) item[kItPages + p] = st.group_pages[pg0 + p];
       if (lane == 0) {
         item[kItN] = n;
         item[kItNpg] = npg;
-        item[kItPg0] = pg0;
       }
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&item_full[ib]);
-      // Queries may have been written by the preceding kernels.
-      if (!waited) {
-        pdl_wait();
-        waited = true;
-      }
-      // This item's query tile: lane = row; rows past n are zero.  The tile's
-      // arrival is tracked on q_full[ib] (one arrival per lane once its copies land).
-      {
-        const uint32_t qt = tc::smem_u32(qtile) + ib * q_bytes;
-        for (int hh = 0; hh < HC; ++hh) {
-          const uint32_t dst = qt + hh * (kHalfRows * 128);
-#pragma unroll
-          for (int c8 = 0; c8 < 8; ++c8) {
-            const uint32_t d8 = dst + blk_off(lane, c8);
-            // rows past n are zero-filled by the copy itself (source size 0)
-            const bf16* src = Q + (lane < n ? (size_t)r * (H * D) + (h0 + hh) * D + 8 * c8 : 0);
-            const uint32_t nbytes = lane < n ? 16u : 0u;
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d8), "l"(src), "r"(nbytes)
-                         : "memory");
-          }
-        }
-        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(tc::smem_u32(&q_full[ib]))
-                     : "memory");
-      }
-    }
-  }
-
-  if (warp == ncw) {
-    // ---------------- page streamer: each item's visible KV pages through the ring ----------------
-    const int64_t num_pages = a.g.num_slots / IMBA_PAGE_TOKENS;
-    int pc = 0;
-    pdl_wait();  // the pages may hold KV written by the preceding projection kernel
-    for (int it = 0;; ++it) {
-      const int ib = it & 1;
-      const int* item = items + ib * kItemInts;
-      int ok = 1;
-      if (lane == 0) ok = wait_bar(&item_full[ib], (it >> 1) & 1, st.status, abort_flag);
-      if (!__shfl_sync(0xffffffffu, ok, 0)) return;
-      const int n = item[kItN];
-      if (n < 0) return;
-      const int npg = item[kItNpg], pg0 = item[kItPg0];
+      // The pages may hold KV written by the preceding projection kernel.
+      pdl_wait();
+      // Stream the visible pages through the ring.
       for (int b0 = 0; b0 < npg; b0 += 32) {
         int pg = 0;
         if (b0 + lane < npg) {
-          pg = b0 + lane < kItMaxPages ? item[kItPages + b0 + lane] : st.group_pages[pg0 + b0 + lane];
+          pg = st.group_pages[pg0 + b0 + lane];
           if (pg < 0 || pg >= num_pages) {
             report(st.status, IMBA_ERR_RANGE);
             pg = 0;
@@ -568,11 +489,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         const int cnt2 = npg - b0 < 32 ? npg - b0 : 32;
         for (int k = 0; k < cnt2; ++k) {
           const int page = __shfl_sync(0xffffffffu, pg, k);
-          int ok2 = 1;
+          int ok = 1;
           if (lane == 0) {
             const int s = pc % S;
-            if (pc >= S) ok2 = wait_bar(&empty[s], ((pc / S) - 1) & 1, st.status, abort_flag);
-            if (ok2) {
+            if (pc >= S) ok = tc::mbar_wait_or_abort(&empty[s], ((pc / S) - 1) & 1, st.status, abort_flag);
+            if (ok) {
               uint8_t* dst = ring + s * stage_bytes;
               const int rowK = ((page * prm.num_layers + a.layer) * 2 * H + h0) * IMBA_PAGE_TOKENS;
               const int rowV = rowK + H * IMBA_PAGE_TOKENS;
@@ -581,93 +502,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
               tc::tma_load_2d(dst + HC * kPageBytes, &kvmap, &full[s], 0, rowV);
             }
           }
-          if (!__shfl_sync(0xffffffffu, ok2, 0)) return;
+          if (!__shfl_sync(0xffffffffu, ok, 0)) return;
           ++pc;
         }
       }
-    }
-  }
-
-  if (warp > ncw + 1) {
-    // ---------------- norm / gate warps (fused epilogue) ----------------
-    // LayerNorm over each row's H dv attention outputs (no affine, eps 1e-6)
-    // times u, stored in bf16 for the output projection; lane l owns columns
-    // 128 k + 4 l .. +3 (k < 4) of a row; warp e takes rows e, e + nepi, ...
-    const int ew = warp - ncw - 2;
-    const int ld = otile_ld(hdv);
-    auto col_ok = [&](int k) { return 128 * k + 4 * lane < hdv; };
-    pdl_wait();  // u comes from the preceding projection kernel
-    for (int it = 0;; ++it) {
-      const int ib = it & 1;
-      const int* item = items + ib * kItemInts;
-      if (!wait_bar(&item_full[ib], (it >> 1) & 1, st.status, abort_flag)) return;
-      const int n = item[kItN];
-      if (n < 0) return;
-      // u of this warp's first row, loaded before O is ready
-      uint2 un[4];
-      {
-        const int gr = ew < n ? item[kItRows + ew] : -1;
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          un[k] = (gr >= 0 && col_ok(k)) ? __ldg(reinterpret_cast<const uint2*>(prm.u + (size_t)gr * hdv + 128 * k +
-                                                                                   4 * lane))
-                                         : make_uint2(0u, 0u);
-      }
-      if (!wait_bar(o_full, it & 1, st.status, abort_flag)) return;
-      for (int rr = ew; rr < n; rr += nepi) {
-        const int gr = item[kItRows + rr];
-        uint2 ur[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) ur[k] = un[k];
-        const int rn = rr + nepi;  // next row of this warp: its u load overlaps this row
-        const int grn = rn < n ? item[kItRows + rn] : -1;
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          un[k] = (grn >= 0 && col_ok(k)) ? __ldg(reinterpret_cast<const uint2*>(prm.u + (size_t)grn * hdv +
-                                                                                    128 * k + 4 * lane))
-                                          : make_uint2(0u, 0u);
-        float v[4][4];
-        float sum = 0.f;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          if (col_ok(k)) {
-            const uint2 w = *reinterpret_cast<const uint2*>(otile + rr * ld + 128 * k + 4 * lane);
-            const float2 a01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
-            const float2 a23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
-            v[k][0] = a01.x;
-            v[k][1] = a01.y;
-            v[k][2] = a23.x;
-            v[k][3] = a23.y;
-          } else {
-            v[k][0] = v[k][1] = v[k][2] = v[k][3] = 0.f;
-          }
-          sum += (v[k][0] + v[k][1]) + (v[k][2] + v[k][3]);
-        }
-        const float mu = warp_sum(sum) / (float)hdv;
-        float sq = 0.f;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          if (col_ok(k))
-#pragma unroll
-            for (int e = 0; e < 4; ++e) sq += (v[k][e] - mu) * (v[k][e] - mu);
-        }
-        const float rsd = 1.0f / sqrtf(warp_sum(sq) / (float)hdv + 1e-6f);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          if (!col_ok(k)) continue;
-          const float2 u01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ur[k].x));
-          const float2 u23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ur[k].y));
-          uint2 o;
-          o.x = pack_bf16(u01.x * ((v[k][0] - mu) * rsd), u01.y * ((v[k][1] - mu) * rsd));
-          o.y = pack_bf16(u23.x * ((v[k][2] - mu) * rsd), u23.y * ((v[k][3] - mu) * rsd));
-          *reinterpret_cast<uint2*>(prm.gated + (size_t)gr * hdv + 128 * k + 4 * lane) = o;
-        }
-      }
-      __syncwarp();
-      if (lane == 0) {
-        tc::mbar_arrive(o_empty);          // the O tile may be overwritten
-        tc::mbar_arrive(&item_empty[ib]);  // done with the item's metadata
-      }
+      ++it;
     }
   }
 
@@ -688,11 +527,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       for (int k = 0; k < 8; ++k)
         if (base + k < total) bias_s[base + k] = __float2half_rn(v[k] * kLog2e);
     }
-    bar_consumers(nct);  // the table is complete before any warp reads it
+    // visible to every consumer warp after the first item's barrier
   }
   // The bias table (weights) and the producer's first item (host-written step
-  // metadata) overlap the previous kernel; the rows' own K / V and the
-  // outputs are ordered after it.
+  // metadata) overlap the previous kernel; queries, u, the rows' own K / V
+  // and the outputs are ordered after it.
   pdl_wait();
   pdl_trigger();
   using Bias = typename std::conditional<kSmemBias, BiasShared, BiasGlobal>::type;
@@ -700,13 +539,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
   if constexpr (kSmemBias) psw.p = bias_s + (size_t)hl * bias_w;
   else psw.p = a.ps_w + (size_t)h * bias_w;
   const bf16* Pool = static_cast<const bf16*>(a.pool);
+  const bf16* Q = static_cast<const bf16*>(a.q);
   const uint32_t ring_base = tc::smem_u32(ring), qtb = tc::smem_u32(qtile);
+  const uint32_t qb = qtb + hl * (kHalfRows * 128) + rb * (16 * 128);  // this warp's 16 query rows
 
   int pc = 0;
   for (int it = 0;; ++it) {
     const int ib = it & 1;
     const int* item = items + ib * kItemInts;
-    const bool ok_item = __all_sync(0xffffffffu, wait_bar(&item_full[ib], (it >> 1) & 1, st.status, abort_flag));
+    const bool ok_item =
+        __all_sync(0xffffffffu, tc::mbar_wait_or_abort(&item_full[ib], (it >> 1) & 1, st.status, abort_flag));
     if (bar_consumers_or(nct, !ok_item)) {
       *abort_flag = 1;
       return;
@@ -714,7 +556,19 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     const int n = item[kItN];
     if (n < 0) return;
     const int npg = item[kItNpg];
-    const uint32_t qb = qtb + ib * q_bytes + hl * (kHalfRows * 128) + rb * (16 * 128);  // this warp's 16 rows
+    // Query tile of the item: row r, head hh, 16-byte chunk c8 (rows past n are zero).
+    for (int idx = tid; idx < kHalfRows * HC * 8; idx += nct) {
+      const int c8 = idx & 7, rest = idx >> 3;
+      const int hh = rest % HC, row = rest / HC;
+      const uint32_t dst = qtb + hh * (kHalfRows * 128) + blk_off(row, c8);
+      if (row < n) {
+        const bf16* src = Q + (size_t)item[kItRows + row] * (H * D) + (h0 + hh) * D + 8 * c8;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+      } else {
+        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};\n" ::"r"(dst), "r"(0u) : "memory");
+      }
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
     // Bring the K / V lines of each row's first extra key (usually the row
     // itself, written by the preceding projection) into L1 while the pages
     // stream: lane t of a quad takes (row rl0 | rl1) x (K | V).
@@ -744,17 +598,18 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     int wvis = max(vis0, vis1);  // pages past every row of this warp are skipped
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) wvis = max(wvis, __shfl_xor_sync(0xffffffffu, wvis, o));
-    // the item's query tile (copied by the producer)
-    bool aborted = !__all_sync(0xffffffffu, wait_bar(&q_full[ib], (it >> 1) & 1, st.status, abort_flag));
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    bar_consumers(nct);  // the query tile is complete
     RowState rs;
 #pragma unroll
     for (int j = 0; j < 8; ++j) rs.o[j][0] = rs.o[j][1] = rs.o[j][2] = rs.o[j][3] = 0.f;
     rs.m0 = rs.m1 = -INFINITY;
     rs.l0 = rs.l1 = 0.f;
 
-    for (int p = 0; p < npg && !aborted; ++p, ++pc) {
+    bool aborted = false;
+    for (int p = 0; p < npg; ++p, ++pc) {
       const int s = pc % S;
-      const bool ok = __all_sync(0xffffffffu, wait_bar(&full[s], (pc / S) & 1, st.status, abort_flag));
+      const bool ok = __all_sync(0xffffffffu, tc::mbar_wait_or_abort(&full[s], (pc / S) & 1, st.status, abort_flag));
       if (!ok) {
         aborted = true;
         break;
@@ -776,6 +631,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     // decision to stop is uniform and no warp waits at a later barrier.
     if (bar_consumers_or(nct, aborted)) {
       *abort_flag = 1;
+      asm volatile("cp.async.wait_all;\n" ::: "memory");
       return;  // the status word already holds the timeout
     }
     // Extra keys, per row: the suffix chain and the row itself.
@@ -787,46 +643,32 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       for (int o = 4; o < 32; o <<= 1) emax = max(emax, __shfl_xor_sync(0xffffffffu, emax, o));
       const uint32_t qr0 = qb + g * 128, qr1 = qb + (g + 8) * 128;  // rows rl0, rl1 of the query tile
       for (int e = 0; e < emax; ++e) {
-        int kpos[2] = {0, 0}, slot[2] = {-1, -1};
 #pragma unroll
         for (int ci = 0; ci < 2; ++ci) {
           const int cnt = ci ? c1 : c0;
+          int slot = -1, kpos = 0;
           if (e == 0) {  // resolved (and range-checked) by the producer
             const int rl = ci ? rl1 : rl0;
             if (cnt > 0) {
-              slot[ci] = item[kItX0slot + rl];
-              kpos[ci] = item[kItX0pos + rl];
+              slot = item[kItX0slot + rl];
+              kpos = item[kItX0pos + rl];
             }
           } else if (e < cnt) {
             const int xi = (ci ? o1 : o0) + e;
-            slot[ci] = st.extra_slot[xi];
-            kpos[ci] = st.extra_pos[xi];
-            if (slot[ci] < 0 || slot[ci] >= a.g.num_slots) {
+            slot = st.extra_slot[xi];
+            kpos = st.extra_pos[xi];
+            if (slot < 0 || slot >= a.g.num_slots) {
               report(st.status, IMBA_ERR_RANGE);
-              slot[ci] = -1;
+              slot = -1;
             }
           }
-        }
-        // Both rows' K / V lines move towards L1 together (lane t of a quad:
-        // row rl0 | rl1 by t & 1, K | V by t & 2), so the second row's loads
-        // below do not wait a second memory round trip.
-        {
-          const int sl = slot[t & 1];
-          if (sl >= 0) {
-            const bf16* ln = Pool + ((t & 2) ? a.g.v_off(sl, a.layer, h) : a.g.k_off(sl, a.layer, h));
-            asm volatile("prefetch.global.L1 [%0];" ::"l"(ln));
-          }
-        }
-#pragma unroll
-        for (int ci = 0; ci < 2; ++ci) {
-          const bool act = slot[ci] >= 0;
-          ExtraKV x;
-          extra_load(x, act, Pool + (act ? a.g.k_off(slot[ci], a.layer, h) : 0),
-                     Pool + (act ? a.g.v_off(slot[ci], a.layer, h) : 0), t);
+          const bool act = slot >= 0;
+          const bf16* kp = Pool + (act ? a.g.k_off(slot, a.layer, h) : 0);
+          const bf16* vp = Pool + (act ? a.g.v_off(slot, a.layer, h) : 0);
           if (ci == 0)
-            extra_apply(rs.m0, rs.l0, rs.o, 0, act, qr0, g & 7, x, kpos[0], qp0, psw, scale2, a.max_pos, t);
+            extra_key(rs.m0, rs.l0, rs.o, 0, act, qr0, g & 7, kp, vp, kpos, qp0, psw, scale2, a.max_pos, t);
           else
-            extra_apply(rs.m1, rs.l1, rs.o, 1, act, qr1, (g + 8) & 7, x, kpos[1], qp1, psw, scale2, a.max_pos, t);
+            extra_key(rs.m1, rs.l1, rs.o, 1, act, qr1, (g + 8) & 7, kp, vp, kpos, qp1, psw, scale2, a.max_pos, t);
         }
       }
     }
@@ -844,8 +686,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       rs.o[j][2] *= i1;
       rs.o[j][3] *= i1;
     }
-    if (!fused) {
-      const int r0 = rl0 < n ? item[kItRows + rl0] : -1, r1 = rl1 < n ? item[kItRows + rl1] : -1;
+    const int r0 = rl0 < n ? item[kItRows + rl0] : -1, r1 = rl1 < n ? item[kItRows + rl1] : -1;
+    if (prm.gated == nullptr) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int col = h * D + 8 * j + 2 * t;
@@ -853,24 +695,72 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         if (r1 >= 0) *reinterpret_cast<float2*>(a.out + (size_t)r1 * hdv + col) = make_float2(rs.o[j][2], rs.o[j][3]);
       }
     } else {
-      // O (rounded to bf16, as the reference's bf16 attention output is) to the
-      // staged tile once the norm warps have read the previous item's.  A
-      // failed wait has set the abort flag: the warp skips the tile and
-      // leaves through the next item's uniform abort vote.
-      if (it == 0 || __all_sync(0xffffffffu, wait_bar(o_empty, (it - 1) & 1, st.status, abort_flag))) {
-        const int ld = otile_ld(hdv);
+      // LayerNorm over the row's H dv outputs, then the gate by u: O goes to
+      // the shared O tile, and after one barrier each warp normalises whole
+      // rows (2 of the 32) with warp reductions; u and the gated output move
+      // as coalesced 8-byte pieces.  The u loads are issued first.
+      // Lane l owns columns 128 k + 4 l .. +3 (k < 4) of a row; warp w
+      // normalises rows w, w + 2 HC, ... (two rows when HC = 8).
+      const int ld = otile_ld(hdv);
+      auto col_ok = [&](int k) { return 128 * k + 4 * lane < hdv; };
+      uint2 uw[2][4];  // u of this warp's first two rows, loaded before the barrier
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int col = hl * D + 8 * j + 2 * t;
-          *reinterpret_cast<uint32_t*>(otile + rl0 * ld + col) = pack_bf16(rs.o[j][0], rs.o[j][1]);
-          *reinterpret_cast<uint32_t*>(otile + rl1 * ld + col) = pack_bf16(rs.o[j][2], rs.o[j][3]);
+      for (int i = 0; i < 2; ++i) {
+        const int rr = warp + i * ncw;
+        const int gr = rr < n ? item[kItRows + rr] : -1;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          uw[i][k] = (gr >= 0 && col_ok(k))
+                         ? __ldg(reinterpret_cast<const uint2*>(prm.u + (size_t)gr * hdv + 128 * k + 4 * lane))
+                         : make_uint2(0u, 0u);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int col = hl * D + 8 * j + 2 * t;
+        *reinterpret_cast<float2*>(otile + rl0 * ld + col) = make_float2(rs.o[j][0], rs.o[j][1]);
+        *reinterpret_cast<float2*>(otile + rl1 * ld + col) = make_float2(rs.o[j][2], rs.o[j][3]);
+      }
+      bar_consumers(nct);
+      for (int i = 0, rr = warp; rr < n; ++i, rr += ncw) {
+        const int gr = item[kItRows + rr];
+        uint2 ur[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          ur[k] = i < 2 ? (i ? uw[1][k] : uw[0][k])
+                        : (col_ok(k) ? __ldg(reinterpret_cast<const uint2*>(prm.u + (size_t)gr * hdv + 128 * k +
+                                                                            4 * lane))
+                                     : make_uint2(0u, 0u));
+        float4 v[4];
+        float sum = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          v[k] = col_ok(k) ? *reinterpret_cast<const float4*>(otile + rr * ld + 128 * k + 4 * lane)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+          sum += (v[k].x + v[k].y) + (v[k].z + v[k].w);
         }
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(o_full);
+        const float mu = warp_sum(sum) / (float)hdv;
+        float sq = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (col_ok(k))
+            sq += (v[k].x - mu) * (v[k].x - mu) + (v[k].y - mu) * (v[k].y - mu) + (v[k].z - mu) * (v[k].z - mu) +
+                  (v[k].w - mu) * (v[k].w - mu);
+        }
+        const float rsd = 1.0f / sqrtf(warp_sum(sq) / (float)hdv + 1e-6f);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (!col_ok(k)) continue;
+          const float2 u01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ur[k].x));
+          const float2 u23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ur[k].y));
+          uint2 o;
+          o.x = pack_bf16(u01.x * ((v[k].x - mu) * rsd), u01.y * ((v[k].y - mu) * rsd));
+          o.y = pack_bf16(u23.x * ((v[k].z - mu) * rsd), u23.y * ((v[k].w - mu) * rsd));
+          *reinterpret_cast<uint2*>(prm.gated + (size_t)gr * hdv + 128 * k + 4 * lane) = o;
+        }
       }
     }
     __syncwarp();
-    if (lane == 0) tc::mbar_arrive(&item_empty[ib]);  // this warp is done with the item buffer and queries
+    if (lane == 0) tc::mbar_arrive(&item_empty[ib]);  // this warp is done with the item buffer
   }
 }
 
@@ -930,7 +820,7 @@ bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& 
   // table, item buffers and barriers.  The bias table is
   // kept in shared memory when at least 3 ring stages still fit.
   const size_t stage_bytes = 2 * (size_t)hc * kPageBytes;
-  const size_t fixed = 1024 + 2 * (size_t)hc * kHalfRows * 128 + (fuse ? (size_t)otile_bytes(H * 64) : 0) + kMetaBytes;
+  const size_t fixed = 1024 + (size_t)hc * kHalfRows * 128 + (fuse ? (size_t)otile_bytes(H * 64) : 0) + kMetaBytes;
   const size_t bias_bytes = ((size_t)hc * (2 * md.max_pos - 1) * 2 + 15) / 16 * 16;
   const bool smem_bias = fixed + bias_bytes + 3 * stage_bytes <= kSmemMax;
   size_t stages = (kSmemMax - fixed - (smem_bias ? bias_bytes : 0)) / stage_bytes;
@@ -949,7 +839,7 @@ bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& 
   PageParams prm{a, num_layers, hc, (int)stages, u, fuse ? gated : nullptr};
   const int ctas = a.st.num_chunks < sms ? a.st.num_chunks : sms;
   dim3 grid(ctas, 1, H / hc);
-  *err = launch_pdl(kern, grid, dim3((2 * hc + 2 + (fuse ? kEpiWarps : 0)) * 32), smem, s, map, prm);
+  *err = launch_pdl(kern, grid, dim3((2 * hc + 1) * 32), smem, s, map, prm);
   *fused = fuse && *err == cudaSuccess;
   return true;
 }
