@@ -46,6 +46,8 @@ size_t workspace_layout(const imba_model* m, int32_t rows, void* base, Workspace
   w.logits = static_cast<float*>(take(R * d.vocab * 4));
   w.pooled = take(d.dtype == IMBA_DTYPE_BF16 ? R * 3 * IMBA_BOARD_DIM * 2 : 0);
   w.counters = static_cast<int*>(take(kNumCounters * sizeof(int)));
+  // paged attention work items: at most one chunk per row, two records per chunk
+  w.recs = static_cast<int*>(take(d.dtype == IMBA_DTYPE_BF16 ? 2 * R * kAttnRecInts * sizeof(int) : 0));
   w.bytes = off;
   if (ws) *ws = w;
   return off;
@@ -92,6 +94,7 @@ imba_status_t validate_step(const imba_model* m, const imba_step_desc* st, const
       st->num_group_pages < 0)
     return IMBA_ERR_ARG;
   if (st->num_rows == 0) return IMBA_OK;
+  if (st->num_chunks > st->num_rows) return IMBA_ERR_ARG;  // every chunk holds at least one row
   if (!pool->base || pool->num_pages <= 0) return IMBA_ERR_ARG;
   if (reinterpret_cast<uintptr_t>(pool->base) & 255) return IMBA_ERR_ARG;  // TMA views need aligned bases
   if (pool->num_pages > (int64_t)INT32_MAX / IMBA_PAGE_TOKENS) return IMBA_ERR_RANGE;
@@ -138,6 +141,9 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
 
   IMBA_CK(pm.mark(s));
   IMBA_CK(cudaMemsetAsync(w.counters, 0, kNumCounters * sizeof(int), s));
+  // The paged attention's work items, resolved once for every layer.
+  const bool paged_attn = md.dtype == IMBA_DTYPE_BF16 && !m->simt_attn;
+  if (paged_attn) IMBA_CK(launch_attn_items(st, g, w.recs, s));
   // bf16 handles run the tensor-core kernels; a launcher that declines
   // (returns false) is an error unless a SIMT test hook selected the SIMT
   // kernel of that component (imba_model_desc.flags).
@@ -176,8 +182,8 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
                 w.counters + l * kCountersPerLayer};
     bool fused = false;
     bf16* gated_bf = std::is_same<T, bf16>::value ? reinterpret_cast<bf16*>(w.gated) : nullptr;
-    if (m->simt_attn || !launch_attn_page(aa, md.num_layers, md, pool.num_pages, static_cast<const bf16*>(w.u),
-                                          gated_bf, s, &e, &fused)) {
+    if (!paged_attn || !launch_attn_page(aa, md.num_layers, md, pool.num_pages, static_cast<const bf16*>(w.u),
+                                         gated_bf, w.recs, s, &e, &fused)) {
       if (md.dtype == IMBA_DTYPE_BF16 && !m->simt_attn) return IMBA_ERR_UNSUPPORTED;
       IMBA_CK(launch_attn_simt<T>(aa, s));
     } else if (e != cudaSuccess) {

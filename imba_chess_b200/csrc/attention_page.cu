@@ -2,39 +2,47 @@
 // models, d_qk = d_v = 64), with the attention-output LayerNorm and the u
 // gate fused into its epilogue.
 //
-// Persistent: one CTA per SM (per head group when H > 8) pulls work items
-// from a per-layer atomic counter.  An item is <= 32 query rows of one
-// sequence group (a chunk; a 64-row chunk is two items) and HC heads (all of
-// them when H <= 8).  Warp roles:
-//   * the producer warp (index 2 HC) claims the next chunk, resolves its
-//     rows' metadata (row ids, visible prefix, query positions, extra-key
-//     offsets and the first extra tile's owners) into one of two item
-//     buffers, then streams the group's visible KV pages: per 16-token page
-//     two TMA tiled loads (K rows of the HC heads, then their V rows:
-//     [HC x 16, 64] bf16 with the 128-byte swizzle) into a ring of stages
-//     with one "full" (transaction bytes) and one "empty" (one arrive per
-//     consumer warp) mbarrier per stage.  It runs ahead into the next item
-//     while the consumers finish the current one, so the metadata and page
-//     latency of an item overlaps the previous item's math.
+// Work items.  An item is <= 32 query rows of one chunk (a 64-row chunk is
+// two items) and HC heads (all of them when H <= 8).  Once per step the item
+// pass (attn_items_kernel) resolves every item's metadata into one record of
+// kAttnRecInts words: row ids, visible prefix lengths, query positions,
+// extra-key offsets and counts, the first extra key's slot and position, and
+// the group's first page ids.  Every layer's attention then fetches a record
+// with one bulk copy instead of a chain of dependent global loads.
+//
+// The attention kernel is persistent: one CTA per SM (per head group when
+// H > 8) pulls chunks from a per-layer atomic counter.  Warp roles, every
+// hand-off an mbarrier or a named barrier:
+//   * the producer warp (index 2 HC) claims a chunk when the previous item's
+//     pages are all issued, bulk-copies its record into one of four item
+//     buffers and streams the item's visible KV pages: per 16-token page two TMA tiled
+//     loads (K rows of the HC heads, then their V rows: [HC x 16, 64] bf16
+//     with the 128-byte swizzle) into a ring of stages with one "full"
+//     (transaction bytes) and one "empty" (one arrive per consumer warp)
+//     mbarrier per stage.  It runs ahead into the next item while the
+//     consumers finish the current one.
 //   * consumer warps 0 .. 2 HC - 1: warp w owns local head w / 2 and query
-//     rows 16 (w % 2) .. +15 of the item.  The item's queries are staged
-//     once in a swizzled shared tile (cp.async) and read per page with
-//     ldmatrix, which keeps a warp's registers to its softmax state and O.
+//     rows 16 (w % 2) .. +15 of the item.  The queries sit in one of two
+//     swizzled shared tiles: while an item's pages are done, the consumers
+//     copy the next item's queries (cp.async) into the other tile, so an
+//     item starts with its queries in place.  Per page a warp computes
+//     S = Q K^T (mma.sync m16n8k16, fp32 accumulate; Q fragments by
+//     ldmatrix), scales it, adds the relative-position bias
+//     ps_w[h, clamp(k - q + max - 1)], masks keys beyond each row's visible
+//     prefix, updates the fp32 online softmax in registers and accumulates
+//     O += P V.  The rows' extra keys (each row's suffix chain and the row
+//     itself: scattered arena slots, usually one to a few per row) are folded
+//     in afterwards: the four lanes that share a row split the 64-dim dot
+//     product (a quad reduction), update the row's online softmax and add
+//     p v to their O columns, reading K / V straight from the pool.
 // Every page is read from HBM once per item and serves every sibling row and
-// every head.  Per page a consumer warp computes S = Q K^T (mma.sync
-// m16n8k16, fp32 accumulate), scales it, adds the relative-position bias
-// ps_w[h, clamp(k - q + max - 1)], masks keys beyond each row's visible
-// prefix, updates the fp32 online softmax in registers and accumulates
-// O += P V.  The rows' extra keys (each row's suffix chain and the row
-// itself: scattered arena slots, usually one to a few per row) are folded in
-// per row afterwards: the four lanes that share a row split the 64-dim dot
-// product (a quad reduction), update the row's online softmax and add p v to
-// their O columns, reading K / V straight from the pool.
-// Epilogue: O / l; when the CTA holds every head, O is staged in shared
-// memory and after one barrier each warp takes whole rows: LayerNorm over the
-// row's H dv outputs (no affine, eps 1e-6, warp reductions) times u, stored
-// in bf16 for the output projection; otherwise fp32 O is stored and the gate
-// runs as its own pass.
+// every head.
+// Epilogue: O / l.  With every head in the CTA, O (rounded to bf16, as the
+// reference's bf16 attention output is) overwrites the warp's own query rows
+// in the tile, and after one barrier each warp takes whole rows: LayerNorm
+// over the row's H dv outputs (no affine, eps 1e-6, warp reductions) times u,
+// stored in bf16 for the output projection.  With more than 8 heads fp32 O
+// is stored and the gate runs as its own pass.
 // Every wait is bounded; a timeout sets the status word and ends the CTA.
 // Semantics: src/imba_chess/model/hstu_attention.py :64-76, :81-132,
 // :134-148, :327-413 (attention), :185-190 (norm and gate).
@@ -48,39 +56,43 @@
 namespace imba {
 namespace {
 
-constexpr int kHalfRows = 32;                                 // query rows per item
-constexpr int kMaxHC = 8;                                     // heads per CTA
-constexpr int kPageBytes = IMBA_PAGE_TOKENS * 128;            // 16 tokens x 64 bf16 of one head
-constexpr size_t kSmemMax = 227 * 1024;                       // dynamic shared memory per CTA
+constexpr int kHalfRows = 32;                          // query rows per item
+constexpr int kMaxHC = 8;                              // heads per CTA
+constexpr int kPageBytes = IMBA_PAGE_TOKENS * 128;     // 16 tokens x 64 bf16 of one head
+constexpr int kHeadTile = kHalfRows * 128;             // one head's 32 query / O rows (bytes)
+constexpr size_t kSmemMax = 227 * 1024;                // dynamic shared memory per CTA
 constexpr int kMaxStages = 8;
-constexpr int kMetaBytes = 8192;
+constexpr int kItemBufs = 4;
 constexpr int kMaxThreads = (2 * kMaxHC + 1) * 32;
 
-// Item buffer (int32 words): header, then per-row arrays.
-constexpr int kItN = 0;        // rows in the item (-1: no more items)
-constexpr int kItNpg = 1;      // visible pages (ceil of the longest row's prefix / 16)
-constexpr int kItRows = 8;     // [32] global row ids
-constexpr int kItVis = 40;     // [32] visible prefix tokens
-constexpr int kItQpos = 72;    // [32] query positions
-constexpr int kItXoff = 104;   // [32] first extra of the row
-constexpr int kItXcnt = 136;   // [32] extras of the row
-constexpr int kItX0slot = 168; // [32] pool slot of the row's first extra (-1: none)
-constexpr int kItX0pos = 200;  // [32] its position
-constexpr int kItemInts = 232;
+// Item record (int32 words; kAttnRecInts * 4 bytes, a multiple of 16).
+constexpr int kRecN = 0;        // rows in the item (0: nothing to do; -1 in a buffer: no more items)
+constexpr int kRecNpg = 1;      // visible pages (ceil of the longest row's prefix / 16)
+constexpr int kRecPg0 = 2;      // first entry of the group's page list
+constexpr int kRecHalves = 3;   // items of the chunk (record of its first half)
+constexpr int kRecRows = 8;     // [32] global row ids
+constexpr int kRecVis = 40;     // [32] visible prefix tokens
+constexpr int kRecQpos = 72;    // [32] query positions
+constexpr int kRecXoff = 104;   // [32] first extra of the row
+constexpr int kRecXcnt = 136;   // [32] extras of the row
+constexpr int kRecX0slot = 168; // [32] pool slot of the row's first extra (-1: none)
+constexpr int kRecX0pos = 200;  // [32] its position
+constexpr int kRecPages = 232;  // [kRecMaxPages] the group's first page ids
+constexpr int kRecMaxPages = 64;
+constexpr uint32_t kRecBytes = kAttnRecInts * 4;
+static_assert(kRecPages + kRecMaxPages == kAttnRecInts, "record layout");
+static_assert(kRecBytes % 16 == 0, "bulk copies move multiples of 16 bytes");
+constexpr int kRows = kHalfRows;
 
 struct PageParams {
   AttnArgs a;
   int num_layers;
-  int hc;         // heads per CTA
+  int hc;            // heads per CTA
   int stages;
-  const bf16* u;  // [R, H dv]
-  bf16* gated;    // [R, H dv]: fused norm + gate output (nullptr: store fp32 O to a.out)
+  const bf16* u;     // [R, H dv]
+  bf16* gated;       // [R, H dv]: fused norm + gate output (nullptr: store fp32 O to a.out)
+  const int* recs;   // [2 C][kAttnRecInts]: record c = chunk c's first 32 rows, C + c its second
 };
-
-// Row stride (floats) of the staged O tile: 4 floats of padding keep the
-// per-lane float2 writes of eight different rows in different banks.
-__host__ __device__ constexpr int otile_ld(int hdv) { return hdv + 4; }
-__host__ __device__ constexpr int otile_bytes(int hdv) { return kHalfRows * otile_ld(hdv) * 4; }
 
 __device__ __forceinline__ int bias_index(int kpos, int qpos, int max_pos) {
   int idx = kpos - qpos + (max_pos - 1);
@@ -112,8 +124,9 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t saddr) {
                : "r"(saddr));
 }
 
-// Byte offset of (token t < 16, 16-byte chunk j of its 128-byte row) in one
-// head's 2 KB page block, 128-byte swizzle (blocks start 1024-aligned).
+// Byte offset of (row t, 16-byte chunk j of its 128-byte row) in a tile of
+// 128-byte rows with the 128-byte swizzle (tiles start 1024-aligned): a
+// page's 16 K or V rows of one head, or a head's 32 query / O rows.
 __device__ __forceinline__ uint32_t blk_off(int t, int j) { return (uint32_t)(t * 128 + ((j ^ (t & 7)) << 4)); }
 
 __device__ __forceinline__ void bar_consumers(int nthreads) {
@@ -150,11 +163,26 @@ __device__ __forceinline__ float exp2_approx(float x) {  // hardware ex2; 2^-inf
 struct BiasShared {
   const __half* p;
   __device__ __forceinline__ float operator()(int idx) const { return __half2float(p[idx]); }
+  // entries idx and idx + 1 (one 4-byte load when idx is even: rows start
+  // 4-byte aligned)
+  __device__ __forceinline__ float2 pair(int idx) const {
+    if (idx & 1) return make_float2(__half2float(p[idx]), __half2float(p[idx + 1]));
+    return __half22float2(*reinterpret_cast<const __half2*>(p + idx));
+  }
 };
 struct BiasGlobal {
   const float* p;
   __device__ __forceinline__ float operator()(int idx) const { return __ldg(p + idx) * kLog2e; }
+  __device__ __forceinline__ float2 pair(int idx) const {
+    return make_float2(__ldg(p + idx) * kLog2e, __ldg(p + idx + 1) * kLog2e);
+  }
 };
+
+// The online softmax keeps a reference max per row and rescales O and the
+// row sums only when a score exceeds it by more than 2^kLazyLog2: weights
+// are then at most 2^kLazyLog2 (exact in the fp32 sums and in bf16 P), and
+// most pages skip the cross-lane max and the rescale.
+constexpr float kLazyLog2 = 8.0f;
 
 // Running softmax state of one 16-row block for this lane's two rows
 // (16 b + g and 16 b + g + 8, g = lane / 4).  l0 / l1 are this lane's
@@ -168,14 +196,25 @@ struct RowState {
 // Scale / bias / mask one 16-row x 16-key score block, update the online
 // softmax of its rows and return P as the bf16 A fragment of P V.
 // Keys are prefix tokens t0 .. t0 + 15; kFast: every key is visible to both
-// rows and no bias index needs clamping (the common case of a full page).
+// rows and no bias index needs clamping (the common case of a full page);
+// kUni (with kFast): the warp's rows share one query position, so the four
+// bias values of this lane's key columns serve both rows.
 // scale2 = scale * log2(e).
-template <bool kFast, class Bias>
+template <bool kFast, bool kUni, class Bias>
 __device__ __forceinline__ void softmax16(RowState& rs, float (&sc)[2][4], uint32_t (&pa)[4], int t0, int vis0,
                                           int vis1, int qp0, int qp1, const Bias& psw, float scale2, int max_pos,
                                           int t) {
-  float mx0 = -INFINITY, mx1 = -INFINITY;
-  if (kFast) {
+  if (kFast && kUni) {
+    const int b0 = t0 - qp0 + max_pos - 1 + 2 * t;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const float2 bp = psw.pair(b0 + 8 * nt);
+      sc[nt][0] = fmaf(sc[nt][0], scale2, bp.x);
+      sc[nt][1] = fmaf(sc[nt][1], scale2, bp.y);
+      sc[nt][2] = fmaf(sc[nt][2], scale2, bp.x);
+      sc[nt][3] = fmaf(sc[nt][3], scale2, bp.y);
+    }
+  } else if (kFast) {
     const int b0 = t0 - qp0 + max_pos - 1 + 2 * t, b1 = t0 - qp1 + max_pos - 1 + 2 * t;
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
@@ -183,8 +222,6 @@ __device__ __forceinline__ void softmax16(RowState& rs, float (&sc)[2][4], uint3
       for (int e = 0; e < 2; ++e) {
         sc[nt][e] = fmaf(sc[nt][e], scale2, psw(b0 + 8 * nt + e));
         sc[nt][2 + e] = fmaf(sc[nt][2 + e], scale2, psw(b1 + 8 * nt + e));
-        mx0 = fmaxf(mx0, sc[nt][e]);
-        mx1 = fmaxf(mx1, sc[nt][2 + e]);
       }
     }
   } else {
@@ -196,20 +233,35 @@ __device__ __forceinline__ void softmax16(RowState& rs, float (&sc)[2][4], uint3
         const bool v0 = kpos < vis0, v1 = kpos < vis1;
         sc[nt][e] = v0 ? fmaf(sc[nt][e], scale2, psw(bias_index(kpos, qp0, max_pos))) : -INFINITY;
         sc[nt][2 + e] = v1 ? fmaf(sc[nt][2 + e], scale2, psw(bias_index(kpos, qp1, max_pos))) : -INFINITY;
-        mx0 = fmaxf(mx0, sc[nt][e]);
-        mx1 = fmaxf(mx1, sc[nt][2 + e]);
       }
     }
   }
-  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-  const float mn0 = fmaxf(rs.m0, mx0), mn1 = fmaxf(rs.m1, mx1);
-  // A row with no visible key yet keeps max -inf; 0 stands in as the
-  // exponent base so that every weight (and the old state's factor) is 0.
-  const float ms0 = mn0 == -INFINITY ? 0.f : mn0, ms1 = mn1 == -INFINITY ? 0.f : mn1;
-  const float c0 = exp2_approx(rs.m0 - ms0), c1 = exp2_approx(rs.m1 - ms1);
+  float mx0 = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+  float mx1 = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
+  if (__any_sync(0xffffffffu, mx0 > rs.m0 + kLazyLog2 || mx1 > rs.m1 + kLazyLog2)) {
+    // New reference max (exact over the row's quad); O and the sums follow.
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(rs.m0, mx0), mn1 = fmaxf(rs.m1, mx1);
+    // A row with no visible key yet keeps max -inf; 0 stands in as the
+    // exponent base so that the old state's factor is 0.
+    const float c0 = exp2_approx(rs.m0 - (mn0 == -INFINITY ? 0.f : mn0));
+    const float c1 = exp2_approx(rs.m1 - (mn1 == -INFINITY ? 0.f : mn1));
+    rs.l0 *= c0;
+    rs.l1 *= c1;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      rs.o[j][0] *= c0;
+      rs.o[j][1] *= c0;
+      rs.o[j][2] *= c1;
+      rs.o[j][3] *= c1;
+    }
+    rs.m0 = mn0;
+    rs.m1 = mn1;
+  }
+  const float ms0 = rs.m0 == -INFINITY ? 0.f : rs.m0, ms1 = rs.m1 == -INFINITY ? 0.f : rs.m1;
   float ps0 = 0.f, ps1 = 0.f;
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt) {
@@ -221,20 +273,8 @@ __device__ __forceinline__ void softmax16(RowState& rs, float (&sc)[2][4], uint3
       ps1 += sc[nt][2 + e];
     }
   }
-  rs.l0 = fmaf(rs.l0, c0, ps0);
-  rs.l1 = fmaf(rs.l1, c1, ps1);
-  rs.m0 = mn0;
-  rs.m1 = mn1;
-  // Rescale O only when some row's running max moved (factor != 1).
-  if (!__all_sync(0xffffffffu, c0 == 1.f && c1 == 1.f)) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      rs.o[j][0] *= c0;
-      rs.o[j][1] *= c0;
-      rs.o[j][2] *= c1;
-      rs.o[j][3] *= c1;
-    }
-  }
+  rs.l0 += ps0;
+  rs.l1 += ps1;
   pa[0] = pack_bf16(sc[0][0], sc[0][1]);
   pa[1] = pack_bf16(sc[0][2], sc[0][3]);
   pa[2] = pack_bf16(sc[1][0], sc[1][1]);
@@ -243,7 +283,7 @@ __device__ __forceinline__ void softmax16(RowState& rs, float (&sc)[2][4], uint3
 
 // One 16-key block for the warp's 16 query rows: S = Q K^T (Q fragments
 // read from the shared Q tile with ldmatrix), softmax16, O += P V.
-template <bool kFast, class Bias>
+template <bool kFast, bool kUni, class Bias>
 __device__ __forceinline__ void step16(RowState& rs, uint32_t qb, uint32_t kb, uint32_t vb, int t0, int vis0,
                                        int vis1, int qp0, int qp1, const Bias& psw, float scale2, int max_pos,
                                        int lane) {
@@ -260,7 +300,7 @@ __device__ __forceinline__ void step16(RowState& rs, uint32_t qb, uint32_t kb, u
     mma16816(sc[1], qa, f[2], f[3]);
   }
   uint32_t pa[4];
-  softmax16<kFast, Bias>(rs, sc, pa, t0, vis0, vis1, qp0, qp1, psw, scale2, max_pos, t);
+  softmax16<kFast, kUni, Bias>(rs, sc, pa, t0, vis0, vis1, qp0, qp1, psw, scale2, max_pos, t);
 #pragma unroll
   for (int np = 0; np < 4; ++np) {
     uint32_t f[4];
@@ -319,12 +359,116 @@ __device__ __forceinline__ void extra_key(float& m, float& l, float (&o)[8][4], 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Item pass: one warp per record.  Record k < C: chunk k's rows 0..31;
+// record C + k: its rows 32..63 (n = 0 when the chunk has <= 32 rows).
+// Every index is range-checked here (IMBA_ERR_RANGE, clamped), so the
+// attention kernel trusts the records.
+__global__ void __launch_bounds__(128) attn_items_kernel(const imba_step_desc st, const PoolGeom g, int* recs) {
+  const int lane = threadIdx.x & 31;
+  const int k = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int C = st.num_chunks;
+  pdl_wait();
+  pdl_trigger();
+  if (k >= 2 * C) return;
+  const int c = k < C ? k : k - C, half = k < C ? 0 : 1;
+  int* rec = recs + (size_t)k * kAttnRecInts;
+  int v0 = 0;
+  if (lane == 0) v0 = st.chunk_group[c];
+  else if (lane == 1) v0 = st.chunk_row_off[c];
+  else if (lane == 2) v0 = st.chunk_nrows[c];
+  const int grp = __shfl_sync(0xffffffffu, v0, 0);
+  const int off0 = __shfl_sync(0xffffffffu, v0, 1);
+  int n_chunk = __shfl_sync(0xffffffffu, v0, 2);
+  int pg0 = 0, cap = 0;
+  if (grp < 0 || grp >= st.num_groups || n_chunk < 0 || n_chunk > IMBA_CHUNK_ROWS || off0 < 0 ||
+      off0 + n_chunk > st.num_rows) {
+    if (lane == 0) report(st.status, IMBA_ERR_RANGE);
+    n_chunk = 0;
+  } else {
+    int pv = 0;
+    if (lane < 2) pv = st.group_page_off[grp + lane];
+    pg0 = __shfl_sync(0xffffffffu, pv, 0);
+    const int pg1 = __shfl_sync(0xffffffffu, pv, 1);
+    if (pg0 < 0 || pg1 < pg0 || pg1 > st.num_group_pages) {
+      if (lane == 0) report(st.status, IMBA_ERR_RANGE);
+      pg0 = 0;
+    } else {
+      cap = (pg1 - pg0) * IMBA_PAGE_TOKENS;
+    }
+  }
+  int n = n_chunk - half * kRows;
+  n = n < 0 ? 0 : (n > kRows ? kRows : n);
+  const int off = off0 + half * kRows;
+  int r = -1, v = 0, qp = 0, e0 = 0, cnt = 0, slot0 = -1, pos0 = 0;
+  if (lane < n) {
+    r = st.row_perm[off + lane];
+    if (r < 0 || r >= st.num_rows) {
+      report(st.status, IMBA_ERR_RANGE);
+      r = 0;
+    }
+    v = st.row_vis[r];
+    qp = st.positions[r];
+    e0 = st.row_extra_off[r];
+    int e1 = st.row_extra_off[r + 1];
+    if (v < 0 || v > cap) {
+      report(st.status, IMBA_ERR_RANGE);
+      v = v < 0 ? 0 : cap;
+    }
+    if (e0 < 0 || e1 < e0 || e1 > st.num_extra) {
+      report(st.status, IMBA_ERR_RANGE);
+      e1 = e0 = 0;
+    }
+    cnt = e1 - e0;
+    if (cnt > 0) {
+      slot0 = st.extra_slot[e0];
+      pos0 = st.extra_pos[e0];
+      if (slot0 < 0 || slot0 >= g.num_slots) {
+        report(st.status, IMBA_ERR_RANGE);
+        slot0 = -1;
+      }
+    }
+  }
+  int vm = v;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) vm = max(vm, __shfl_xor_sync(0xffffffffu, vm, o));
+  const int npg = (vm + IMBA_PAGE_TOKENS - 1) / IMBA_PAGE_TOKENS;
+  const int64_t num_pages = g.num_slots / IMBA_PAGE_TOKENS;
+  rec[kRecRows + lane] = r;
+  rec[kRecVis + lane] = v;
+  rec[kRecQpos + lane] = qp;
+  rec[kRecXoff + lane] = e0;
+  rec[kRecXcnt + lane] = cnt;
+  rec[kRecX0slot + lane] = slot0;
+  rec[kRecX0pos + lane] = pos0;
+  for (int p = lane; p < kRecMaxPages; p += 32) {
+    int pg = 0;
+    if (p < npg) {
+      pg = st.group_pages[pg0 + p];
+      if (pg < 0 || pg >= num_pages) {
+        report(st.status, IMBA_ERR_RANGE);
+        pg = 0;
+      }
+    }
+    rec[kRecPages + p] = pg;
+  }
+  if (lane < 8) {
+    int h = 0;
+    if (lane == kRecN) h = n;
+    else if (lane == kRecNpg) h = npg;
+    else if (lane == kRecPg0) h = pg0;
+    else if (lane == kRecHalves) h = (n_chunk + kRows - 1) / kRows;
+    rec[lane] = h;
+  }
+}
+
 template <bool kSmemBias>
 __global__ void __launch_bounds__(kMaxThreads, 1)
     attn_page_kernel(const __grid_constant__ CUtensorMap kvmap, const PageParams prm) {
   const AttnArgs& a = prm.a;
   const imba_step_desc& st = a.st;
   const int HC = prm.hc, S = prm.stages;
+  const bool fused = prm.gated != nullptr;
   const int ncw = 2 * HC, nct = ncw * 32;  // consumer warps (head, row block) / threads
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int H = a.g.H;
@@ -332,23 +476,23 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
   const int hdv = H * D;
   const int h0 = blockIdx.z * HC;
   const int stage_bytes = 2 * HC * kPageBytes;
+  const int q_bytes = HC * kHeadTile;  // one query tile: [HC][32 rows][128 B]
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ring = base;                                    // S stages: [K: HC x 2 KB][V: HC x 2 KB]
-  uint8_t* qtile = ring + S * stage_bytes;                 // [HC][32 rows][128 B] queries, 128-byte swizzle
-  const int bias_w = 2 * a.max_pos - 1;                    // ps_w row length
-  // Fused epilogue: the item's O [32 rows][H dv + 4] fp32, staged.
-  float* otile = reinterpret_cast<float*>(qtile + HC * kHalfRows * 128);
-  const int otile_size = prm.gated ? otile_bytes(hdv) : 0;
-  __half* bias_s = reinterpret_cast<__half*>(qtile + HC * kHalfRows * 128 + otile_size);  // [HC][bias_w] (kSmemBias)
-  const int bias_bytes = kSmemBias ? (HC * bias_w * 2 + 15) / 16 * 16 : 0;
-  int* items = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bias_s) + bias_bytes);  // [2][kItemInts]
-  int* misc = items + 2 * kItemInts;                       // [0] abort flag, [1] pad
-  uint64_t* full = reinterpret_cast<uint64_t*>(misc + 2);           // 8-byte aligned: even int count precedes
+  uint8_t* ring = base;                                  // S stages: [K: HC x 2 KB][V: HC x 2 KB]
+  uint8_t* qtile = ring + S * stage_bytes;               // [2] query tiles, 128-byte swizzle
+  const int bias_w = 2 * a.max_pos - 1;                  // ps_w row length (odd)
+  const int bias_ld = bias_w + 1;                        // its row stride in shared memory: even, so that
+                                                         // pairs at even indices are 4-byte aligned
+  __half* bias_s = reinterpret_cast<__half*>(qtile + 2 * q_bytes);  // [HC][bias_ld] (kSmemBias)
+  const int bias_bytes = kSmemBias ? (HC * bias_ld * 2 + 15) / 16 * 16 : 0;
+  int* items = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bias_s) + bias_bytes);  // [kItemBufs][rec]
+  int* misc = items + kItemBufs * kAttnRecInts;          // [0] abort flag, [1] pad
+  uint64_t* full = reinterpret_cast<uint64_t*>(misc + 2);  // 8-byte aligned: even int count precedes
   uint64_t* empty = full + kMaxStages;
   uint64_t* item_full = empty + kMaxStages;
-  uint64_t* item_empty = item_full + 2;
+  uint64_t* item_empty = item_full + kItemBufs;
   volatile int* abort_flag = misc;
 
   if (tid == 0) {
@@ -356,7 +500,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], ncw);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kItemBufs; ++b) {
       tc::mbar_init(&item_full[b], 1);
       tc::mbar_init(&item_empty[b], ncw);
     }
@@ -367,133 +511,76 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
 
   if (warp == ncw) {
     // ---------------- producer ----------------
+    // Its j-th item goes to buffer j % kItemBufs.
     const int64_t num_pages = a.g.num_slots / IMBA_PAGE_TOKENS;
+    const int C = st.num_chunks;
     int* ctr = a.counters + blockIdx.z;
-    int next_c = 0;
-    if (lane == 0) next_c = atomicAdd(ctr, 1);
-    int c = 0, half = 0, nhalves = 0, off0 = 0, n_chunk = 0, pg0 = 0, cap = 0;
-    int it = 0, pc = 0;
+    // Every kernel of a step waits for its predecessor before it lets its
+    // dependents launch, so once this CTA runs, every kernel before the
+    // preceding one has completed: the item pass's records and the zeroed
+    // counters are readable now.  The pages hold KV of the preceding
+    // projection: the first page waits for it.
+    bool waited = false;
+    auto claim = [&]() {
+      int c = 0;
+      if (lane == 0) c = atomicAdd(ctr, 1);
+      return __shfl_sync(0xffffffffu, c, 0);
+    };
+    // lane 0: buffer of item j free again (item j - kItemBufs released by the consumers)
+    auto buffer_free = [&](int j) -> bool {
+      return j < kItemBufs ||
+             tc::mbar_wait_park_or_abort(&item_empty[j % kItemBufs], ((j / kItemBufs) - 1) & 1, st.status, abort_flag);
+    };
+    auto load_record = [&](int j, int rec) {  // lane 0
+      const int b = j % kItemBufs;
+      tc::mbar_arrive_expect_tx(&item_full[b], kRecBytes);
+      tc::bulk_load(items + b * kAttnRecInts, prm.recs + (size_t)rec * kAttnRecInts, kRecBytes, &item_full[b]);
+    };
+    auto put_end = [&](int j) {  // lane 0: no more items
+      const int b = j % kItemBufs;
+      items[b * kAttnRecInts + kRecN] = -1;
+      tc::mbar_arrive(&item_full[b]);
+    };
+    int c = claim();
+    if (c >= C) {
+      if (lane == 0) put_end(0);
+      return;
+    }
+    if (lane == 0) load_record(0, c);
+    int j = 0, pc = 0, half = 0;
     while (true) {
-      if (++half >= nhalves) {  // claim the next non-empty chunk
-        half = 0;
-        nhalves = 0;
-        while (true) {
-          c = __shfl_sync(0xffffffffu, next_c, 0);
-          if (c >= st.num_chunks) break;
-          if (lane == 0) next_c = atomicAdd(ctr, 1);  // consumed on the next claim
-          int v = 0;
-          if (lane == 0) v = st.chunk_group[c];
-          else if (lane == 1) v = st.chunk_row_off[c];
-          else if (lane == 2) v = st.chunk_nrows[c];
-          const int grp = __shfl_sync(0xffffffffu, v, 0);
-          off0 = __shfl_sync(0xffffffffu, v, 1);
-          n_chunk = __shfl_sync(0xffffffffu, v, 2);
-          if (grp < 0 || grp >= st.num_groups || n_chunk < 0 || n_chunk > IMBA_CHUNK_ROWS || off0 < 0 ||
-              off0 + n_chunk > st.num_rows) {
-            if (lane == 0) report(st.status, IMBA_ERR_RANGE);
-            continue;
-          }
-          int pv = 0;
-          if (lane < 2) pv = st.group_page_off[grp + lane];
-          pg0 = __shfl_sync(0xffffffffu, pv, 0);
-          const int pg1 = __shfl_sync(0xffffffffu, pv, 1);
-          if (pg0 < 0 || pg1 < pg0 || pg1 > st.num_group_pages) {
-            if (lane == 0) report(st.status, IMBA_ERR_RANGE);
-            pg0 = 0;
-            cap = 0;
-          } else {
-            cap = (pg1 - pg0) * IMBA_PAGE_TOKENS;
-          }
-          nhalves = (n_chunk + kHalfRows - 1) / kHalfRows;
-          if (nhalves > 0) break;
-        }
+      const int b = j % kItemBufs;
+      int ok = 1;
+      if (lane == 0) ok = tc::mbar_wait_park_or_abort(&item_full[b], (j / kItemBufs) & 1, st.status, abort_flag);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+      const int* item = items + b * kAttnRecInts;
+      const int npg = item[kRecNpg], pg0 = item[kRecPg0], nhalves = item[kRecHalves];
+      if (!waited) {
+        pdl_wait();
+        waited = true;
       }
-      const int ib = it & 1;
-      int* item = items + ib * kItemInts;
-      if (it >= 2) {  // the consumers release a buffer after the item's epilogue
-        int ok = 1;
-        if (lane == 0) ok = tc::mbar_wait_or_abort(&item_empty[ib], ((it >> 1) - 1) & 1, st.status, abort_flag);
-        if (!__shfl_sync(0xffffffffu, ok, 0)) return;
-      }
-      if (c >= st.num_chunks) {
-        if (lane == 0) {
-          item[kItN] = -1;
-          tc::mbar_arrive(&item_full[ib]);
-        }
-        return;
-      }
-      // Rows of this item, one lane per row.
-      const int n = n_chunk - half * kHalfRows < kHalfRows ? n_chunk - half * kHalfRows : kHalfRows;
-      const int off = off0 + half * kHalfRows;
-      int r = -1, v = 0, qp = 0, e0 = 0, cnt = 0;
-      if (lane < n) {
-        r = st.row_perm[off + lane];
-        if (r < 0 || r >= st.num_rows) {
-          report(st.status, IMBA_ERR_RANGE);
-          r = 0;
-        }
-        v = st.row_vis[r];
-        qp = st.positions[r];
-        e0 = st.row_extra_off[r];
-        int e1 = st.row_extra_off[r + 1];
-        if (v < 0 || v > cap) {
-          report(st.status, IMBA_ERR_RANGE);
-          v = v < 0 ? 0 : cap;
-        }
-        if (e0 < 0 || e1 < e0 || e1 > st.num_extra) {
-          report(st.status, IMBA_ERR_RANGE);
-          e1 = e0 = 0;
-        }
-        cnt = e1 - e0;
-      }
-      int vm = v;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) vm = max(vm, __shfl_xor_sync(0xffffffffu, vm, o));
-      const int npg = (vm + IMBA_PAGE_TOKENS - 1) / IMBA_PAGE_TOKENS;
-      item[kItRows + lane] = r;
-      item[kItVis + lane] = v;
-      item[kItQpos + lane] = qp;
-      item[kItXoff + lane] = e0;
-      item[kItXcnt + lane] = cnt;
-      {
-        int slot0 = -1, pos0 = 0;
-        if (cnt > 0) {
-          slot0 = st.extra_slot[e0];
-          pos0 = st.extra_pos[e0];
-          if (slot0 < 0 || slot0 >= a.g.num_slots) {
-            report(st.status, IMBA_ERR_RANGE);
-            slot0 = -1;
-          }
-        }
-        item[kItX0slot + lane] = slot0;
-        item[kItX0pos + lane] = pos0;
-      }
-      if (lane == 0) {
-        item[kItN] = n;
-        item[kItNpg] = npg;
-      }
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&item_full[ib]);
-      // The pages may hold KV written by the preceding projection kernel.
-      pdl_wait();
       // Stream the visible pages through the ring.
       for (int b0 = 0; b0 < npg; b0 += 32) {
         int pg = 0;
         if (b0 + lane < npg) {
-          pg = st.group_pages[pg0 + b0 + lane];
-          if (pg < 0 || pg >= num_pages) {
-            report(st.status, IMBA_ERR_RANGE);
-            pg = 0;
+          if (b0 + lane < kRecMaxPages) {
+            pg = item[kRecPages + b0 + lane];
+          } else {
+            pg = st.group_pages[pg0 + b0 + lane];
+            if (pg < 0 || pg >= num_pages) {
+              report(st.status, IMBA_ERR_RANGE);
+              pg = 0;
+            }
           }
         }
         const int cnt2 = npg - b0 < 32 ? npg - b0 : 32;
         for (int k = 0; k < cnt2; ++k) {
           const int page = __shfl_sync(0xffffffffu, pg, k);
-          int ok = 1;
+          int ok2 = 1;
           if (lane == 0) {
             const int s = pc % S;
-            if (pc >= S) ok = tc::mbar_wait_or_abort(&empty[s], ((pc / S) - 1) & 1, st.status, abort_flag);
-            if (ok) {
+            if (pc >= S) ok2 = tc::mbar_wait_park_or_abort(&empty[s], ((pc / S) - 1) & 1, st.status, abort_flag);
+            if (ok2) {
               uint8_t* dst = ring + s * stage_bytes;
               const int rowK = ((page * prm.num_layers + a.layer) * 2 * H + h0) * IMBA_PAGE_TOKENS;
               const int rowV = rowK + H * IMBA_PAGE_TOKENS;
@@ -502,11 +589,34 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
               tc::tma_load_2d(dst + HC * kPageBytes, &kvmap, &full[s], 0, rowV);
             }
           }
-          if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+          if (!__shfl_sync(0xffffffffu, ok2, 0)) return;
           ++pc;
         }
       }
-      ++it;
+      // The next chunk is claimed once this item's pages are all issued (the
+      // ring still holds up to S of them), so the longest-first queue hands
+      // out work as CTAs free up; its record travels while those pages are
+      // consumed.
+      int next = -1, next_half = 0;
+      if (half == 0 && nhalves > 1) {
+        next = C + c;
+        next_half = 1;
+      } else {
+        c = claim();
+        if (c < C) next = c;
+      }
+      ok = 1;
+      if (lane == 0) {
+        ok = buffer_free(j + 1);
+        if (ok) {
+          if (next >= 0) load_record(j + 1, next);
+          else put_end(j + 1);
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+      ++j;
+      half = next_half;
+      if (next < 0) return;  // item j is the end marker
     }
   }
 
@@ -519,62 +629,71 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     const int total = HC * bias_w;
     // Each thread loads 8 values before converting and storing them, so the
     // loads of a round are in flight together.
-    for (int base = tid * 8; base < total; base += nct * 8) {
+    for (int b = tid * 8; b < total; b += nct * 8) {
       float v[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) v[k] = base + k < total ? __ldg(src + base + k) : 0.f;
+      for (int k = 0; k < 8; ++k) v[k] = b + k < total ? __ldg(src + b + k) : 0.f;
 #pragma unroll
       for (int k = 0; k < 8; ++k)
-        if (base + k < total) bias_s[base + k] = __float2half_rn(v[k] * kLog2e);
+        if (b + k < total) bias_s[(b + k) / bias_w * bias_ld + (b + k) % bias_w] = __float2half_rn(v[k] * kLog2e);
     }
     // visible to every consumer warp after the first item's barrier
   }
-  // The bias table (weights) and the producer's first item (host-written step
-  // metadata) overlap the previous kernel; queries, u, the rows' own K / V
-  // and the outputs are ordered after it.
+  // The bias table (weights) overlaps the previous kernel; queries, u, the
+  // rows' own K / V and the outputs are ordered after it.
   pdl_wait();
   pdl_trigger();
   using Bias = typename std::conditional<kSmemBias, BiasShared, BiasGlobal>::type;
   Bias psw;
-  if constexpr (kSmemBias) psw.p = bias_s + (size_t)hl * bias_w;
+  if constexpr (kSmemBias) psw.p = bias_s + (size_t)hl * bias_ld;
   else psw.p = a.ps_w + (size_t)h * bias_w;
   const bf16* Pool = static_cast<const bf16*>(a.pool);
   const bf16* Q = static_cast<const bf16*>(a.q);
   const uint32_t ring_base = tc::smem_u32(ring), qtb = tc::smem_u32(qtile);
-  const uint32_t qb = qtb + hl * (kHalfRows * 128) + rb * (16 * 128);  // this warp's 16 query rows
+  const float scale2 = a.scale * kLog2e;
 
-  int pc = 0;
-  for (int it = 0;; ++it) {
-    const int ib = it & 1;
-    const int* item = items + ib * kItemInts;
-    const bool ok_item =
-        __all_sync(0xffffffffu, tc::mbar_wait_or_abort(&item_full[ib], (it >> 1) & 1, st.status, abort_flag));
-    if (bar_consumers_or(nct, !ok_item)) {
-      *abort_flag = 1;
-      return;
-    }
-    const int n = item[kItN];
-    if (n < 0) return;
-    const int npg = item[kItNpg];
-    // Query tile of the item: row r, head hh, 16-byte chunk c8 (rows past n are zero).
+  // Queries of an item (record rec, n rows) into query tile `tile`: row r,
+  // head hh, 16-byte chunk c8; rows past n are zero-filled by the copy
+  // itself (source size 0).  Consecutive threads read consecutive chunks of
+  // a row.
+  auto copy_queries = [&](const int* rec, int n, int tile) {
+    const uint32_t dst0 = qtb + tile * q_bytes;
     for (int idx = tid; idx < kHalfRows * HC * 8; idx += nct) {
       const int c8 = idx & 7, rest = idx >> 3;
       const int hh = rest % HC, row = rest / HC;
-      const uint32_t dst = qtb + hh * (kHalfRows * 128) + blk_off(row, c8);
-      if (row < n) {
-        const bf16* src = Q + (size_t)item[kItRows + row] * (H * D) + (h0 + hh) * D + 8 * c8;
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
-      } else {
-        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};\n" ::"r"(dst), "r"(0u) : "memory");
-      }
+      const bool live = row < n;
+      const bf16* src = Q + (live ? (size_t)rec[kRecRows + row] * (H * D) + (h0 + hh) * D + 8 * c8 : 0);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst0 + hh * kHeadTile + blk_off(row, c8)),
+                   "l"(src), "r"(live ? 16u : 0u)
+                   : "memory");
     }
     asm volatile("cp.async.commit_group;\n" ::: "memory");
+  };
+
+  // The first item's record and queries.
+  bool ok_next = __all_sync(0xffffffffu, tc::mbar_wait_park_or_abort(&item_full[0], 0, st.status, abort_flag));
+  if (ok_next && items[kRecN] > 0) copy_queries(items, items[kRecN], 0);
+  int pc = 0;
+  for (int j = 0;; ++j) {
+    const int b = j % kItemBufs, tile = j & 1;
+    const int* item = items + b * kAttnRecInts;
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    // The item's queries (and, at j = 0, the bias table) are visible to every
+    // consumer warp past this barrier; a failed record wait anywhere stops all.
+    if (bar_consumers_or(nct, !ok_next)) {
+      *abort_flag = 1;
+      return;
+    }
+    const int n = item[kRecN];
+    if (n < 0) return;
+    const int npg = item[kRecNpg];
+    const uint32_t qb = qtb + tile * q_bytes + hl * kHeadTile + rb * (16 * 128);  // this warp's 16 query rows
     // Bring the K / V lines of each row's first extra key (usually the row
     // itself, written by the preceding projection) into L1 while the pages
     // stream: lane t of a quad takes (row rl0 | rl1) x (K | V).
     {
       const int rl = (t & 1) ? rl1 : rl0;
-      const int slot = rl < n ? item[kItX0slot + rl] : -1;
+      const int slot = rl < n ? item[kRecX0slot + rl] : -1;
       if (slot >= 0) {
         const bf16* ln = Pool + ((t & 2) ? a.g.v_off(slot, a.layer, h) : a.g.k_off(slot, a.layer, h));
         asm volatile("prefetch.global.L1 [%0];" ::"l"(ln));
@@ -583,9 +702,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     const bool live = 16 * rb < n;
     // Rows past n mirror row 0 (never stored): they keep the fast path and
     // every bias index of a full page in range.
-    const int vis0 = item[kItVis + (rl0 < n ? rl0 : 0)], vis1 = item[kItVis + (rl1 < n ? rl1 : 0)];
-    const int qp0 = item[kItQpos + (rl0 < n ? rl0 : 0)], qp1 = item[kItQpos + (rl1 < n ? rl1 : 0)];
-    const float scale2 = a.scale * kLog2e;
+    const int vis0 = item[kRecVis + (rl0 < n ? rl0 : 0)], vis1 = item[kRecVis + (rl1 < n ? rl1 : 0)];
+    const int qp0 = item[kRecQpos + (rl0 < n ? rl0 : 0)], qp1 = item[kRecQpos + (rl1 < n ? rl1 : 0)];
     // Pages [fast_lo, fast_hi) are fully visible to every row of the warp and
     // need no bias-index clamping (warp-uniform bounds).
     int fast_lo = max(max(qp0, qp1) - a.max_pos + 1, 0);
@@ -595,21 +713,22 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       fast_lo = max(fast_lo, __shfl_xor_sync(0xffffffffu, fast_lo, o));
       fast_hi = min(fast_hi, __shfl_xor_sync(0xffffffffu, fast_hi, o));
     }
+    // The warp's rows share one query position (siblings of one parent).
+    const int qp_lane0 = __shfl_sync(0xffffffffu, qp0, 0);  // every lane takes part in the shuffle
+    const bool uni = __all_sync(0xffffffffu, qp0 == qp1 && qp0 == qp_lane0);
     int wvis = max(vis0, vis1);  // pages past every row of this warp are skipped
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) wvis = max(wvis, __shfl_xor_sync(0xffffffffu, wvis, o));
-    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
-    bar_consumers(nct);  // the query tile is complete
     RowState rs;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) rs.o[j][0] = rs.o[j][1] = rs.o[j][2] = rs.o[j][3] = 0.f;
+    for (int q = 0; q < 8; ++q) rs.o[q][0] = rs.o[q][1] = rs.o[q][2] = rs.o[q][3] = 0.f;
     rs.m0 = rs.m1 = -INFINITY;
     rs.l0 = rs.l1 = 0.f;
 
     bool aborted = false;
     for (int p = 0; p < npg; ++p, ++pc) {
       const int s = pc % S;
-      const bool ok = __all_sync(0xffffffffu, tc::mbar_wait_or_abort(&full[s], (pc / S) & 1, st.status, abort_flag));
+      const bool ok = __all_sync(0xffffffffu, tc::mbar_wait_park_or_abort(&full[s], (pc / S) & 1, st.status, abort_flag));
       if (!ok) {
         aborted = true;
         break;
@@ -617,12 +736,17 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       if (live && p * IMBA_PAGE_TOKENS < wvis) {
         const uint32_t kb = ring_base + s * stage_bytes + hl * kPageBytes;
         const int t0 = p * IMBA_PAGE_TOKENS;
-        if (t0 >= fast_lo && t0 + IMBA_PAGE_TOKENS <= fast_hi)
-          step16<true, Bias>(rs, qb, kb, kb + HC * kPageBytes, t0, vis0, vis1, qp0, qp1, psw, scale2, a.max_pos,
-                             lane);
-        else
-          step16<false, Bias>(rs, qb, kb, kb + HC * kPageBytes, t0, vis0, vis1, qp0, qp1, psw, scale2, a.max_pos,
-                              lane);
+        if (t0 >= fast_lo && t0 + IMBA_PAGE_TOKENS <= fast_hi) {
+          if (uni)
+            step16<true, true, Bias>(rs, qb, kb, kb + HC * kPageBytes, t0, vis0, vis1, qp0, qp1, psw, scale2,
+                                     a.max_pos, lane);
+          else
+            step16<true, false, Bias>(rs, qb, kb, kb + HC * kPageBytes, t0, vis0, vis1, qp0, qp1, psw, scale2,
+                                      a.max_pos, lane);
+        } else {
+          step16<false, false, Bias>(rs, qb, kb, kb + HC * kPageBytes, t0, vis0, vis1, qp0, qp1, psw, scale2,
+                                     a.max_pos, lane);
+        }
       }
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&empty[s]);
@@ -634,10 +758,20 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       asm volatile("cp.async.wait_all;\n" ::: "memory");
       return;  // the status word already holds the timeout
     }
+    // The next item's queries go into the other tile (its previous contents,
+    // the item before this one, were last read before this item's first
+    // barrier) while this item's extra keys and epilogue run.
+    {
+      const int jn = j + 1, bn = jn % kItemBufs;
+      ok_next = __all_sync(0xffffffffu,
+                           tc::mbar_wait_park_or_abort(&item_full[bn], (jn / kItemBufs) & 1, st.status, abort_flag));
+      const int nn = ok_next ? items[bn * kAttnRecInts + kRecN] : 0;
+      if (nn > 0) copy_queries(items + bn * kAttnRecInts, nn, jn & 1);
+    }
     // Extra keys, per row: the suffix chain and the row itself.
     {
-      const int c0 = rl0 < n ? item[kItXcnt + rl0] : 0, c1 = rl1 < n ? item[kItXcnt + rl1] : 0;
-      const int o0 = item[kItXoff + rl0], o1 = item[kItXoff + rl1];
+      const int c0 = rl0 < n ? item[kRecXcnt + rl0] : 0, c1 = rl1 < n ? item[kRecXcnt + rl1] : 0;
+      const int o0 = item[kRecXoff + rl0], o1 = item[kRecXoff + rl1];
       int emax = max(c0, c1);
 #pragma unroll
       for (int o = 4; o < 32; o <<= 1) emax = max(emax, __shfl_xor_sync(0xffffffffu, emax, o));
@@ -647,11 +781,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         for (int ci = 0; ci < 2; ++ci) {
           const int cnt = ci ? c1 : c0;
           int slot = -1, kpos = 0;
-          if (e == 0) {  // resolved (and range-checked) by the producer
+          if (e == 0) {  // resolved (and range-checked) by the item pass
             const int rl = ci ? rl1 : rl0;
             if (cnt > 0) {
-              slot = item[kItX0slot + rl];
-              kpos = item[kItX0pos + rl];
+              slot = item[kRecX0slot + rl];
+              kpos = item[kRecX0pos + rl];
             }
           } else if (e < cnt) {
             const int xi = (ci ? o1 : o0) + e;
@@ -673,94 +807,107 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       }
     }
 
-    // ---- epilogue: this lane holds rows rl0 / rl1, columns 8 j + 2 t, +1 ----
+    // ---- epilogue: this lane holds rows rl0 / rl1, columns 8 q + 2 t, +1 ----
     rs.l0 += __shfl_xor_sync(0xffffffffu, rs.l0, 1);  // the quad's partial row sums
     rs.l0 += __shfl_xor_sync(0xffffffffu, rs.l0, 2);
     rs.l1 += __shfl_xor_sync(0xffffffffu, rs.l1, 1);
     rs.l1 += __shfl_xor_sync(0xffffffffu, rs.l1, 2);
     const float i0 = rs.l0 > 0.f ? 1.0f / rs.l0 : 0.f, i1 = rs.l1 > 0.f ? 1.0f / rs.l1 : 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      rs.o[j][0] *= i0;
-      rs.o[j][1] *= i0;
-      rs.o[j][2] *= i1;
-      rs.o[j][3] *= i1;
+    for (int q = 0; q < 8; ++q) {
+      rs.o[q][0] *= i0;
+      rs.o[q][1] *= i0;
+      rs.o[q][2] *= i1;
+      rs.o[q][3] *= i1;
     }
-    const int r0 = rl0 < n ? item[kItRows + rl0] : -1, r1 = rl1 < n ? item[kItRows + rl1] : -1;
-    if (prm.gated == nullptr) {
+    if (!fused) {
+      const int r0 = rl0 < n ? item[kRecRows + rl0] : -1, r1 = rl1 < n ? item[kRecRows + rl1] : -1;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int col = h * D + 8 * j + 2 * t;
-        if (r0 >= 0) *reinterpret_cast<float2*>(a.out + (size_t)r0 * hdv + col) = make_float2(rs.o[j][0], rs.o[j][1]);
-        if (r1 >= 0) *reinterpret_cast<float2*>(a.out + (size_t)r1 * hdv + col) = make_float2(rs.o[j][2], rs.o[j][3]);
+      for (int q = 0; q < 8; ++q) {
+        const int col = h * D + 8 * q + 2 * t;
+        if (r0 >= 0) *reinterpret_cast<float2*>(a.out + (size_t)r0 * hdv + col) = make_float2(rs.o[q][0], rs.o[q][1]);
+        if (r1 >= 0) *reinterpret_cast<float2*>(a.out + (size_t)r1 * hdv + col) = make_float2(rs.o[q][2], rs.o[q][3]);
       }
     } else {
-      // LayerNorm over the row's H dv outputs, then the gate by u: O goes to
-      // the shared O tile, and after one barrier each warp normalises whole
-      // rows (2 of the 32) with warp reductions; u and the gated output move
-      // as coalesced 8-byte pieces.  The u loads are issued first.
-      // Lane l owns columns 128 k + 4 l .. +3 (k < 4) of a row; warp w
-      // normalises rows w, w + 2 HC, ... (two rows when HC = 8).
-      const int ld = otile_ld(hdv);
-      auto col_ok = [&](int k) { return 128 * k + 4 * lane < hdv; };
-      uint2 uw[2][4];  // u of this warp's first two rows, loaded before the barrier
+      // O (bf16) over this warp's own query rows of the tile, then, after one
+      // barrier, LayerNorm over each row's H dv outputs times u, whole rows
+      // per warp: warp w takes rows w, w + 2 HC, ...; lane l takes 16-byte
+      // chunks l and l + 32 of a row (chunk c: head c / 8, columns 8 (c % 8)).
+      const uint32_t ot = qtb + tile * q_bytes;
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int rr = warp + i * ncw;
-        const int gr = rr < n ? item[kItRows + rr] : -1;
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          uw[i][k] = (gr >= 0 && col_ok(k))
-                         ? __ldg(reinterpret_cast<const uint2*>(prm.u + (size_t)gr * hdv + 128 * k + 4 * lane))
-                         : make_uint2(0u, 0u);
+      for (int q = 0; q < 8; ++q) {
+        asm volatile("st.shared.u32 [%0], %1;" ::"r"(ot + hl * kHeadTile + blk_off(rl0, q) + 4 * t),
+                     "r"(pack_bf16(rs.o[q][0], rs.o[q][1]))
+                     : "memory");
+        asm volatile("st.shared.u32 [%0], %1;" ::"r"(ot + hl * kHeadTile + blk_off(rl1, q) + 4 * t),
+                     "r"(pack_bf16(rs.o[q][2], rs.o[q][3]))
+                     : "memory");
       }
+      const int nck = H * 8;  // 16-byte chunks per row
+      uint4 un[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};  // u of this warp's first row
+      {
+        const int gr = warp < n ? item[kRecRows + warp] : -1;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int col = hl * D + 8 * j + 2 * t;
-        *reinterpret_cast<float2*>(otile + rl0 * ld + col) = make_float2(rs.o[j][0], rs.o[j][1]);
-        *reinterpret_cast<float2*>(otile + rl1 * ld + col) = make_float2(rs.o[j][2], rs.o[j][3]);
+        for (int c2 = 0; c2 < 2; ++c2)
+          if (gr >= 0 && lane + 32 * c2 < nck)
+            un[c2] = __ldg(reinterpret_cast<const uint4*>(prm.u + (size_t)gr * hdv + 8 * (lane + 32 * c2)));
       }
       bar_consumers(nct);
-      for (int i = 0, rr = warp; rr < n; ++i, rr += ncw) {
-        const int gr = item[kItRows + rr];
-        uint2 ur[4];
+      for (int rr = warp; rr < n; rr += ncw) {
+        const int gr = item[kRecRows + rr];
+        const uint4 ur[2] = {un[0], un[1]};
+        const int rn = rr + ncw;  // this warp's next row: its u load overlaps this row
+        const int grn = rn < n ? item[kRecRows + rn] : -1;
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          ur[k] = i < 2 ? (i ? uw[1][k] : uw[0][k])
-                        : (col_ok(k) ? __ldg(reinterpret_cast<const uint2*>(prm.u + (size_t)gr * hdv + 128 * k +
-                                                                            4 * lane))
-                                     : make_uint2(0u, 0u));
-        float4 v[4];
+        for (int c2 = 0; c2 < 2; ++c2)
+          un[c2] = (grn >= 0 && lane + 32 * c2 < nck)
+                       ? __ldg(reinterpret_cast<const uint4*>(prm.u + (size_t)grn * hdv + 8 * (lane + 32 * c2)))
+                       : make_uint4(0, 0, 0, 0);
+        float v[2][8];
         float sum = 0.f;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          v[k] = col_ok(k) ? *reinterpret_cast<const float4*>(otile + rr * ld + 128 * k + 4 * lane)
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
-          sum += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+        for (int c2 = 0; c2 < 2; ++c2) {
+          const int ck = lane + 32 * c2;
+          uint4 w = make_uint4(0, 0, 0, 0);
+          if (ck < nck)
+            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
+                         : "r"(ot + (ck >> 3) * kHeadTile + blk_off(rr, ck & 7)));
+          const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ww[e]));
+            v[c2][2 * e] = f.x;
+            v[c2][2 * e + 1] = f.y;
+            sum += f.x + f.y;
+          }
         }
         const float mu = warp_sum(sum) / (float)hdv;
         float sq = 0.f;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          if (col_ok(k))
-            sq += (v[k].x - mu) * (v[k].x - mu) + (v[k].y - mu) * (v[k].y - mu) + (v[k].z - mu) * (v[k].z - mu) +
-                  (v[k].w - mu) * (v[k].w - mu);
+        for (int c2 = 0; c2 < 2; ++c2) {
+          if (lane + 32 * c2 < nck)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) sq += (v[c2][e] - mu) * (v[c2][e] - mu);
         }
         const float rsd = 1.0f / sqrtf(warp_sum(sq) / (float)hdv + 1e-6f);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          if (!col_ok(k)) continue;
-          const float2 u01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ur[k].x));
-          const float2 u23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ur[k].y));
-          uint2 o;
-          o.x = pack_bf16(u01.x * ((v[k].x - mu) * rsd), u01.y * ((v[k].y - mu) * rsd));
-          o.y = pack_bf16(u23.x * ((v[k].z - mu) * rsd), u23.y * ((v[k].w - mu) * rsd));
-          *reinterpret_cast<uint2*>(prm.gated + (size_t)gr * hdv + 128 * k + 4 * lane) = o;
+        for (int c2 = 0; c2 < 2; ++c2) {
+          const int ck = lane + 32 * c2;
+          if (ck >= nck) continue;
+          const uint32_t uu[4] = {ur[c2].x, ur[c2].y, ur[c2].z, ur[c2].w};
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 uf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&uu[e]));
+            o[e] = pack_bf16(uf.x * ((v[c2][2 * e] - mu) * rsd), uf.y * ((v[c2][2 * e + 1] - mu) * rsd));
+          }
+          *reinterpret_cast<uint4*>(prm.gated + (size_t)gr * hdv + 8 * ck) = make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
     }
     __syncwarp();
-    if (lane == 0) tc::mbar_arrive(&item_empty[ib]);  // this warp is done with the item buffer
+    if (lane == 0) tc::mbar_arrive(&item_empty[b]);  // this warp is done with the item buffer
   }
 }
 
@@ -784,17 +931,24 @@ EncodeTiledFn encode_fn() {
 
 }  // namespace
 
+cudaError_t launch_attn_items(const imba_step_desc& st, const PoolGeom& g, int* recs, cudaStream_t s) {
+  if (st.num_chunks <= 0) return cudaSuccess;
+  const int warps = 2 * st.num_chunks;
+  return launch_pdl(attn_items_kernel, dim3((warps + 3) / 4), dim3(128), 0, s, st, g, recs);
+}
+
 // Returns false (nothing launched) when the model / pool cannot use this
 // kernel.  *fused is set when the norm + gate was done in the epilogue (the
-// caller then skips its gate pass).  a.counters[0 .. H / hc) must be zero.
+// caller then skips its gate pass).  a.counters[0 .. H / hc) must be zero and
+// recs must hold this step's item records (launch_attn_items).
 bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& md, int64_t num_pages,
-                      const bf16* u, bf16* gated, cudaStream_t s, cudaError_t* err, bool* fused) {
+                      const bf16* u, bf16* gated, const int* recs, cudaStream_t s, cudaError_t* err, bool* fused) {
   *fused = false;
   if (md.dtype != IMBA_DTYPE_BF16 || md.attention_dim != 64 || md.linear_dim != 64) return false;
   const int H = md.num_heads;
   int hc = H < kMaxHC ? H : kMaxHC;
   while (H % hc) --hc;  // largest divisor of H up to 8
-  if (H / hc > kCountersPerLayer || !a.counters) return false;
+  if (H / hc > kCountersPerLayer || !a.counters || !recs) return false;
   const bool fuse = hc == H && gated != nullptr;
   if (a.st.num_chunks <= 0) {
     *err = cudaSuccess;
@@ -816,12 +970,13 @@ bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& 
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return false;
-  // Shared memory: alignment slack, KV ring, query tile, optional fp16 bias
-  // table, item buffers and barriers.  The bias table is
-  // kept in shared memory when at least 3 ring stages still fit.
+  // Shared memory: alignment slack, KV ring, the two query tiles, optional
+  // fp16 bias table, item buffers and barriers.  The bias table is kept in
+  // shared memory when at least 3 ring stages still fit.
   const size_t stage_bytes = 2 * (size_t)hc * kPageBytes;
-  const size_t fixed = 1024 + (size_t)hc * kHalfRows * 128 + (fuse ? (size_t)otile_bytes(H * 64) : 0) + kMetaBytes;
-  const size_t bias_bytes = ((size_t)hc * (2 * md.max_pos - 1) * 2 + 15) / 16 * 16;
+  const size_t meta = kItemBufs * (size_t)kRecBytes + 2 * 4 + (2 * kMaxStages + 2 * kItemBufs) * 8;
+  const size_t fixed = 1024 + 2 * (size_t)hc * kHeadTile + meta;
+  const size_t bias_bytes = ((size_t)hc * (2 * md.max_pos) * 2 + 15) / 16 * 16;  // rows padded to even length
   const bool smem_bias = fixed + bias_bytes + 3 * stage_bytes <= kSmemMax;
   size_t stages = (kSmemMax - fixed - (smem_bias ? bias_bytes : 0)) / stage_bytes;
   stages = stages > kMaxStages ? kMaxStages : stages;
@@ -836,7 +991,7 @@ bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& 
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  PageParams prm{a, num_layers, hc, (int)stages, u, fuse ? gated : nullptr};
+  PageParams prm{a, num_layers, hc, (int)stages, u, fuse ? gated : nullptr, recs};
   const int ctas = a.st.num_chunks < sms ? a.st.num_chunks : sms;
   dim3 grid(ctas, 1, H / hc);
   *err = launch_pdl(kern, grid, dim3((2 * hc + 1) * 32), smem, s, map, prm);

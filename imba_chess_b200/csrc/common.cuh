@@ -131,6 +131,9 @@ namespace imba {
 // Work-queue counters per step: one per (layer, attention head group).
 constexpr int kCountersPerLayer = 16;
 constexpr int kNumCounters = IMBA_MAX_LAYERS * kCountersPerLayer;
+// One resolved attention work item (<= 32 rows of one chunk), int32 words:
+// written once per step by the item pass, read by every layer's attention.
+constexpr int kAttnRecInts = 296;
 
 struct Workspace {
   float* x;        // [R, d]      residual stream
@@ -145,6 +148,7 @@ struct Workspace {
   float* logits;   // [R, vocab]  used when the caller passes no logits buffer
   void* pooled;    // [R, 192]    bf16 models: mean-pooled board-encoder output, split bf16
   int* counters;   // [kNumCounters] work-queue counters, zeroed at the start of every step
+  int* recs;       // [2 R][kAttnRecInts] bf16 models: resolved attention work items
   size_t bytes;
 };
 

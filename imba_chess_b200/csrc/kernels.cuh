@@ -49,8 +49,11 @@ cudaError_t launch_attn_simt(const AttnArgs& a, cudaStream_t s);
 // Tensor-core paged attention (bf16, head dims 64); false when it does not
 // apply.  With every head in one CTA it also applies the attention-output
 // norm and the u gate, writes `gated` and sets *fused.
+// recs: this step's resolved work items, written once per step by
+// launch_attn_items ([2 num_chunks][kAttnRecInts]).
+cudaError_t launch_attn_items(const imba_step_desc& st, const PoolGeom& g, int* recs, cudaStream_t s);
 bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& md, int64_t num_pages,
-                      const bf16* u, bf16* gated, cudaStream_t s, cudaError_t* err, bool* fused);
+                      const bf16* u, bf16* gated, const int* recs, cudaStream_t s, cudaError_t* err, bool* fused);
 
 // Places imba_step_noalloc's scratch array on the current device (noalloc.cu).
 imba_status_t noalloc_prepare_device();

@@ -84,6 +84,38 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parit
   }
 }
 
+// try_wait with a suspend-time hint: the hardware may park the thread for
+// up to hint_ns and wakes it as soon as the phase completes, so a waiting
+// warp takes no issue slots from the warps sharing its scheduler.
+__device__ __forceinline__ bool mbar_try_wait_park(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait_or_abort whose polls park (the same bounds and abort checks).
+__device__ __forceinline__ bool mbar_wait_park_or_abort(uint64_t* bar, uint32_t parity, int32_t* status,
+                                                        volatile int* abort) {
+  constexpr uint32_t kParkNs = 20000;
+  if (mbar_try_wait_park(bar, parity, kParkNs)) return true;
+  const uint64_t t0 = global_ns();
+  while (true) {
+    if (mbar_try_wait_park(bar, parity, kParkNs)) return true;
+    if (*abort) return false;
+    if (global_ns() - t0 > kWaitNs) {
+      report(status, IMBA_ERR_TIMEOUT);
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -99,6 +131,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
           smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Untiled bulk copy global -> shared (no multicast): both addresses 16-byte
+// aligned, bytes a multiple of 16; completion as transaction bytes on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
 

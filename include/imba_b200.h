@@ -148,7 +148,8 @@ typedef struct imba_pool_desc {
  *  - the relative bias uses key position minus positions[r] (unclamped);
  *    the position embedding clamps positions[r] to max_pos - 1.
  * Attention work is given as chunks of <= IMBA_CHUNK_ROWS rows of one group:
- * chunk c covers row_perm[chunk_row_off[c] .. chunk_row_off[c] + chunk_nrows[c]). */
+ * chunk c covers row_perm[chunk_row_off[c] .. chunk_row_off[c] + chunk_nrows[c]).
+ * A step has at most num_rows chunks (IMBA_ERR_ARG otherwise). */
 typedef struct imba_step_desc {
   int32_t num_rows;
   int32_t num_groups;
