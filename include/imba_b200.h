@@ -224,7 +224,7 @@ IMBA_API imba_status_t imba_step(const imba_model* model, const imba_step_desc* 
  * that follow need no set-up; the array's address is looked up on every call
  * (no address outlives a device reset).  Returns IMBA_ERR_OOM, launching
  * nothing, when imba_step_workspace_bytes(model, step->num_rows) exceeds that
- * size (about 370 rows at d512 / 8 layers).  All calls share the array and
+ * size (about 335 rows at d512 / 8 layers).  All calls share the array and
  * it keeps the last call's contents (no step reads scratch it did not write
  * first): calls that overlap on the GPU race and must be serialised by the
  * caller. */
