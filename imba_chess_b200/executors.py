@@ -70,6 +70,33 @@ class PagedDecodeRequest:
     legal_ids: list = field(default_factory=list)
 
 
+class LegalLogits:
+    """One game's rows' legal logits as a sequence: item ``i`` is row i's
+    float32 logits at its legal ids (a view into the wave's flat result),
+    made when it is read."""
+
+    __slots__ = ("_flat", "_off")
+
+    def __init__(self, flat: np.ndarray, off: np.ndarray) -> None:
+        self._flat = flat
+        self._off = off
+
+    def __len__(self) -> int:
+        return len(self._off) - 1
+
+    def __getitem__(self, i: int) -> np.ndarray:
+        n = len(self._off) - 1
+        if i < 0:
+            i += n
+        if not 0 <= i < n:
+            raise IndexError("row index out of range")
+        return self._flat[self._off[i] : self._off[i + 1]]
+
+    def __iter__(self):
+        flat, off = self._flat, self._off.tolist()
+        return (flat[a:b] for a, b in zip(off[:-1], off[1:]))
+
+
 def _step(model, pool: KVPool, plan, buffers: StepBuffers, full_logits: bool):
     """Run one step; (value_stm [R], legal logits flat, logits or None)."""
     R = plan.num_rows
@@ -124,8 +151,8 @@ def make_root_eval_executor(*, model, pool: KVPool, stats=None):
 def make_decode_wave_executor(*, model, pool: KVPool, stats=None, full_logits: bool = False):
     """Executor over ``PagedDecodeRequest`` payloads: one grouped decode step
     for every game's rows.  Returns per payload ``{"value_stm": [n],
-    "legal_logits": [n arrays], "arena_rows": [n], "logits": [n, V] (when
-    ``full_logits``)}``; the rows' KV is appended to each game's arena (rows
+    "legal_logits": LegalLogits (n arrays), "arena_rows": [n], "logits":
+    [n, V] (when ``full_logits``)}``; the rows' KV is appended to each game's arena (rows
     numbered consecutively in payload order, like ``_KVArena.append``)."""
     buffers = StepBuffers(model.device)
 
@@ -157,7 +184,7 @@ def make_decode_wave_executor(*, model, pool: KVPool, stats=None, full_logits: b
         for p, n, s in zip(payloads, counts.tolist(), starts.tolist()):
             entry = {
                 "value_stm": v[r0 : r0 + n],
-                "legal_logits": [ll[loff[r] : loff[r + 1]] for r in range(r0, r0 + n)],
+                "legal_logits": LegalLogits(ll, loff[r0 : r0 + n + 1]),
                 "arena_rows": list(range(s, s + n)),
             }
             if logits is not None:

@@ -550,7 +550,45 @@ PyObject* record_chains(PyObject*, PyObject* args) {
   Py_RETURN_NONE;
 }
 
+// ids_csr(rows) -> (offsets bytes, ids bytes): the CSR of per-row integer
+// sequences (int32 offsets [R+1], int32 ids), e.g. every row's legal move
+// ids.  Lists and tuples of exact one-digit ints are read inline; other
+// sequences and integer types take the general conversion (TypeError for
+// non-integers).
+PyObject* ids_csr(PyObject*, PyObject* args) {
+  PyObject* rows;
+  if (!PyArg_ParseTuple(args, "O", &rows)) return nullptr;
+  Ref seq(PySequence_Fast(rows, "ids_csr expects a sequence of id sequences"));
+  if (!seq) return nullptr;
+  const Py_ssize_t R = PySequence_Fast_GET_SIZE(seq.get());
+  PyObject** items = PySequence_Fast_ITEMS(seq.get());
+  std::vector<int32_t> off((size_t)R + 1, 0);
+  std::vector<int32_t> ids;
+  ids.reserve((size_t)R * 32);
+  for (Py_ssize_t r = 0; r < R; ++r) {
+    Ref row(PySequence_Fast(items[r], "ids_csr: each row must be a sequence of ints"));
+    if (!row) return nullptr;
+    const Py_ssize_t n = PySequence_Fast_GET_SIZE(row.get());
+    PyObject** e = PySequence_Fast_ITEMS(row.get());
+    for (Py_ssize_t k = 0; k < n; ++k) {
+      long long v;
+      if (!as_long(e[k], &v)) return nullptr;
+      ids.push_back(clamp32(v));
+    }
+    if (ids.size() > (size_t)INT32_MAX) {
+      PyErr_SetString(PyExc_OverflowError, "ids_csr: more than 2^31 ids");
+      return nullptr;
+    }
+    off[(size_t)r + 1] = (int32_t)ids.size();
+  }
+  static const char kEmpty[1] = {0};
+  const char* idp = ids.empty() ? kEmpty : reinterpret_cast<const char*>(ids.data());
+  return Py_BuildValue("(y#y#)", reinterpret_cast<const char*>(off.data()), (Py_ssize_t)(off.size() * 4), idp,
+                       (Py_ssize_t)(ids.size() * 4));
+}
+
 PyMethodDef kMethods[] = {
+    {"ids_csr", ids_csr, METH_VARARGS, "CSR (int32 offsets, int32 ids) of per-row integer sequences."},
     {"pack_wave_rows", pack_wave_rows, METH_VARARGS, "Pack the rows of wave requests into flat arrays."},
     {"wave_responses", wave_responses, METH_VARARGS, "Per-request response rows from a step's results."},
     {"wave_chains", wave_chains, METH_VARARGS, "Depths and parent-chain arena rows of a wave's rows."},

@@ -21,19 +21,17 @@ from itertools import chain
 
 import numpy as np
 
+from . import _hostpath
 from .kvpool import PAGE, KVSequence
 from .plan import StepPlan
 from .synth import TOKEN_FIELDS
 
 
 def ids_csr(id_lists) -> tuple[np.ndarray, np.ndarray]:
-    """List of per-row id lists -> (int32 offsets [R+1], int32 flat ids).
-    Iterates with C-level iterators (no per-element Python code)."""
-    lengths = np.fromiter(map(len, id_lists), dtype=np.int64, count=len(id_lists))
-    off = np.zeros(len(id_lists) + 1, dtype=np.int64)
-    np.cumsum(lengths, out=off[1:])
-    flat = np.fromiter(chain.from_iterable(id_lists), dtype=np.int64, count=int(off[-1]))
-    return off.astype(np.int32), flat.astype(np.int32)
+    """List of per-row id lists -> (int32 offsets [R+1], int32 flat ids),
+    built by the C++ host path (no per-element Python code)."""
+    off_b, ids_b = _hostpath.ids_csr(id_lists)
+    return np.frombuffer(off_b, dtype=np.int32), np.frombuffer(ids_b, dtype=np.int32)
 
 
 def _token_arrays(tokens: list[dict]) -> tuple[np.ndarray, np.ndarray]:

@@ -89,3 +89,23 @@ def test_responses_match_python_restatement():
         _hostpath.wave_responses(counts, vals.astype(np.float64), legal, off)
     with pytest.raises(ValueError):
         _hostpath.wave_responses([R + 1], vals, legal, np.zeros(R + 1, np.int32))
+
+
+def test_ids_csr_matches_python_restatement():
+    rng = np.random.default_rng(3)
+    rows = [synth.random_legal_ids(rng, int(rng.integers(0, 40)), 1970).tolist() for _ in range(50)]
+    rows[7] = []
+    rows[11] = tuple(rows[11])
+    rows[13] = np.asarray(rows[13], dtype=np.int64)  # numpy integers take the general conversion
+    off, ids = ids_csr(rows)
+    want_off = np.concatenate([[0], np.cumsum([len(r) for r in rows])]).astype(np.int32)
+    want_ids = np.asarray([int(v) for r in rows for v in r], dtype=np.int32)
+    assert off.dtype == np.int32 and ids.dtype == np.int32
+    np.testing.assert_array_equal(off, want_off)
+    np.testing.assert_array_equal(ids, want_ids)
+    off, ids = ids_csr([])
+    assert off.tolist() == [0] and ids.size == 0
+    with pytest.raises(TypeError):
+        ids_csr([[1, 2.5]])
+    with pytest.raises(TypeError):
+        ids_csr([3])
