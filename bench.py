@@ -65,6 +65,11 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
+if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+    # NCCL reads these when torch first loads it: its communicator init lines
+    # (rank, device, ring) go to the log of a multi-GPU run.
+    os.environ.setdefault("NCCL_DEBUG", "INFO")
+    os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
 
 METRIC = "positions evaluated/sec (grouped decode)"
 # Per-workload defaults (per GPU; weak scaling under torchrun).
@@ -986,7 +991,6 @@ def run_b200(args):
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
-        os.environ.setdefault("NCCL_DEBUG", "INFO")  # communicator init lines (ranks) in the log
         dist.init_process_group("nccl", device_id=device, timeout=__import__("datetime").timedelta(seconds=300))
 
     from imba_chess_b200 import synth
