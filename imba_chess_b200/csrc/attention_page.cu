@@ -23,7 +23,7 @@
 //     consumers finish the current one.
 //   * consumer warps 0 .. 2 HC - 1: warp w owns local head w / 2 and query
 //     rows 16 (w % 2) .. +15 of the item.  The queries sit in one of two
-//     swizzled shared tiles: while an item's pages are done, the consumers
+//     swizzled shared tiles: while an item's epilogue runs, the consumers
 //     copy the next item's queries (cp.async) into the other tile, so an
 //     item starts with its queries in place.  Per page a warp computes
 //     S = Q K^T (mma.sync m16n8k16, fp32 accumulate; Q fragments by
@@ -758,16 +758,6 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       asm volatile("cp.async.wait_all;\n" ::: "memory");
       return;  // the status word already holds the timeout
     }
-    // The next item's queries go into the other tile (its previous contents,
-    // the item before this one, were last read before this item's first
-    // barrier) while this item's extra keys and epilogue run.
-    {
-      const int jn = j + 1, bn = jn % kItemBufs;
-      ok_next = __all_sync(0xffffffffu,
-                           tc::mbar_wait_park_or_abort(&item_full[bn], (jn / kItemBufs) & 1, st.status, abort_flag));
-      const int nn = ok_next ? items[bn * kAttnRecInts + kRecN] : 0;
-      if (nn > 0) copy_queries(items + bn * kAttnRecInts, nn, jn & 1);
-    }
     // Extra keys, per row: the suffix chain and the row itself.
     {
       const int c0 = rl0 < n ? item[kRecXcnt + rl0] : 0, c1 = rl1 < n ? item[kRecXcnt + rl1] : 0;
@@ -807,6 +797,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       }
     }
 
+    // The next item's queries go into the other tile (its previous contents,
+    // the item before this one, were last read before this item's first
+    // barrier) while this item's epilogue runs.
+    {
+      const int jn = j + 1, bn = jn % kItemBufs;
+      ok_next = __all_sync(0xffffffffu,
+                           tc::mbar_wait_park_or_abort(&item_full[bn], (jn / kItemBufs) & 1, st.status, abort_flag));
+      const int nn = ok_next ? items[bn * kAttnRecInts + kRecN] : 0;
+      if (nn > 0) copy_queries(items + bn * kAttnRecInts, nn, jn & 1);
+    }
     // ---- epilogue: this lane holds rows rl0 / rl1, columns 8 q + 2 t, +1 ----
     rs.l0 += __shfl_xor_sync(0xffffffffu, rs.l0, 1);  // the quad's partial row sums
     rs.l0 += __shfl_xor_sync(0xffffffffu, rs.l0, 2);
