@@ -13,8 +13,8 @@
 // The attention kernel is persistent: one CTA per SM (per head group when
 // H > 8) pulls chunks from a per-layer atomic counter.  Warp roles, every
 // hand-off an mbarrier or a named barrier:
-//   * the producer warp (index 2 HC) claims a chunk when the previous item's
-//     pages are all issued, bulk-copies its record into one of four item
+//   * the producer warp (index 2 HC) claims a chunk when the consumers have
+//     finished the previous item's pages, bulk-copies its record into one of four item
 //     buffers and streams the item's visible KV pages: per 16-token page two TMA tiled
 //     loads (K rows of the HC heads, then their V rows: [HC x 16, 64] bf16
 //     with the 128-byte swizzle) into a ring of stages with one "full"
@@ -493,6 +493,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
   uint64_t* empty = full + kMaxStages;
   uint64_t* item_full = empty + kMaxStages;
   uint64_t* item_empty = item_full + kItemBufs;
+  uint64_t* pages_done = item_empty + kItemBufs;  // the consumers finished an item's pages
   volatile int* abort_flag = misc;
 
   if (tid == 0) {
@@ -504,6 +505,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       tc::mbar_init(&item_full[b], 1);
       tc::mbar_init(&item_empty[b], ncw);
     }
+    tc::mbar_init(pages_done, 1);
     misc[0] = 0;
     tc::fence_mbar_init();
   }
@@ -593,10 +595,13 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
           ++pc;
         }
       }
-      // The next chunk is claimed once this item's pages are all issued (the
-      // ring still holds up to S of them), so the longest-first queue hands
-      // out work as CTAs free up; its record travels while those pages are
-      // consumed.
+      // The next chunk is claimed once the consumers have finished this
+      // item's pages, so the longest-first queue hands out work as CTAs are
+      // about to free up; its record and first pages travel while the
+      // consumers fold in the extra keys and run the epilogue.
+      ok = 1;
+      if (lane == 0) ok = tc::mbar_wait_park_or_abort(pages_done, j & 1, st.status, abort_flag);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) return;
       int next = -1, next_half = 0;
       if (half == 0 && nhalves > 1) {
         next = C + c;
@@ -758,6 +763,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       asm volatile("cp.async.wait_all;\n" ::: "memory");
       return;  // the status word already holds the timeout
     }
+    if (tid == 0) tc::mbar_arrive(pages_done);  // the producer claims the next chunk
     // Extra keys, per row: the suffix chain and the row itself.
     {
       const int c0 = rl0 < n ? item[kRecXcnt + rl0] : 0, c1 = rl1 < n ? item[kRecXcnt + rl1] : 0;
@@ -974,7 +980,7 @@ bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& 
   // fp16 bias table, item buffers and barriers.  The bias table is kept in
   // shared memory when at least 3 ring stages still fit.
   const size_t stage_bytes = 2 * (size_t)hc * kPageBytes;
-  const size_t meta = kItemBufs * (size_t)kRecBytes + 2 * 4 + (2 * kMaxStages + 2 * kItemBufs) * 8;
+  const size_t meta = kItemBufs * (size_t)kRecBytes + 2 * 4 + (2 * kMaxStages + 2 * kItemBufs + 1) * 8;
   const size_t fixed = 1024 + 2 * (size_t)hc * kHeadTile + meta;
   const size_t bias_bytes = ((size_t)hc * (2 * md.max_pos) * 2 + 15) / 16 * 16;  // rows padded to even length
   const bool smem_bias = fixed + bias_bytes + 3 * stage_bytes <= kSmemMax;
