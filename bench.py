@@ -754,8 +754,24 @@ def measure(args, model, dims, device, rank, world, sampler=None):
         model.check_status()
         ntok = sum(p.num_rows for p in extra)
         pms = e0.elapsed_time(e1)
+        # Its roofline: the tensor work of every token (board encoder, content,
+        # trunk and value GEMMs) plus the causal attention products over each
+        # token's visible keys, against the sustained bf16 peak.
+        d, H = dims.model_dim, dims.num_heads
+        qkv = dims.attention_dim + dims.linear_dim
+        board_mac = 2 * (64 * 64 * 192 + 2 * 4 * 64 * 64 * 16 + 64 * 64 * 64 + 2 * 64 * 64 * 128) + 64 * d
+        dense_mac = (board_mac + 3 * 64 * d + dims.num_layers * (d * 2 * H * qkv + H * dims.linear_dim * d)
+                     + d * (d // 2))
+        attn_mac = sum(int(p.row_vis.astype(np.int64).sum()) for p in extra) * dims.num_layers * H * qkv
+        flop = 2.0 * (dense_mac * ntok + attn_mac)
+        peaks, _src = load_peaks()
+        achieved = flop / (pms / 1000.0) / 1e12
         result["prefill"] = {"tokens": int(ntok), "batches": len(extra), "ms": round(pms, 3),
-                             "tokens_per_s": ntok / (pms / 1000.0)}
+                             "tokens_per_s": ntok / (pms / 1000.0),
+                             "roofline": {"bound": "tensor", "achieved": round(achieved, 2),
+                                          "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                                          "frac": round(achieved / peaks["bf16_tflops_sustained"], 4),
+                                          "gflop": round(flop / 1e9, 1)}}
 
     def make_events():
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
