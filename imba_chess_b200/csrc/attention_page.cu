@@ -462,6 +462,16 @@ __global__ void __launch_bounds__(128) attn_items_kernel(const imba_step_desc st
   }
 }
 
+#ifndef IMBA_CLAIM_EARLY
+#define IMBA_CLAIM_EARLY 2
+#endif
+#ifndef IMBA_CLAIM_LEAD
+#define IMBA_CLAIM_LEAD(n) ((n) <= 8 ? 3 : ((n) <= 16 ? 2 : 0))
+#endif
+// Pages before the end of an item at which its CTA claims the next chunk,
+// by the item's row count.
+__device__ __forceinline__ int claim_lead(int n) { return IMBA_CLAIM_LEAD(n); }
+
 template <bool kSmemBias>
 __global__ void __launch_bounds__(kMaxThreads, 1)
     attn_page_kernel(const __grid_constant__ CUtensorMap kvmap, const PageParams prm) {
@@ -493,7 +503,6 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
   uint64_t* empty = full + kMaxStages;
   uint64_t* item_full = empty + kMaxStages;
   uint64_t* item_empty = item_full + kItemBufs;
-  uint64_t* pages_done = item_empty + kItemBufs;  // the consumers finished an item's pages
   volatile int* abort_flag = misc;
 
   if (tid == 0) {
@@ -505,7 +514,6 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       tc::mbar_init(&item_full[b], 1);
       tc::mbar_init(&item_empty[b], ncw);
     }
-    tc::mbar_init(pages_done, 1);
     misc[0] = 0;
     tc::fence_mbar_init();
   }
@@ -595,12 +603,24 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
           ++pc;
         }
       }
-      // The next chunk is claimed once the consumers have finished this
-      // item's pages, so the longest-first queue hands out work as CTAs are
-      // about to free up; its record and first pages travel while the
-      // consumers fold in the extra keys and run the epilogue.
+      // The next chunk is claimed when the consumers release this item's
+      // page claim_lead(n) from its end: early enough that the next item's
+      // record and first pages arrive before the consumers finish this one
+      // (a small item has little work after its pages), late enough that a
+      // CTA which stays busy for a while does not take work that another CTA
+      // would start sooner from the longest-first queue.  Page q's release is
+      // the (q / S)-th phase of its stage's empty barrier; while page q + S
+      // is not issued (lead < S) that barrier is at most one phase past it.
+      // A lead of npg or S or more claims at once (page q, if any, was
+      // released before page q + S was issued).
+      // While more than IMBA_CLAIM_EARLY chunks per CTA remain, the tail is far
+      // off and the claim goes out at once.
+      const int lead = C - c > IMBA_CLAIM_EARLY * (int)gridDim.x ? S : claim_lead(item[kRecN]);
       ok = 1;
-      if (lane == 0) ok = tc::mbar_wait_park_or_abort(pages_done, j & 1, st.status, abort_flag);
+      if (lane == 0 && lead < npg && lead < S) {
+        const int q = pc - 1 - lead;
+        ok = tc::mbar_wait_park_or_abort(&empty[q % S], (q / S) & 1, st.status, abort_flag);
+      }
       if (!__shfl_sync(0xffffffffu, ok, 0)) return;
       int next = -1, next_half = 0;
       if (half == 0 && nhalves > 1) {
@@ -763,7 +783,6 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       asm volatile("cp.async.wait_all;\n" ::: "memory");
       return;  // the status word already holds the timeout
     }
-    if (tid == 0) tc::mbar_arrive(pages_done);  // the producer claims the next chunk
     // Extra keys, per row: the suffix chain and the row itself.
     {
       const int c0 = rl0 < n ? item[kRecXcnt + rl0] : 0, c1 = rl1 < n ? item[kRecXcnt + rl1] : 0;
@@ -980,7 +999,7 @@ bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& 
   // fp16 bias table, item buffers and barriers.  The bias table is kept in
   // shared memory when at least 3 ring stages still fit.
   const size_t stage_bytes = 2 * (size_t)hc * kPageBytes;
-  const size_t meta = kItemBufs * (size_t)kRecBytes + 2 * 4 + (2 * kMaxStages + 2 * kItemBufs + 1) * 8;
+  const size_t meta = kItemBufs * (size_t)kRecBytes + 2 * 4 + (2 * kMaxStages + 2 * kItemBufs) * 8;
   const size_t fixed = 1024 + 2 * (size_t)hc * kHeadTile + meta;
   const size_t bias_bytes = ((size_t)hc * (2 * md.max_pos) * 2 + 15) / 16 * 16;  // rows padded to even length
   const bool smem_bias = fixed + bias_bytes + 3 * stage_bytes <= kSmemMax;
