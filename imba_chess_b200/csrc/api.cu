@@ -144,6 +144,11 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
   // The paged attention's work items, resolved once for every layer.
   const bool paged_attn = md.dtype == IMBA_DTYPE_BF16 && !m->simt_attn;
   if (paged_attn) IMBA_CK(launch_attn_items(st, g, w.recs, s));
+  // A step whose rows find every key in their groups' pages and that has
+  // several rows per group on average (a jagged prefill of documents) runs
+  // the prefill attention kernel; decode waves (every row has extra keys)
+  // and short root extensions run the paged decode kernel.
+  const bool prefill_attn = paged_attn && st.num_extra == 0 && st.num_rows >= 4 * st.num_groups;
   // bf16 handles run the tensor-core kernels; a launcher that declines
   // (returns false) is an error unless a SIMT test hook selected the SIMT
   // kernel of that component (imba_model_desc.flags).
@@ -182,8 +187,10 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
                 w.counters + l * kCountersPerLayer};
     bool fused = false;
     bf16* gated_bf = std::is_same<T, bf16>::value ? reinterpret_cast<bf16*>(w.gated) : nullptr;
-    if (!paged_attn || !launch_attn_page(aa, md.num_layers, md, pool.num_pages, static_cast<const bf16*>(w.u),
-                                         gated_bf, w.recs, s, &e, &fused)) {
+    if (prefill_attn && launch_attn_prefill(aa, md.num_layers, pool.num_pages, w.recs, s, &e)) {
+      if (e != cudaSuccess) return IMBA_ERR_CUDA;
+    } else if (!paged_attn || !launch_attn_page(aa, md.num_layers, md, pool.num_pages, static_cast<const bf16*>(w.u),
+                                                gated_bf, w.recs, s, &e, &fused)) {
       if (md.dtype == IMBA_DTYPE_BF16 && !m->simt_attn) return IMBA_ERR_UNSUPPORTED;
       IMBA_CK(launch_attn_simt<T>(aa, s));
     } else if (e != cudaSuccess) {

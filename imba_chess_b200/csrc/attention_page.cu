@@ -1,6 +1,8 @@
-// Grouped paged-KV decode / prefill attention on the tensor cores (bf16
-// models, d_qk = d_v = 64), with the attention-output LayerNorm and the u
-// gate fused into its epilogue.
+// Grouped paged-KV decode attention on the tensor cores (bf16 models,
+// d_qk = d_v = 64), with the attention-output LayerNorm and the u gate fused
+// into its epilogue.  It also runs steps without extra keys that have few
+// rows per group (root extensions); jagged prefills of whole documents run
+// attention_prefill.cu.
 //
 // Work items.  An item is <= 32 query rows of one chunk (a 64-row chunk is
 // two items) and HC heads (all of them when H <= 8).  Once per step the item
@@ -13,8 +15,9 @@
 // The attention kernel is persistent: one CTA per SM (per head group when
 // H > 8) pulls chunks from a per-layer atomic counter.  Warp roles, every
 // hand-off an mbarrier or a named barrier:
-//   * the producer warp (index 2 HC) claims a chunk when the consumers have
-//     finished the previous item's pages, bulk-copies its record into one of four item
+//   * the producer warp (index 2 HC) claims a chunk (at once while the queue
+//     is far from its end, then when the consumers near the end of the
+//     previous item's pages), bulk-copies its record into one of four item
 //     buffers and streams the item's visible KV pages: per 16-token page two TMA tiled
 //     loads (K rows of the HC heads, then their V rows: [HC x 16, 64] bf16
 //     with the 128-byte swizzle) into a ring of stages with one "full"
@@ -50,6 +53,7 @@
 
 #include <type_traits>
 
+#include "attn_common.cuh"
 #include "kernels.cuh"
 #include "tc_ptx.cuh"
 
@@ -65,23 +69,6 @@ constexpr int kMaxStages = 8;
 constexpr int kItemBufs = 4;
 constexpr int kMaxThreads = (2 * kMaxHC + 1) * 32;
 
-// Item record (int32 words; kAttnRecInts * 4 bytes, a multiple of 16).
-constexpr int kRecN = 0;        // rows in the item (0: nothing to do; -1 in a buffer: no more items)
-constexpr int kRecNpg = 1;      // visible pages (ceil of the longest row's prefix / 16)
-constexpr int kRecPg0 = 2;      // first entry of the group's page list
-constexpr int kRecHalves = 3;   // items of the chunk (record of its first half)
-constexpr int kRecRows = 8;     // [32] global row ids
-constexpr int kRecVis = 40;     // [32] visible prefix tokens
-constexpr int kRecQpos = 72;    // [32] query positions
-constexpr int kRecXoff = 104;   // [32] first extra of the row
-constexpr int kRecXcnt = 136;   // [32] extras of the row
-constexpr int kRecX0slot = 168; // [32] pool slot of the row's first extra (-1: none)
-constexpr int kRecX0pos = 200;  // [32] its position
-constexpr int kRecPages = 232;  // [kRecMaxPages] the group's first page ids
-constexpr int kRecMaxPages = 64;
-constexpr uint32_t kRecBytes = kAttnRecInts * 4;
-static_assert(kRecPages + kRecMaxPages == kAttnRecInts, "record layout");
-static_assert(kRecBytes % 16 == 0, "bulk copies move multiples of 16 bytes");
 constexpr int kRows = kHalfRows;
 
 struct PageParams {
@@ -93,12 +80,6 @@ struct PageParams {
   bf16* gated;       // [R, H dv]: fused norm + gate output (nullptr: store fp32 O to a.out)
   const int* recs;   // [2 C][kAttnRecInts]: record c = chunk c's first 32 rows, C + c its second
 };
-
-__device__ __forceinline__ int bias_index(int kpos, int qpos, int max_pos) {
-  int idx = kpos - qpos + (max_pos - 1);
-  idx = idx < 0 ? 0 : idx;
-  return idx > 2 * max_pos - 2 ? 2 * max_pos - 2 : idx;
-}
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
@@ -144,17 +125,6 @@ __device__ __forceinline__ bool bar_consumers_or(int nthreads, bool pred) {
       : "r"((uint32_t)pred), "r"(nthreads)
       : "memory");
   return r != 0;
-}
-
-// Scores are kept in the log2 domain: s2 = (q.k) * scale * log2(e) +
-// bias * log2(e), weights 2^(s2 - max), which is the same softmax as
-// exp(s - max) with one multiply less per element.
-constexpr float kLog2e = 1.4426950408889634f;
-
-__device__ __forceinline__ float exp2_approx(float x) {  // hardware ex2; 2^-inf = +0
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
 }
 
 // Relative-position bias lookups log2(e) * ps_w[h, idx]: from a per-CTA fp16
@@ -452,12 +422,15 @@ __global__ void __launch_bounds__(128) attn_items_kernel(const imba_step_desc st
     }
     rec[kRecPages + p] = pg;
   }
+  const int r0 = __shfl_sync(0xffffffffu, r, 0);
+  const bool contig = __all_sync(0xffffffffu, lane >= n || r == r0 + lane);
   if (lane < 8) {
     int h = 0;
     if (lane == kRecN) h = n;
     else if (lane == kRecNpg) h = npg;
     else if (lane == kRecPg0) h = pg0;
     else if (lane == kRecHalves) h = (n_chunk + kRows - 1) / kRows;
+    else if (lane == kRecContig) h = contig ? 1 : 0;
     rec[lane] = h;
   }
 }
@@ -936,24 +909,6 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
   }
 }
 
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
-  return fn;
-}
-
 }  // namespace
 
 cudaError_t launch_attn_items(const imba_step_desc& st, const PoolGeom& g, int* recs, cudaStream_t s) {
@@ -984,7 +939,7 @@ bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& 
   // one box = one page's 16 rows of hc consecutive heads.
   const uint64_t rows = (uint64_t)num_pages * num_layers * 2 * H * IMBA_PAGE_TOKENS;
   if (rows > (uint64_t)INT32_MAX) return false;
-  EncodeTiledFn enc = encode_fn();
+  EncodeTiledFn enc = attn_encode_fn();
   if (!enc || (reinterpret_cast<uintptr_t>(a.pool) & 15)) return false;
   CUtensorMap map;
   const cuuint64_t dims[2] = {64, rows};

@@ -54,6 +54,11 @@ cudaError_t launch_attn_simt(const AttnArgs& a, cudaStream_t s);
 cudaError_t launch_attn_items(const imba_step_desc& st, const PoolGeom& g, int* recs, cudaStream_t s);
 bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& md, int64_t num_pages,
                       const bf16* u, bf16* gated, const int* recs, cudaStream_t s, cudaError_t* err, bool* fused);
+// Jagged prefill attention (tcgen05; bf16, head dims 64, an even head
+// count): for steps without extra keys.  Writes fp32 O to a.out (the norm /
+// gate is a separate pass); false when it does not apply.
+bool launch_attn_prefill(const AttnArgs& a, int num_layers, int64_t num_pages, const int* recs, cudaStream_t s,
+                         cudaError_t* err);
 
 // Places imba_step_noalloc's scratch array on the current device (noalloc.cu).
 imba_status_t noalloc_prepare_device();

@@ -116,7 +116,11 @@ class StepPlan:
 
     def finalize(self) -> "StepPlan":
         if self.chunks is None:
-            self.chunks = build_chunks(self.row_group, self.num_groups, row_vis=self.row_vis)
+            # Steps without extra keys (prefills) take 64-row chunks: the
+            # prefill attention stacks a chunk's rows for two heads in one
+            # 128-row tensor-core tile.
+            rows = CHUNK if self.extra_slot.shape[0] == 0 else 32
+            self.chunks = build_chunks(self.row_group, self.num_groups, max_rows=rows, row_vis=self.row_vis)
         return self
 
     def arrays(self) -> dict[str, np.ndarray]:

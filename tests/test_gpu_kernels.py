@@ -90,9 +90,11 @@ def test_tensor_core_kernel_matches_simt(component, dims, parents):
 
 def test_attention_result_independent_of_chunking():
     """The C ABI accepts chunks of up to 64 rows; the planner emits <= 32-row
-    chunks (one attention work item).  Re-chunking the same steps into 64-row
-    and 16-row chunks must give bit-identical results (each row's attention
-    depends only on its own keys; a 64-row chunk is processed as two items)."""
+    chunks (one attention work item) for decode steps and 64-row chunks for
+    prefills.  Re-chunking the same steps into 32-, 64- and 16-row chunks
+    must give bit-identical results (each row's attention depends only on its
+    own keys; a 64-row chunk is processed as two decode items or one prefill
+    unit)."""
     from imba_chess_b200.plan import build_chunks
 
     dims = synth.D256
@@ -104,7 +106,7 @@ def test_attention_result_independent_of_chunking():
         model = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
         orig = build_chunks
 
-        def rechunk(row_group, num_groups, max_rows_=32, row_vis=None, _m=max_rows):
+        def rechunk(row_group, num_groups, max_rows=32, row_vis=None, _m=max_rows):  # noqa: ARG001
             return orig(row_group, num_groups, max_rows=_m, row_vis=row_vis)
 
         import imba_chess_b200.plan as plan_mod
@@ -137,6 +139,54 @@ def test_attention_positions_past_max_pos():
     assert float((a["value_logits"] - b["value_logits"]).abs().max()) <= tv
 
 
+def _prefill(model, dims, lens, seed):
+    """One packed jagged prefill of documents of the given lengths: every
+    row's hidden state, logits and value logits."""
+    rng = np.random.default_rng(seed)
+    tokens = [synth.random_tokens(rng, n, dims) for n in lens]
+    pool = model.new_pool(sum(-(-n // 16) for n in lens) + 8)
+    seqs = [KVSequence(pool) for _ in lens]
+    plan, _ = root_plan(seqs, tokens)
+    R = plan.num_rows
+    out = {
+        "logits": torch.empty((R, dims.vocab), device=model.device),
+        "value_logits": torch.empty((R, 3), device=model.device),
+        "hidden": torch.empty((R, dims.model_dim), device=model.device),
+    }
+    model.run(DeviceStep(plan, model.device), pool, **out)
+    torch.cuda.synchronize()
+    model.check_status()
+    return out
+
+
+@pytest.mark.parametrize(
+    "dims,lens",
+    [
+        (synth.D512, [1, 2, 17, 31, 32, 33, 63, 64, 65, 130, 300]),
+        (synth.SMALL, [5, 47, 48, 64, 100]),  # positions past max_pos 48: bias indices clamp
+        (synth.ModelDims(256, 2, 4, max_pos=96), [230, 1, 96, 97, 64]),
+        (synth.D1024, [40, 129, 7]),
+    ],
+    ids=["d512", "d128", "d256-maxpos96", "d1024"],
+)
+def test_prefill_attention_matches_simt(dims, lens):
+    """The jagged prefill attention (tcgen05 S and P.V over 64-row chunks and
+    head pairs, fp32 O and a separate norm / gate pass) against the SIMT
+    attention on the same packed prefill: documents from one token to several
+    pages, chunk and block boundaries on both sides, odd page counts."""
+    sd = synth.make_state_dict(dims, 31, profile="reference")
+    model_tc = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
+    model_simt = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0", simt=("attn",))
+    a = _prefill(model_tc, dims, lens, 5)
+    b = _prefill(model_simt, dims, lens, 5)
+    th, tl, tv = TOL["attn"]
+    scale = float(b["hidden"].abs().max())
+    assert torch.isfinite(a["hidden"]).all() and torch.isfinite(a["logits"]).all()
+    assert float((a["hidden"] - b["hidden"]).abs().max()) <= th * scale
+    assert float((a["logits"] - b["logits"]).abs().max()) <= tl
+    assert float((a["value_logits"] - b["value_logits"]).abs().max()) <= tv
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["fp32", "bf16"])
 @pytest.mark.parametrize("max_rows", [32, 64])
 def test_legal_gather_matches_full_projection(dtype, max_rows):
@@ -153,7 +203,7 @@ def test_legal_gather_matches_full_projection(dtype, max_rows):
     model = B200HSTUChessModel(sd, dtype=dtype, device="cuda:0")
     orig = plan_mod.build_chunks
 
-    def rechunk(row_group, num_groups, max_rows_=32, row_vis=None):
+    def rechunk(row_group, num_groups, max_rows_=32, row_vis=None, **kw):  # noqa: ARG001
         return orig(row_group, num_groups, max_rows=max_rows, row_vis=row_vis)
 
     plan_mod.build_chunks = rechunk
