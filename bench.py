@@ -67,9 +67,10 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 if int(os.environ.get("WORLD_SIZE", "1")) > 1:
     # NCCL reads these when torch first loads it: its communicator init lines
-    # (rank, device, ring) go to the log of a multi-GPU run.
-    os.environ.setdefault("NCCL_DEBUG", "INFO")
-    os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+    # (rank, device, ring) go to the log of a multi-GPU run, whatever level
+    # the environment had.
+    os.environ["NCCL_DEBUG"] = "INFO"
+    os.environ["NCCL_DEBUG_SUBSYS"] = "INIT,ENV"
 
 METRIC = "positions evaluated/sec (grouped decode)"
 # Per-workload defaults (per GPU; weak scaling under torchrun).
