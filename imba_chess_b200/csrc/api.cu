@@ -187,8 +187,10 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
                 w.counters + l * kCountersPerLayer};
     bool fused = false;
     bf16* gated_bf = std::is_same<T, bf16>::value ? reinterpret_cast<bf16*>(w.gated) : nullptr;
+    bool gate_bf16 = false;  // the attention output was stored as bf16
     if (prefill_attn && launch_attn_prefill(aa, md.num_layers, pool.num_pages, w.recs, s, &e)) {
       if (e != cudaSuccess) return IMBA_ERR_CUDA;
+      gate_bf16 = true;
     } else if (!paged_attn || !launch_attn_page(aa, md.num_layers, md, pool.num_pages, static_cast<const bf16*>(w.u),
                                                 gated_bf, w.recs, s, &e, &fused)) {
       if (md.dtype == IMBA_DTYPE_BF16 && !m->simt_attn) return IMBA_ERR_UNSUPPORTED;
@@ -197,7 +199,11 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
       return IMBA_ERR_CUDA;
     }
     IMBA_CK(pm.mark(s));
-    if (!fused) IMBA_CK(launch_gate<T>(w.attn, static_cast<const T*>(w.u), R, hdv, static_cast<T*>(w.gated), s));
+    if (gate_bf16)
+      IMBA_CK(launch_gate_bf16(reinterpret_cast<const bf16*>(w.attn), static_cast<const bf16*>(w.u), R, hdv,
+                               static_cast<bf16*>(w.gated), s));
+    else if (!fused)
+      IMBA_CK(launch_gate<T>(w.attn, static_cast<const T*>(w.u), R, hdv, static_cast<T*>(w.gated), s));
     IMBA_CK(pm.mark(s));
     EpiResidual er{w.x, md.o_b[l], d};
     if (!gemm_tc_launch_out(m, l, R, static_cast<const T*>(w.gated), er, st.status, s, &e)) {

@@ -35,8 +35,9 @@
 //     block from TMEM, adds the bias,
 //     masks keys past its visible prefix and keeps the online softmax (lazy
 //     rescale: O' in TMEM is rescaled only when the max grows by more than
-//     2^8), writes its P' row, and at the end stores O / l as fp32 rows; the
-//     attention-output norm and u gate then run as their own pass.
+//     2^8), writes its P' row, and at the end stores O / l as bf16 rows (the
+//     attention output's type); the attention-output norm and u gate then
+//     run as their own pass.
 // Every wait is bounded; a timeout sets the status word and the CTA drains
 // its copies and MMAs before freeing TMEM.
 // Semantics: src/imba_chess/model/hstu_attention.py:64-76 (bias),
@@ -465,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         tc::fence_after_sync();
       }
       const float inv = l > 0.f ? 1.0f / l : 0.f;
-      float* dst = a.out + (size_t)r * HD + h * 64;
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(a.out) + (size_t)r * HD + h * 64);
 #pragma unroll
       for (int hp = 0; hp < 2; ++hp) {
         float ov[32];
@@ -477,9 +478,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         if (valid) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            *reinterpret_cast<float4*>(dst + 32 * hp + i) =
-                make_float4(ov[i] * inv, ov[i + 1] * inv, ov[i + 2] * inv, ov[i + 3] * inv);
+          for (int i = 0; i < 32; i += 8)
+            dst[4 * hp + i / 8] = make_uint4(pack2_bf16(ov[i] * inv, ov[i + 1] * inv),
+                                             pack2_bf16(ov[i + 2] * inv, ov[i + 3] * inv),
+                                             pack2_bf16(ov[i + 4] * inv, ov[i + 5] * inv),
+                                             pack2_bf16(ov[i + 6] * inv, ov[i + 7] * inv));
         }
       }
       tc::fence_before_sync();  // O' read before the next unit's first P' V' overwrites it

@@ -28,6 +28,8 @@ template <typename T>
 cudaError_t launch_ln_rows(const float* x, int rows, int n, float eps, T* out, cudaStream_t s);
 template <typename T>
 cudaError_t launch_gate(const float* attn, const T* u, int rows, int n, T* out, cudaStream_t s);
+// The same with the attention output already rounded to bf16 (n a multiple of 128).
+cudaError_t launch_gate_bf16(const bf16* attn, const bf16* u, int rows, int n, bf16* out, cudaStream_t s);
 template <typename T>
 cudaError_t launch_final_ln(const float* x, int rows, int n, const float* w, const float* b, float* out32, T* out3,
                             cudaStream_t s);
@@ -55,8 +57,9 @@ cudaError_t launch_attn_items(const imba_step_desc& st, const PoolGeom& g, int* 
 bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& md, int64_t num_pages,
                       const bf16* u, bf16* gated, const int* recs, cudaStream_t s, cudaError_t* err, bool* fused);
 // Jagged prefill attention (tcgen05; bf16, head dims 64, an even head
-// count): for steps without extra keys.  Writes fp32 O to a.out (the norm /
-// gate is a separate pass); false when it does not apply.
+// count): for steps without extra keys.  Writes O rounded to bf16 over a.out
+// ([R, H dv] bf16 in its first half; the norm / gate is a separate pass,
+// launch_gate_bf16); false when it does not apply.
 bool launch_attn_prefill(const AttnArgs& a, int num_layers, int64_t num_pages, const int* recs, cudaStream_t s,
                          cudaError_t* err);
 

@@ -188,21 +188,21 @@ __global__ void ln_rows4_kernel(const float* __restrict__ x, int rows, int n, fl
       store4(o + 128 * i, (v[i].x - mu) * rs, (v[i].y - mu) * rs, (v[i].z - mu) * rs, (v[i].w - mu) * rs);
 }
 
-template <typename TOut>
-__global__ void gate4_kernel(const float* __restrict__ attn, const TOut* __restrict__ u, int rows, int n,
+template <typename TIn, typename TOut>
+__global__ void gate4_kernel(const TIn* __restrict__ attn, const TOut* __restrict__ u, int rows, int n,
                              TOut* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= rows) return;
   const int nv = n >> 7;
-  const float* ar = attn + (size_t)warp * n + 4 * lane;
+  const TIn* ar = attn + (size_t)warp * n + 4 * lane;
   const TOut* ur = u + (size_t)warp * n + 4 * lane;
   float4 v[kMaxVec], w[kMaxVec];
 #pragma unroll
   for (int i = 0; i < kMaxVec; ++i)
     if (i < nv) {
-      v[i] = *reinterpret_cast<const float4*>(ar + 128 * i);
+      v[i] = load4(ar + 128 * i);
       w[i] = load4(ur + 128 * i);
     }
   float mu, rs;
@@ -454,11 +454,16 @@ template cudaError_t launch_ln_rows<bf16>(const float*, int, int, float, bf16*, 
 template <typename T>
 cudaError_t launch_gate(const float* attn, const T* u, int rows, int n, T* out, cudaStream_t s) {
   if (n % 128 == 0 && n <= 128 * kMaxVec)
-    return launch_pdl(gate4_kernel<T>, dim3(warp_blocks(rows)), dim3(256), 0, s, attn, u, rows, n, out);
+    return launch_pdl(gate4_kernel<float, T>, dim3(warp_blocks(rows)), dim3(256), 0, s, attn, u, rows, n, out);
   return launch_pdl(gate_kernel<T>, dim3(warp_blocks(rows)), dim3(256), 0, s, attn, u, rows, n, out);
 }
 template cudaError_t launch_gate<float>(const float*, const float*, int, int, float*, cudaStream_t);
 template cudaError_t launch_gate<bf16>(const float*, const bf16*, int, int, bf16*, cudaStream_t);
+
+cudaError_t launch_gate_bf16(const bf16* attn, const bf16* u, int rows, int n, bf16* out, cudaStream_t s) {
+  if (n % 128 || n > 128 * kMaxVec) return cudaErrorInvalidValue;
+  return launch_pdl(gate4_kernel<bf16, bf16>, dim3(warp_blocks(rows)), dim3(256), 0, s, attn, u, rows, n, out);
+}
 
 template <typename T>
 cudaError_t launch_final_ln(const float* x, int rows, int n, const float* w, const float* b, float* out32, T* out3,
