@@ -67,10 +67,24 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 if int(os.environ.get("WORLD_SIZE", "1")) > 1:
     # NCCL reads these when torch first loads it: its communicator init lines
-    # (rank, device, ring) go to the log of a multi-GPU run, whatever level
-    # the environment had.
+    # (rank, device, ring) go to the run's log, whatever level the
+    # environment had.  Stdout carries only rank 0's JSON line: file
+    # descriptor 1 (NCCL's log included) is pointed at stderr, and the JSON
+    # line goes to a copy of the original stdout.
     os.environ["NCCL_DEBUG"] = "INFO"
-    os.environ["NCCL_DEBUG_SUBSYS"] = "INIT,ENV"
+    os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(sys.stdout.fileno()), "w") if int(os.environ.get("RANK", "0")) == 0 else None
+    os.dup2(sys.stderr.fileno(), sys.stdout.fileno())
+else:
+    _JSON_OUT = None
+
+
+def emit(line: dict) -> None:
+    """Print one result line (the JSON line of the run) on stdout."""
+    out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
 
 METRIC = "positions evaluated/sec (grouped decode)"
 # Per-workload defaults (per GPU; weak scaling under torchrun).
@@ -453,12 +467,11 @@ def run_reference(args):
     if rank != 0:
         return
     if args.workload not in ("grouped", "d1024"):
-        print(json.dumps({"impl": "reference", "unavailable": "the reference arm is timed on the grouped-decode "
-                                                              "wave workloads only"}), flush=True)
+        emit({"impl": "reference", "unavailable": "the reference arm is timed on the grouped-decode wave workloads "
+                                                  "only"})
         return
     if not os.path.isdir(os.path.join(REF_PATH, "imba_chess")):
-        print(json.dumps({"impl": "reference", "unavailable": "the reference is not installed under baseline/_ref"}),
-              flush=True)
+        emit({"impl": "reference", "unavailable": "the reference is not installed under baseline/_ref"})
         return
     dims, wave = workload(args, 0, world)
     rows_all = wave.num_rows * world
@@ -498,7 +511,7 @@ def run_reference(args):
             "value": rows * len(ct) / sum(ct), "unit": UNIT, "ms_per_step": 1000.0 * sum(ct) / len(ct),
             "rows_per_step": rows, "steps": csteps,
             "what": "reference ActorInferenceServer.service() on cuda:0 with bf16 autocast, eager torch, full wave"}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ----------------------------------------------------------------------
@@ -1044,11 +1057,11 @@ def run_b200(args):
     model = B200HSTUChessModel(sd, dtype=torch.bfloat16, device=device)
     if args.workload == "model_api":
         line = run_model_api(args, model, dims, device, rank, world)
-        if rank == 0:
-            print(json.dumps(line), flush=True)
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
+        if rank == 0:
+            emit(line)
         return
     sampler = ClockSampler(local)
     res = measure(args, model, dims, device, rank, world, sampler=sampler)
@@ -1109,11 +1122,11 @@ def run_b200(args):
             line["cpu_baseline_port"] = port
         else:
             line["cpu_baseline"] = port
-    if rank == 0:
-        print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if rank == 0:
+        emit(line)
 
 
 def service_api(args, dims, wave, sd, device):
