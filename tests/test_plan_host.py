@@ -49,6 +49,33 @@ def test_chunks_listed_longest_prefix_first():
         assert (row_group[perm[co[c] : co[c] + cn[c]]] == cg[c]).all()
 
 
+def test_prefill_steps_take_64_row_chunks_and_decode_steps_32():
+    """Steps without extra keys (prefills) are chunked by 64 rows (one
+    prefill-attention unit stacks a chunk's rows for two heads in a 128-row
+    tile); steps with extra keys by 32 (one decode-attention item)."""
+    from imba_chess_b200.kvpool import KVPool, KVSequence
+    from imba_chess_b200.steps import root_plan
+    from imba_chess_b200 import synth
+
+    dims = synth.ModelDims(128, 1, 2)
+    import torch
+
+    pool = KVPool(num_layers=1, num_heads=2, attention_dim=64, linear_dim=64, num_pages=64, dtype=torch.float32,
+                  device=torch.device("cpu"))
+    seqs = [KVSequence(pool) for _ in range(2)]
+    rng = np.random.default_rng(4)
+    plan, _ = root_plan(seqs, [synth.random_tokens(rng, n, dims) for n in (150, 40)])
+    plan.finalize()
+    _, cg, co, cn = plan.chunks
+    assert int(cn.max()) > 32 and int(cn.max()) <= 64 and int(cn.sum()) == 190
+    decode = _plan(70)
+    decode.row_extra_off = np.arange(71, dtype=np.int32)
+    decode.extra_slot = np.arange(70, dtype=np.int32)
+    decode.extra_pos = np.arange(70, dtype=np.int32)
+    decode.finalize()
+    assert int(decode.chunks[3].max()) <= 32
+
+
 def _plan(R=5):
     rng = np.random.default_rng(1)
     return StepPlan(
