@@ -328,8 +328,8 @@ SIDE_KEYS = ("turn_id", "castle_id", "ep_file_id", "halfmove_bucket_id", "fullmo
 class ReferenceServerRun:
     """The reference's ``ActorInferenceServer`` (installed unmodified under
     baseline/_ref, imported through the oracle's import shims) serving the
-    roots and the wave of the given parents: the path ``north_star`` calls the
-    reference's torch path (actor_server.py:519-551 -> forward_decode_grouped,
+    roots and the wave of the given parents, through the reference's own torch
+    decode path (actor_server.py:519-551 -> forward_decode_grouped,
     hstu_model.py:651-752).  CPU: fp32 eager on all host threads; CUDA: the
     server's own bf16 autocast (position_evaluator.py:184-194)."""
 
