@@ -9,7 +9,8 @@ error reaches the caller as ``ImbaError`` with the right code, and that the
 next clean step on the same handle and pool is correct:
 
 * an extra-key slot outside the pool and a visible-prefix length above its
-  group's page capacity (IMBA_ERR_RANGE), on the bf16 tensor-core path;
+  group's page capacity (IMBA_ERR_RANGE), on the bf16 tensor-core path of a
+  decode wave and of a jagged prefill;
 * a bounded wait that runs out (IMBA_ERR_TIMEOUT): the library's wait on an
   mbarrier nothing arrives at, with a 1 ms limit instead of the production
   2 s (``imba_selftest_wait_timeout``).
@@ -90,6 +91,43 @@ def test_out_of_range_indices_raise_and_next_step_is_clean():
         v2, ll2 = _run(model, pool, plan2)
         model.check_status()
         assert torch.equal(v2, v_ok) and torch.equal(ll2, ll_ok)
+
+
+def test_prefill_out_of_range_prefix_raises_and_next_step_is_clean():
+    """The jagged prefill attention path: a visible-prefix length above its
+    document's page capacity is reported (IMBA_ERR_RANGE) and clamped; a
+    clean re-run of the same prefill on the same handle and pool is bit-exact
+    with the first."""
+    dims = synth.D256
+    sd = synth.make_state_dict(dims, 8, profile="reference")
+    model = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
+    rng = np.random.default_rng(6)
+    lens = [70, 40, 33, 5]
+    tokens = [synth.random_tokens(rng, n, dims) for n in lens]
+    pool = model.new_pool(64)
+    seqs = [KVSequence(pool) for _ in lens]
+    plan, _ = root_plan(seqs, tokens)
+
+    def run(step):
+        out = torch.empty((plan.num_rows, dims.vocab), device=model.device)
+        model.run(step, pool, logits=out)
+        torch.cuda.synchronize()
+        return out
+
+    ok = run(DeviceStep(plan, model.device))
+    model.check_status()
+    bad = DeviceStep(plan, model.device)
+    vis = plan.row_vis.copy()
+    vis[3] = 16 * pool.num_pages  # beyond its document's pages (row 3 is in the first, 70-token document)
+    o, n = bad.layout["row_vis"]
+    bad.buf[o:o + n].copy_(torch.from_numpy(vis.astype(np.int32)))
+    run(bad)
+    with pytest.raises(_native.ImbaError) as ei:
+        model.check_status()
+    assert ei.value.code == _native.IMBA_ERR_RANGE
+    again = run(DeviceStep(plan, model.device))
+    model.check_status()
+    assert torch.equal(again, ok)
 
 
 def test_bounded_wait_times_out_with_status_and_context_survives():
