@@ -31,13 +31,12 @@
 //     read S' of block b, then P' V' of block b once its P' is in shared
 //     memory; tcgen05.commit releases the ring stage and signals O'.
 //   * warps 0-3: thread i owns tile row i (TMEM lane i).  It copies its
-//     query row (rows that are not consecutive), reads its 32 scores per
-//     block from TMEM, adds the bias,
-//     masks keys past its visible prefix and keeps the online softmax (lazy
-//     rescale: O' in TMEM is rescaled only when the max grows by more than
-//     2^8), writes its P' row, and at the end stores O / l as bf16 rows (the
-//     attention output's type); the attention-output norm and u gate then
-//     run as their own pass.
+//     query row (when the unit's rows are not consecutive), reads its 32
+//     scores per block from TMEM, adds the bias, masks keys past its visible
+//     prefix and keeps the online softmax (lazy rescale: O' in TMEM is
+//     rescaled only when the max grows by more than 2^8), writes its P' row,
+//     and at the end stores O / l as bf16 rows (the attention output's
+//     type); the attention-output norm and u gate then run as their own pass.
 // Every wait is bounded; a timeout sets the status word and the CTA drains
 // its copies and MMAs before freeing TMEM.
 // Semantics: src/imba_chess/model/hstu_attention.py:64-76 (bias),
@@ -210,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         auto request_next = [&](bool block) {
           if (requested) return true;
           if (j >= 1) {
-            const uint32_t par = ((j + 1) >> 1) - 1 & 1;
+            const uint32_t par = (((j + 1) >> 1) - 1) & 1;  // unit j - 1's use of the buffer
             if (block) {
               if (!wait(&unit_empty[(j + 1) & 1], par)) return false;
             } else if (!tc::mbar_try_wait(&unit_empty[(j + 1) & 1], par)) {
