@@ -48,6 +48,8 @@ size_t workspace_layout(const imba_model* m, int32_t rows, void* base, Workspace
   w.counters = static_cast<int*>(take(kNumCounters * sizeof(int)));
   // paged attention work items: at most one chunk per row, two records per chunk
   w.recs = static_cast<int*>(take(d.dtype == IMBA_DTYPE_BF16 ? 2 * R * kAttnRecInts * sizeof(int) : 0));
+  // per row and head (max, sum) of the paged attention's pages-only pass
+  w.ml = static_cast<float2*>(take(d.dtype == IMBA_DTYPE_BF16 ? R * d.num_heads * sizeof(float2) : 0));
   w.bytes = off;
   if (ws) *ws = w;
   return off;
@@ -149,6 +151,14 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
   // the prefill attention kernel; decode waves (every row has extra keys)
   // and short root extensions run the paged decode kernel.
   const bool prefill_attn = paged_attn && st.num_extra == 0 && st.num_rows >= 4 * st.num_groups;
+  // Decode steps whose rows carry suffix chains (extra keys beyond
+  // themselves) or whose groups have few rows run the paged kernel over the
+  // pages only and fold the extra keys, norm and gate into a per-row pass
+  // (attn_combine): the per-item extra-key and norm work then leaves the
+  // kernel's critical path.  Sibling waves (many rows per group, one extra
+  // key each) keep the fused kernel.
+  const bool partial_attn = paged_attn && !prefill_attn && md.num_heads <= 8 &&
+                            (st.num_extra > st.num_rows || st.num_rows < 4 * st.num_groups);
   // bf16 handles run the tensor-core kernels; a launcher that declines
   // (returns false) is an error unless a SIMT test hook selected the SIMT
   // kernel of that component (imba_model_desc.flags).
@@ -191,6 +201,12 @@ imba_status_t run_step(const imba_model* m, const imba_step_desc& st, const imba
     if (prefill_attn && launch_attn_prefill(aa, md.num_layers, pool.num_pages, w.recs, s, &e)) {
       if (e != cudaSuccess) return IMBA_ERR_CUDA;
       gate_bf16 = true;
+    } else if (partial_attn && launch_attn_page(aa, md.num_layers, md, pool.num_pages,
+                                                         static_cast<const bf16*>(w.u), nullptr, w.recs, s, &e,
+                                                         &fused, w.ml)) {
+      if (e != cudaSuccess) return IMBA_ERR_CUDA;
+      IMBA_CK(launch_attn_combine(aa, w.ml, static_cast<const bf16*>(w.u), gated_bf, s));
+      fused = true;
     } else if (!paged_attn || !launch_attn_page(aa, md.num_layers, md, pool.num_pages, static_cast<const bf16*>(w.u),
                                                 gated_bf, w.recs, s, &e, &fused)) {
       if (md.dtype == IMBA_DTYPE_BF16 && !m->simt_attn) return IMBA_ERR_UNSUPPORTED;

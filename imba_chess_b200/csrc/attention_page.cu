@@ -79,6 +79,8 @@ struct PageParams {
   const bf16* u;     // [R, H dv]
   bf16* gated;       // [R, H dv]: fused norm + gate output (nullptr: store fp32 O to a.out)
   const int* recs;   // [2 C][kAttnRecInts]: record c = chunk c's first 32 rows, C + c its second
+  float2* ml;        // [R, H] or null: the pages only; O / l, and (max, sum) per row and head,
+                     // for attn_combine (extra keys, norm, gate)
 };
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
@@ -757,7 +759,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       return;  // the status word already holds the timeout
     }
     // Extra keys, per row: the suffix chain and the row itself.
-    {
+    if (!prm.ml) {
       const int c0 = rl0 < n ? item[kRecXcnt + rl0] : 0, c1 = rl1 < n ? item[kRecXcnt + rl1] : 0;
       const int o0 = item[kRecXoff + rl0], o1 = item[kRecXoff + rl1];
       int emax = max(c0, c1);
@@ -825,6 +827,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         const int col = h * D + 8 * q + 2 * t;
         if (r0 >= 0) *reinterpret_cast<float2*>(a.out + (size_t)r0 * hdv + col) = make_float2(rs.o[q][0], rs.o[q][1]);
         if (r1 >= 0) *reinterpret_cast<float2*>(a.out + (size_t)r1 * hdv + col) = make_float2(rs.o[q][2], rs.o[q][3]);
+      }
+      if (prm.ml && t == 0) {
+        if (r0 >= 0) prm.ml[(size_t)r0 * H + h] = make_float2(rs.m0, rs.l0);
+        if (r1 >= 0) prm.ml[(size_t)r1 * H + h] = make_float2(rs.m1, rs.l1);
       }
     } else {
       // O (bf16) over this warp's own query rows of the tile, then, after one
@@ -922,7 +928,8 @@ cudaError_t launch_attn_items(const imba_step_desc& st, const PoolGeom& g, int* 
 // caller then skips its gate pass).  a.counters[0 .. H / hc) must be zero and
 // recs must hold this step's item records (launch_attn_items).
 bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& md, int64_t num_pages,
-                      const bf16* u, bf16* gated, const int* recs, cudaStream_t s, cudaError_t* err, bool* fused) {
+                      const bf16* u, bf16* gated, const int* recs, cudaStream_t s, cudaError_t* err, bool* fused,
+                      float2* ml) {
   *fused = false;
   if (md.dtype != IMBA_DTYPE_BF16 || md.attention_dim != 64 || md.linear_dim != 64) return false;
   const int H = md.num_heads;
@@ -971,12 +978,153 @@ bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& 
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  PageParams prm{a, num_layers, hc, (int)stages, u, fuse ? gated : nullptr, recs};
+  PageParams prm{a, num_layers, hc, (int)stages, u, fuse ? gated : nullptr, recs, fuse ? nullptr : ml};
   const int ctas = a.st.num_chunks < sms ? a.st.num_chunks : sms;
   dim3 grid(ctas, 1, H / hc);
   *err = launch_pdl(kern, grid, dim3((2 * hc + 1) * 32), smem, s, map, prm);
   *fused = fuse && *err == cudaSuccess;
   return true;
+}
+
+namespace {
+
+// The rest of a row's attention after the page kernel's partial pass: its
+// extra keys (suffix chain and itself) folded into each head's softmax
+// state, O rounded to bf16, the LayerNorm over the row's H dv outputs (no
+// affine, eps 1e-6) and the u gate.  One warp per row, H <= 8: lane l takes
+// head l / 4 and dims 16 (l % 4) .. +15.
+__global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a, const float2* __restrict__ ml,
+                                                           const bf16* __restrict__ u, bf16* __restrict__ gated) {
+  pdl_wait();
+  pdl_trigger();
+  const imba_step_desc& st = a.st;
+  const int r = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+  if (r >= st.num_rows) return;
+  const int H = a.g.H, hdv = H * 64;
+  const int hh = lane >> 2, part = lane & 3;
+  const bool on = hh < H;
+  const int col = hh * 64 + 16 * part;
+  float o[16];
+  float m = -INFINITY, l = 0.f;
+  if (on) {
+    const float4* op = reinterpret_cast<const float4*>(a.out + (size_t)r * hdv + col);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 v = op[i];
+      o[4 * i] = v.x;
+      o[4 * i + 1] = v.y;
+      o[4 * i + 2] = v.z;
+      o[4 * i + 3] = v.w;
+    }
+    const float2 s = ml[(size_t)r * H + hh];
+    m = s.x;
+    l = s.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o[i] = 0.f;
+  }
+  // O back to the unnormalised sum relative to m.
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i] *= l;
+  int e0 = st.row_extra_off[r], e1 = st.row_extra_off[r + 1];
+  if (e0 < 0 || e1 < e0 || e1 > st.num_extra) {
+    report(st.status, IMBA_ERR_RANGE);
+    e0 = e1 = 0;
+  }
+  if (e1 > e0) {
+    const int qpos = st.positions[r];
+    const float scale2 = a.scale * kLog2e;
+    uint4 qv[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+    if (on) {
+      const uint4* qp = reinterpret_cast<const uint4*>(static_cast<const bf16*>(a.q) + (size_t)r * hdv + col);
+      qv[0] = __ldg(qp);
+      qv[1] = __ldg(qp + 1);
+    }
+    const bf16* pool = static_cast<const bf16*>(a.pool);
+    for (int e = e0; e < e1; ++e) {
+      int slot = st.extra_slot[e];
+      const int kpos = st.extra_pos[e];
+      if (slot < 0 || slot >= a.g.num_slots) {
+        report(st.status, IMBA_ERR_RANGE);
+        continue;  // uniform across the warp
+      }
+      float dot = 0.f;
+      float vv[16];
+      if (on) {
+        const uint4* kp = reinterpret_cast<const uint4*>(pool + a.g.k_off(slot, a.layer, hh) + 16 * part);
+        const uint4* vp = reinterpret_cast<const uint4*>(pool + a.g.v_off(slot, a.layer, hh) + 16 * part);
+        const uint4 k2[2] = {__ldg(kp), __ldg(kp + 1)}, v2[2] = {__ldg(vp), __ldg(vp + 1)};
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const uint32_t qw[4] = {qv[c].x, qv[c].y, qv[c].z, qv[c].w}, kw[4] = {k2[c].x, k2[c].y, k2[c].z, k2[c].w};
+          const uint32_t vw[4] = {v2[c].x, v2[c].y, v2[c].z, v2[c].w};
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const float2 qf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qw[w]));
+            const float2 kf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kw[w]));
+            const float2 vf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vw[w]));
+            dot = fmaf(qf.x, kf.x, dot);
+            dot = fmaf(qf.y, kf.y, dot);
+            vv[8 * c + 2 * w] = vf.x;
+            vv[8 * c + 2 * w + 1] = vf.y;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) vv[i] = 0.f;
+      }
+      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+      if (on) {
+        const float sx = fmaf(dot, scale2, __ldg(a.ps_w + (size_t)hh * (2 * a.max_pos - 1) +
+                                                  bias_index(kpos, qpos, a.max_pos)) * kLog2e);
+        const float mn = fmaxf(m, sx);
+        const float c = exp2_approx(m - mn), p = exp2_approx(sx - mn);
+        l = fmaf(l, c, p);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = fmaf(o[i], c, p * vv[i]);
+        m = mn;
+      }
+    }
+  }
+  const float inv = l > 0.f ? 1.0f / l : 0.f;
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    o[i] = __bfloat162float(__float2bfloat16_rn(o[i] * inv));  // the attention output's type
+    sum += o[i];
+  }
+  const float mu = warp_sum(sum) / (float)hdv;
+  float q2 = 0.f;
+  if (on) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) q2 += (o[i] - mu) * (o[i] - mu);
+  }
+  const float rstd = rsqrtf(warp_sum(q2) / (float)hdv + 1e-6f);
+  if (on) {
+    const uint4* up = reinterpret_cast<const uint4*>(u + (size_t)r * hdv + col);
+    uint4* gp = reinterpret_cast<uint4*>(gated + (size_t)r * hdv + col);
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const uint4 uv = __ldg(up + c);
+      const uint32_t uw[4] = {uv.x, uv.y, uv.z, uv.w};
+      uint32_t g[4];
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float2 uf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&uw[w]));
+        g[w] = pack_bf16(uf.x * ((o[8 * c + 2 * w] - mu) * rstd), uf.y * ((o[8 * c + 2 * w + 1] - mu) * rstd));
+      }
+      gp[c] = make_uint4(g[0], g[1], g[2], g[3]);
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_attn_combine(const AttnArgs& a, const float2* ml, const bf16* u, bf16* gated, cudaStream_t s) {
+  if (a.g.H > 8 || a.st.num_rows <= 0) return a.st.num_rows <= 0 ? cudaSuccess : cudaErrorInvalidValue;
+  const int blocks = (a.st.num_rows + 7) / 8;
+  return launch_pdl(attn_combine_kernel, dim3(blocks), dim3(256), 0, s, a, ml, u, gated);
 }
 
 }  // namespace imba

@@ -149,6 +149,7 @@ struct Workspace {
   void* pooled;    // [R, 192]    bf16 models: mean-pooled board-encoder output, split bf16
   int* counters;   // [kNumCounters] work-queue counters, zeroed at the start of every step
   int* recs;       // [2 R][kAttnRecInts] bf16 models: resolved attention work items
+  float2* ml;      // [R, H]      bf16 models: (max, sum) of each row's pages-only attention pass
   size_t bytes;
 };
 

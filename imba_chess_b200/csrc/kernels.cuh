@@ -55,7 +55,11 @@ cudaError_t launch_attn_simt(const AttnArgs& a, cudaStream_t s);
 // launch_attn_items ([2 num_chunks][kAttnRecInts]).
 cudaError_t launch_attn_items(const imba_step_desc& st, const PoolGeom& g, int* recs, cudaStream_t s);
 bool launch_attn_page(const AttnArgs& a, int num_layers, const imba_model_desc& md, int64_t num_pages,
-                      const bf16* u, bf16* gated, const int* recs, cudaStream_t s, cudaError_t* err, bool* fused);
+                      const bf16* u, bf16* gated, const int* recs, cudaStream_t s, cudaError_t* err, bool* fused,
+                      float2* ml = nullptr);
+// After launch_attn_page with `ml` (the pages only): the rows' extra keys,
+// the attention-output norm and the u gate (H <= 8).
+cudaError_t launch_attn_combine(const AttnArgs& a, const float2* ml, const bf16* u, bf16* gated, cudaStream_t s);
 // Jagged prefill attention (tcgen05; bf16, head dims 64, an even head
 // count): for steps without extra keys.  Writes O rounded to bf16 over a.out
 // ([R, H dv] bf16 in its first half; the norm / gate is a separate pass,
