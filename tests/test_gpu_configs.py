@@ -22,6 +22,9 @@ benchmark runs, on real positions from seeded uniformly-random legal play:
   single-token decode + KV-append steps per game (incremental roots); the
   same bf16 bars over the 1,200 evaluated positions; the persisted prefix
   lengths are checked exactly.
+* config 4, seeded subset: bf16, d512 / 8 / 8 with max_pos 1024, 36 games of
+  U[40, 250] plies, sequential-halving rounds of 16 / 8 / 4 / 2 arms whose
+  rows carry their arms' suffix chains (1,080 rows).
 * config 5, seeded subset: bf16, d1024 / 16 layers / 16 heads, 26 parents of
   U[300, 600] plies with K = 40 sibling rows each (1,040 rows).
 
@@ -296,6 +299,74 @@ def test_config5_subset_bf16_through_server():
     assert wave.num_rows == 1040
     stats = _bf16_server_wave(synth.D1024, wave, seed=2)
     _report("config5_subset", parents=26, **stats)
+    _assert_bf16(stats)
+
+
+# ----------------------------------------------------------------------
+# config 4 subset: sequential-halving rounds with suffix chains
+# ----------------------------------------------------------------------
+def test_config4_halving_subset_bf16_through_server():
+    """36 games of U[40, 250] plies, rounds of 16 / 8 / 4 / 2 surviving arms
+    (1,080 rows): round r evaluates one node per arm at depth r whose suffix is
+    the arm's chain in the turn arena (rounds 1-3 run the pages-only attention
+    and the per-row combine pass), against the fp32 oracle fed its own KV of
+    the chain nodes as suffix keys."""
+    dims = synth.D512_LONG
+    sd = synth.make_state_dict(dims, 2, profile="reference")
+    model = B200HSTUChessModel(sd, dtype=torch.bfloat16, device="cuda:0")
+    orc = OracleModel(sd, dims)
+    rng = np.random.default_rng(1234)
+    G, rounds = 36, (16, 8, 4, 2)
+    prefixes = [synth.game_tokens(rng, int(rng.integers(40, 251)), dims) for _ in range(G)]
+    lens = [int(p["piece_ids"].shape[0]) for p in prefixes]
+    server = ActorInferenceServer(model=model, device="cuda:0", dtype=torch.bfloat16,
+                                  kv_pool_pages=_pool_pages(lens, G * sum(rounds), extra=256))
+    server.service(_roots(prefixes))
+    grouped = _stack([orc.forward(pt, [0, lens[g]])["kv_caches"] for g, pt in enumerate(prefixes)], orc.L)
+    node_kv = {}  # node id -> per-layer (k [H, d], v [H, d]) from the oracle
+    got_all, ref_logits, ref_values, legal_all = [], [], [], []
+    for r, K in enumerate(rounds):
+        tok = synth.random_tokens(rng, G * K, dims)
+        legal = [synth.random_legal_ids(rng, int(rng.integers(20, 41)), dims.vocab) for _ in range(G * K)]
+        reqs, nodes, parents = [], [], []
+        for g in range(G):
+            rows = []
+            for a in range(K):
+                i = g * K + a
+                nid = 10000 * g + 100 * r + a
+                pid = None if r == 0 else 10000 * g + 100 * (r - 1) + a
+                bs = {"piece_ids": tok["piece_ids"][i].tolist(), **{k: int(tok[k][i]) for k in SIDE}}
+                rows.append(WaveRow(node_id=nid, parent_id=pid, prev_move_vocab_id=int(tok["prev_move_id"][i]),
+                                    board_state=bs, legal_vocab_ids=legal[i].tolist()))
+                nodes.append(nid)
+                parents.append(pid)
+            reqs.append(WaveRequest(worker_id=g, turn_id=0, rows=rows))
+        resp = server.service(reqs)
+        got_all += [row for wr in resp for row in wr.rows]
+        gi = np.repeat(np.arange(G), K)
+        kw = {}
+        if r > 0:
+            chains = []
+            for pid in parents:  # the arm's nodes of rounds 0 .. r - 1
+                ch, p = [], pid
+                while p is not None:
+                    ch.append(p)
+                    p = p - 100 if (p % 10000) >= 100 else None
+                chains.append(ch[::-1])
+            sk = [np.stack([np.stack([node_kv[n][l][0] for n in ch], axis=1) for ch in chains]) for l in range(orc.L)]
+            sv = [np.stack([np.stack([node_kv[n][l][1] for n in ch], axis=1) for ch in chains]) for l in range(orc.L)]
+            kw = dict(suffix_kv=list(zip(sk, sv)), suffix_positions=np.asarray(lens)[gi][:, None] + np.arange(r)[None, :],
+                      suffix_mask=np.ones((G * K, r), dtype=bool))
+        ref = orc.forward_decode_grouped(new_token_batch=tok, positions=np.asarray(lens)[gi] + r, group_index=gi,
+                                         prefix_kv_grouped=grouped, prefix_lens_list=lens, **kw)
+        for i, nid in enumerate(nodes):
+            node_kv[nid] = [(ref["kv"][l][0][i, :, 0], ref["kv"][l][1][i, :, 0]) for l in range(orc.L)]
+        ref_logits.append(ref["logits"])
+        ref_values.append(ref["value_logits"])
+        legal_all += legal
+    stats = _compare_rows(got_all, np.concatenate(ref_logits), np.concatenate(ref_values), legal_all)
+    assert stats["rows"] == G * sum(rounds) >= TOP1_MIN_ROWS
+    _report("config4_halving_subset", games=G, rounds=list(rounds), **stats)
     _assert_bf16(stats)
 
 
